@@ -1,0 +1,346 @@
+#!/usr/bin/env python3
+"""MoE-layer tokens/s on B200 for the GPT-OSS-120B-shaped stack.
+
+One step = one pass of T tokens through the 36-layer MoE stack
+(h <- h + MoE(RMSNorm(h)), 128 MXFP4 experts per layer, top-4, hidden 2880,
+expert FFN 2880; attention omitted, as the config says).  Weights are
+generated on the device from seed 0 (~61 GB); inputs are seeded bf16 N(0,1)
+tokens drawn from a pool of 16 batches so that routing changes every step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--mode decode|prefill]
+                  [--tokens T] [--layers L] [--impl umsx|reference]
+
+With N > 1 (torchrun, one rank per GPU) every rank holds the whole stack and
+runs its own tokens (data-parallel replicas, weak scaling); the value is all
+ranks' tokens over the slowest rank's time.  `--impl reference` times the
+reference's own CPU implementation of the path (tools/trace/exact_packed_cpu.h
+packed MXFP4 GEMV compiled from the reference sources into oracle/_ref/) on
+this host's cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HBM_FALLBACK_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--mode", choices=("decode", "prefill"), default="decode")
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--impl", choices=("umsx", "reference"), default="umsx")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the bounded CPU sample")
+    a = ap.parse_args()
+    if a.tokens is None:
+        a.tokens = 1 if a.mode == "decode" else 4096
+    a.warmup = max(a.warmup, 3)
+    return a
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def metric_name(a):
+    return (f"MoE-layer tokens/s, GPT-OSS-120B-shaped {a.layers}-layer MXFP4 stack, "
+            f"{a.mode} T={a.tokens}")
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class Clocks:
+    """nvidia-smi samples during the timed region (read-only)."""
+
+    def __init__(self, index: int):
+        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+        self.proc = None
+        self.index = index
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
+            os.unlink(self.path)
+        except Exception:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+def cpu_baseline(a, budget_s: float) -> dict:
+    """The reference's exact packed MXFP4 path (oracle/_ref) on this host's cores, bounded sample."""
+    import numpy as np
+    from oracle.oracle import Oracle, OrcDesc, RefKernels
+    from tests.helpers import host_weights, oracle_desc
+    pkg = load_pkg()
+    cfg = pkg.configs.GPT_OSS_120B
+    orc = Oracle()
+    cores = len(os.sched_getaffinity(0))
+    kind = "port"
+    ref = None
+    try:
+        ref = RefKernels()
+        if ref.supported():
+            kind = "reference"
+        else:
+            ref = None
+    except Exception:
+        ref = None
+    t0 = time.time()
+    w = host_weights(orc, cfg, layer=0)
+    gen_s = time.time() - t0
+    T = a.tokens if a.mode == "decode" else min(a.tokens, 64)
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((T, cfg.hidden)).astype(np.float32)
+    desc = oracle_desc(cfg)
+    if kind == "reference":
+        h = ref.layer(desc, w)
+        run = lambda: ref.layer_forward(h, x, cfg.hidden, cores)  # noqa: E731
+    else:
+        run = lambda: orc.moe_layer(desc, w, x, threads=cores)  # noqa: E731
+    run()
+    times = []
+    t_start = time.time()
+    while time.time() - t_start < budget_s and len(times) < 2000:
+        s = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - s)
+    if kind == "reference":
+        ref.layer_destroy(h)
+    layer_s = statistics.median(times)
+    tok_s = T / (layer_s * a.layers)
+    return {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": (f"{T} token(s) through one seeded GPT-OSS-120B-shaped layer (128 MXFP4 experts, "
+                       f"host-generated in {gen_s:.1f}s), median of {len(times)} passes "
+                       f"({layer_s * 1e3:.3f} ms/layer) scaled to {a.layers} layers"
+                       + ("" if a.mode == "decode" else f"; prefill sampled at T={T} tokens/s")),
+            "layer_ms": layer_s * 1e3}
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def load_pkg():
+    import __graft_entry__
+    return __graft_entry__.load_package()
+
+
+def algorithmic_bytes(cfg, tokens: int):
+    """Per-launch algorithmic bytes of gate_up and down, averaged over layers.
+
+    Distinct experts touched by T tokens with top-k of E: E*(1-(1-k/E)^T) (exactly k at T=1)."""
+    E, k, H, I = cfg.experts, cfg.top_k, cfg.hidden, cfg.intermediate
+    distinct = k if tokens == 1 else E * (1 - (1 - k / E) ** tokens)
+    jobs = tokens * k
+    gu = distinct * (2 * I * H // 32 * 17 + 2 * I * 2) + tokens * H * (1 + 4 / 32) + jobs * I * (1 + 4 / 32)
+    dn = distinct * (H * I // 32 * 17 + H * 2) + jobs * I * (1 + 4 / 32) + jobs * H * 4
+    return gu, dn, distinct
+
+
+def gpu_arm(a):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    pkg = load_pkg()
+    cfg = pkg.configs.GPT_OSS_120B
+    T = a.tokens
+    layers = [pkg.MoeLayer(cfg.desc(max_tokens=1), synthetic=cfg.synthetic(layer=l), device=dev.index,
+                           reserve_bytes=2 << 30) for l in range(a.layers)]
+    stack = pkg.MoeStack(layers, max_tokens=T)
+    pool = 16
+    rng = np.random.default_rng(1000 + rank)
+    xs = torch.from_numpy(rng.standard_normal((pool, T, cfg.hidden)).astype(np.float32)).to(torch.bfloat16)
+    xs_dev = xs.to(dev)
+    out = torch.empty((T, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # device-resident timed region
+    stack.set_timing(True)
+    for i in range(a.warmup):
+        stack.forward(xs_dev[i % pool], out)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = pkg.kernel_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index) as clk:
+        ev0.record(stream)
+        for i in range(a.steps):
+            stack.forward(xs_dev[i % pool], out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = pkg.kernel_launches() - launches0
+    stages = stack.stage_times()  # the last replay, every layer, on the stack's launching stream
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_step = ms / a.steps
+    value = world * T * a.steps / (ms / 1e3)
+    clocks = clk.summary()
+
+    # end-to-end through the C ABI with host buffers (pinned), copies inside the timed region
+    e2e = None
+    if not a.no_e2e:
+        xh = xs.pin_memory()
+        oh = torch.empty((T, cfg.hidden), dtype=torch.float32).pin_memory()
+        for i in range(a.warmup):
+            stack.forward_host(xh[i % pool], oh)
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(a.steps):
+            stack.forward_host(xh[i % pool], oh)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": world * T * a.steps / (ems / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(T * cfg.hidden * 2), "d2h_bytes_per_step": int(T * cfg.hidden * 4),
+               "ms_per_step": ems / a.steps, "api": "umsx_stack_forward_host"}
+
+    peak, peak_kind = peaks()
+    gu_bytes, dn_bytes, distinct = algorithmic_bytes(cfg, T)
+    gu_ms = stages["gate_up"] / a.layers
+    roof = {"kernel": "k_gate_up (MXFP4 x Q8_0 exact GEMV, fused SwiGLU-OAI + Q8_0)", "bound": "hbm",
+            "achieved": gu_bytes / (gu_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+            "frac": gu_bytes / (gu_ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+            "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms, "traffic": traffic_for(a, "k_gate_up")}
+    stack_bytes = a.layers * (gu_bytes + dn_bytes + cfg.router_bytes())
+    res = {"metric": metric_name(a), "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
+           "config": {"workload": f"gpt-oss-120b-stack {a.mode}", "layers": a.layers, "experts": cfg.experts,
+                      "top_k": cfg.top_k, "hidden": cfg.hidden, "ffn": cfg.intermediate, "quant": "mxfp4",
+                      "tokens_per_step_per_gpu": T, "global_batch": T * world,
+                      "parallelism": "replicas" if world > 1 else "single",
+                      "l2": f"inputs larger than L2: {stack_bytes / 1e9:.2f} GB of weights read per step",
+                      "expected_distinct_experts_per_layer": distinct},
+           "roofline": roof,
+           "stack_roofline": {"bytes_per_step": stack_bytes, "achieved_gbs": stack_bytes / (ms_step / 1e3) / 1e9,
+                              "frac": stack_bytes / (ms_step / 1e3) / 1e9 / peak},
+           "stages_ms_last_step": stages, "gpu_launches": launches, "clocks": clocks, "e2e": e2e}
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        try:
+            res["cpu_baseline"] = {k: v for k, v in cpu_baseline(a, a.cpu_seconds).items() if k != "layer_ms"}
+        except Exception as exc:  # the GPU line must still be printed
+            res["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
+    stack.close()
+    for l in layers:
+        l.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res))
+
+
+def traffic_for(a, kernel: str):
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary, when one exists."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            t = json.load(f)
+        return t[f"{a.mode}_T{a.tokens}"][kernel]
+    except Exception:
+        return None
+
+
+def reference_arm(a):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    base = cpu_baseline(a, a.cpu_seconds)
+    per_step_ms = a.tokens / base["value"] * 1e3
+    res = {"metric": metric_name(a), "value": base["value"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": per_step_ms, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
+           "impl": "reference",
+           "config": {"workload": f"gpt-oss-120b-stack {a.mode}", "layers": a.layers, "experts": 128, "top_k": 4,
+                      "hidden": 2880, "ffn": 2880, "quant": "mxfp4", "tokens_per_step_per_gpu": a.tokens},
+           "cpu_baseline": {k: base[k] for k in ("kind", "cores", "sample", "value", "unit")},
+           "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(res))
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        reference_arm(a)
+    else:
+        gpu_arm(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+/*
+ * umsx -- B200-native (sm_100a) MoE-layer hot path behind a C ABI.
+ *
+ * The ABI carries plain pointers and sizes only.  Device pointers are
+ * caller-owned; calls are stream-ordered and asynchronous unless the name
+ * says `_host`.  No exception crosses it: every call returns a umsx_status and
+ * umsx_last_error() holds the message of the last failure on this thread.
+ * One handle per host thread, or the caller serialises (the reference guards
+ * its CUDA runner with a mutex, tools/engine/quantized_cuda.cu:415).
+ *
+ * Reference interfaces replaced (paths inside appatalks/unified-memory-scheduler):
+ *   ExpertPlan + ExpertRunner           tools/engine/expert_dispatch.hpp:21-48, .cpp:22-89
+ *   Mxfp4NativeCudaDown                 tools/engine/quantized_cuda.hpp:38-50, .cu:367-453
+ *   ggml MUL_MAT_ID -> ADD_ID -> SWIGLU_OAI -> MUL -> rank sum
+ *                                       third_party/patches/llama-b11669-hybrid-experts.patch:1394-1683, :1911-1916
+ *   router build_lora_mm(gate_inp, cur) hybrid patch :1361-1384 (softmax/top-k upstream)
+ *   Q8_0 activation quantizer (x86 rule) llama-b11669-mxfp4-q8-parity-experimental.patch:41-44, :96
+ */
+#ifndef UMSX_H
+#define UMSX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UMSX_VERSION 1
+
+typedef enum umsx_status {
+    UMSX_OK = 0,
+    UMSX_EINVAL = 1,        /* invalid argument / shape (std::invalid_argument in the reference) */
+    UMSX_ENOTRESIDENT = 2,  /* expert out of range or not resident on this handle */
+    UMSX_EOOM = 3,          /* allocation would violate the configured free-memory reserve */
+    UMSX_ETIMEOUT = 4,      /* a bounded device wait (expert-parallel exchange) gave up */
+    UMSX_EDEVICE = 5,       /* CUDA runtime error */
+    UMSX_EUNSUPPORTED = 6,  /* shape or mode this build does not implement */
+    UMSX_ENONFINITE = 7     /* non-finite result (the reference rejects these, expert_dispatch.cpp:14-18) */
+} umsx_status;
+
+/* A cudaStream_t, passed as void* so this header needs no CUDA include.  NULL = legacy default stream. */
+typedef void *umsx_stream;
+
+enum { UMSX_QUANT_Q8_0 = 8, UMSX_QUANT_MXFP4 = 39 }; /* ggml type ids */
+
+enum {
+    UMSX_ROUTE_TOPK_SOFTMAX = 0,      /* gpt-oss: top-k of logits, softmax over the k selected */
+    UMSX_ROUTE_SOFTMAX_TOPK_NORM = 1, /* qwen3: softmax over all experts, top-k, renormalise */
+    UMSX_ROUTE_SOFTMAX_TOPK = 2       /* deepseek: softmax over all experts, top-k, times routed_scale */
+};
+
+enum { UMSX_ACT_SILU = 0, UMSX_ACT_SWIGLU_OAI = 1 }; /* F32Activation, tools/engine/f32_experts.hpp:11 */
+
+enum { UMSX_DTYPE_F32 = 0, UMSX_DTYPE_BF16 = 1 };
+
+enum { UMSX_PROJ_GATE_UP = 0, UMSX_PROJ_GATE = 1, UMSX_PROJ_UP = 2, UMSX_PROJ_DOWN = 3 };
+
+typedef struct umsx_moe_desc {
+    int32_t hidden;          /* H: model width (K of gate/up, N of down); multiple of 64 */
+    int32_t intermediate;    /* I: expert FFN width; multiple of 64 */
+    int32_t experts;         /* E: routed experts in the whole layer */
+    int32_t top_k;           /* k <= 32 */
+    int32_t quant;           /* UMSX_QUANT_MXFP4 or UMSX_QUANT_Q8_0 */
+    int32_t routing;         /* UMSX_ROUTE_* */
+    int32_t activation;      /* UMSX_ACT_* */
+    int32_t fused_gate_up;   /* 1: one [E][2I][H] matrix, gate rows [0,I) then up rows [I,2I) */
+    int32_t has_bias;        /* expert biases present (bf16) */
+    int32_t has_router_bias; /* router bias present (fp32) */
+    float swiglu_alpha;      /* 1.702 for GPT-OSS */
+    float swiglu_limit;      /* 7.0 for GPT-OSS */
+    float routed_scale;      /* weight multiplier for UMSX_ROUTE_SOFTMAX_TOPK (1.0 for DeepSeek-V2-Lite) */
+    int32_t max_tokens;      /* largest T a forward call passes; sizes the handle's workspace */
+    int32_t ep_rank;         /* expert-parallel rank: experts [ep_rank*E/ep_world, ...) are resident */
+    int32_t ep_world;        /* 1 for a single GPU */
+} umsx_moe_desc;
+
+/* HOST pointers in ggml layouts (what a GGUF holds); create() copies the
+ * resident experts to the device and repacks them.  NULL for absent tensors. */
+typedef struct umsx_moe_weights {
+    const float *router_w;         /* [E][H] fp32 */
+    const float *router_b;         /* [E] fp32 */
+    const void *gate_up;           /* fused: [E][2I][H/32] blocks */
+    const void *gate;              /* separate: [E][I][H/32] blocks */
+    const void *up;                /* separate: [E][I][H/32] blocks */
+    const void *down;              /* [E][H][I/32] blocks */
+    const uint16_t *gate_up_bias;  /* bf16 [E][2I]: gate bias then up bias */
+    const uint16_t *down_bias;     /* bf16 [E][H] */
+} umsx_moe_weights;
+
+typedef struct umsx_moe umsx_moe;
+
+/* Replaces Mxfp4NativeCudaDown(const LoadedExperts&, resident, device) (quantized_cuda.cu:377-407)
+ * and the graph's expert tensors: uploads, repacks into the sm_100a tile layout, keeps
+ * `reserve_bytes` of device memory free (the reference keeps 1 GiB, quantized_cuda.cu:18,25-30). */
+umsx_status umsx_moe_create(const umsx_moe_desc *desc, const umsx_moe_weights *weights, int device,
+                            size_t reserve_bytes, umsx_moe **out);
+
+/* Same, with every tensor generated on the device from (seed, layer) by the
+ * counter-based generator (router and bias normal sigmas as given). */
+umsx_status umsx_moe_create_synthetic(const umsx_moe_desc *desc, uint64_t seed, uint32_t layer,
+                                      float router_sigma, float router_bias_sigma, float bias_sigma,
+                                      int device, size_t reserve_bytes, umsx_moe **out);
+
+void umsx_moe_destroy(umsx_moe *moe);
+
+/* Whole layer, device buffers: out[T][H] = sum_r w[t,r] * expert(ids[t,r], x[t]) in rank order.
+ * Replaces build_moe_ffn's expert branch + rank sum (hybrid patch :1394-1683, :1911-1916).
+ * x is [T][H] fp32 or bf16 (x_dtype).  Optional ids/weights outputs may be NULL. */
+umsx_status umsx_moe_forward(umsx_moe *moe, const void *x, int x_dtype, int tokens, float *out,
+                             int32_t *ids, float *weights, umsx_stream stream);
+
+/* Same with HOST buffers: copies in, runs, copies out, synchronises (the reference's
+ * synchronous host-vector contract, quantized_cuda.cu:413-453). */
+umsx_status umsx_moe_forward_host(umsx_moe *moe, const void *x, int x_dtype, int tokens, float *out,
+                                  umsx_stream stream);
+
+/* Router only: logits (fixed fp32 reduction order), softmax/top-k/renormalise per
+ * desc.routing, ties to the lowest expert index (topk-tie-probe.cpp:111-113),
+ * per-expert counts.  ids [T][k] int32, weights [T][k] fp32, counts [E] int32 (may be NULL). */
+umsx_status umsx_route(umsx_moe *moe, const void *x, int x_dtype, int tokens, int32_t *ids, float *weights,
+                       int32_t *counts, umsx_stream stream);
+
+/* Mxfp4NativeCudaDown::execute(packed_q8, jobs) (quantized_cuda.cu:413-453), device buffers:
+ * packed_q8 is [jobs][I/32] ggml block_q8_0 rows, experts[j] the job's expert id, out [jobs][H] fp32
+ * including the down bias.  Bit-exact with the reference CPU vec_dot.  Non-resident or
+ * out-of-range experts give UMSX_ENOTRESIDENT (checked on the host copy of `experts`,
+ * so `experts` is a HOST pointer here, as the reference's job vector is). */
+umsx_status umsx_expert_down_q8(umsx_moe *moe, const void *packed_q8, const int32_t *experts, int jobs,
+                                float *out, umsx_stream stream);
+
+/* ggml MUL_MAT_ID shape (hybrid patch :1394-1683): as = the handle's projection `proj`
+ * ([K][N][E] in ggml order), b = [T][n_b][K] fp32 rows (n_b = 1 broadcasts one row per token,
+ * else n_b = n_ids), ids = [T][n_ids] int32 (-1 = masked: that output row is zero,
+ * hybrid patch :617-621), dst = [T][n_ids][N] fp32.  The activation is quantized to Q8_0 with
+ * the x86 rule and the dot is the reference's exact one; no bias is added (ADD_ID is separate). */
+umsx_status umsx_mul_mat_id(umsx_moe *moe, int proj, const float *b, int n_b, const int32_t *ids, int n_ids,
+                            int tokens, float *dst, umsx_stream stream);
+
+/* Weighted combine in rank order from 0.0f without contraction
+ * (ExpertPlan::execute, expert_dispatch.cpp:77-87): out[t][i] = sum_r w[t][r] * y[t][r][i]. */
+umsx_status umsx_combine(const float *y, const float *weights, int tokens, int top_k, int width, float *out,
+                         umsx_stream stream);
+
+/* Copies expert `expert` of projection `proj` back out of the device tile layout into
+ * ggml blocks (host buffer of `size` bytes); the round trip must reproduce the original
+ * bytes (the reference's repack export hook, tests/test_masked_matmul.cpp). */
+umsx_status umsx_moe_export_expert(umsx_moe *moe, int proj, int expert, void *host_out, size_t size);
+
+/* A stack of MoE layers with the residual stream of a transformer block, attention
+ * omitted: h <- h + MoE_l(RMSNorm(h)) for every layer l in order (RMSNorm with unit
+ * weight, eps rms_eps; the norm is fused into each layer's router and the residual add
+ * into its combine).  The layers must share device and shape; the stack owns one
+ * workspace for up to max_tokens tokens and replays the whole stack as one CUDA graph
+ * per token count, on a stream of its own ordered after / before the caller's stream.
+ * Replaces the per-layer ffn_norm -> build_moe_ffn -> residual sequence of the
+ * llama.cpp graph the hybrid patch modifies (llama-b11669-hybrid-experts.patch:1355-1930). */
+typedef struct umsx_stack umsx_stack;
+umsx_status umsx_stack_create(umsx_moe *const *layers, int n_layers, int max_tokens, float rms_eps, umsx_stack **out);
+void umsx_stack_destroy(umsx_stack *stack);
+/* x [T][H] (device, fp32 or bf16) -> out [T][H] fp32 final hidden state. */
+umsx_status umsx_stack_forward(umsx_stack *stack, const void *x, int x_dtype, int tokens, float *out, umsx_stream stream);
+/* Same with host buffers (pinned for overlap); copies in and out and synchronises. */
+umsx_status umsx_stack_forward_host(umsx_stack *stack, const void *x, int x_dtype, int tokens, float *out,
+                                    umsx_stream stream);
+/* With timing on, each replay timestamps the router, gate_up, down and combine stage of every
+ * layer; stage_times returns the four per-stage sums (ms) over the layers of the last replay. */
+umsx_status umsx_stack_set_timing(umsx_stack *stack, int enable);
+umsx_status umsx_stack_stage_times(umsx_stack *stack, float *ms, int n_stages);
+
+/* Number of this library's kernels launched by the calling thread since load (graph replays count
+ * every kernel they contain). */
+uint64_t umsx_kernel_launches(void);
+
+const char *umsx_last_error(void);
+int umsx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* UMSX_H */

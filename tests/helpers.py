@@ -1,0 +1,67 @@
+"""Test helpers: host twins of the synthetic weights, oracle descriptors, small configs."""
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+
+from __graft_entry__ import load_package
+from oracle.oracle import LayerWeights, OrcDesc
+
+umsx = load_package()
+C = umsx.configs
+U = umsx.umsx
+
+
+def oracle_desc(cfg) -> OrcDesc:
+    return OrcDesc(cfg.hidden, cfg.intermediate, cfg.experts, cfg.top_k, cfg.quant, cfg.routing, cfg.activation,
+                   int(cfg.fused_gate_up), int(cfg.has_bias), cfg.swiglu_alpha, cfg.swiglu_limit, cfg.routed_scale)
+
+
+def host_weights(orc, cfg, layer: int = 0) -> LayerWeights:
+    """The same tensors umsx_moe_create_synthetic draws on the device, drawn here by the oracle."""
+    E, H, I = cfg.experts, cfg.hidden, cfg.intermediate
+    s = cfg.seed
+    sid = C.stream_id
+    bb = U.BLOCK_BYTES[cfg.quant]
+
+    def blocks(kind, n):
+        if cfg.quant == U.QUANT_MXFP4:
+            return orc.gen_mxfp4(s, sid(layer, kind), 0, n, 119, 5)
+        return orc.gen_q8_0(s, sid(layer, kind), 0, n)
+
+    router_w = orc.gen_normal_f32(s, sid(layer, C.KIND_ROUTER_W), 0, E * H, cfg.router_sigma).reshape(E, H)
+    router_b = orc.gen_normal_f32(s, sid(layer, C.KIND_ROUTER_B), 0, E, cfg.router_bias_sigma) \
+        if cfg.has_router_bias else None
+    gate_up = gate = up = None
+    if cfg.fused_gate_up:
+        gate_up = blocks(C.KIND_GATE_UP, E * 2 * I * (H // 32)).reshape(E, 2 * I, H // 32 * bb)
+    else:
+        gate = blocks(C.KIND_GATE_UP, E * I * (H // 32)).reshape(E, I, H // 32 * bb)
+        up = blocks(C.KIND_UP, E * I * (H // 32)).reshape(E, I, H // 32 * bb)
+    down = blocks(C.KIND_DOWN, E * H * (I // 32)).reshape(E, H, I // 32 * bb)
+    gub = db = None
+    if cfg.has_bias:
+        gub = orc.gen_normal_bf16(s, sid(layer, C.KIND_GU_BIAS), 0, E * 2 * I, cfg.bias_sigma).reshape(E, 2 * I)
+        db = orc.gen_normal_bf16(s, sid(layer, C.KIND_DOWN_BIAS), 0, E * H, cfg.bias_sigma).reshape(E, H)
+    return LayerWeights(router_w, router_b, gate_up, gate, up, down, gub, db)
+
+
+def weights_dict(w: LayerWeights) -> dict:
+    return {k: getattr(w, k) for k in ("router_w", "router_b", "gate_up", "gate", "up", "down", "gate_up_bias",
+                                       "down_bias")}
+
+
+def small_config(**over):
+    """A gpt-oss-shaped layer shrunk so the oracle finishes in milliseconds."""
+    base = dataclasses.replace(C.GPT_OSS_20B, name="small-mxfp4", hidden=256, intermediate=192, experts=8, top_k=2,
+                               seed=11)
+    return dataclasses.replace(base, **over)
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def x_bits(orc, cfg, tokens: int, stream: int = 0xFFFF0, sigma: float = 1.0) -> np.ndarray:
+    return orc.gen_normal_bf16(cfg.seed, stream, 0, tokens * cfg.hidden, sigma).reshape(tokens, cfg.hidden)

@@ -1,0 +1,779 @@
+// C ABI of libumsx: handle lifecycle, weight upload / repack, and the entry
+// points declared in include/umsx.h.  No exception crosses the ABI; failures
+// set a thread-local message and return a umsx_status.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "umsx_internal.h"
+
+using namespace umsx;
+
+namespace {
+
+thread_local std::string g_error;
+thread_local uint64_t g_launches = 0;
+
+umsx_status fail(umsx_status s, const std::string &msg) {
+    g_error = msg;
+    return s;
+}
+
+#define UMSX_CUDA(call)                                                                        \
+    do {                                                                                       \
+        cudaError_t err_ = (call);                                                             \
+        if (err_ != cudaSuccess) return fail(UMSX_EDEVICE, std::string(#call) + ": " + cudaGetErrorString(err_)); \
+    } while (0)
+
+#define UMSX_LAUNCHED(n)                                                                       \
+    do {                                                                                       \
+        g_launches += (uint64_t)(n);                                                           \
+        cudaError_t err_ = cudaGetLastError();                                                 \
+        if (err_ != cudaSuccess) return fail(UMSX_EDEVICE, std::string("kernel launch: ") + cudaGetErrorString(err_)); \
+    } while (0)
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Bump allocator over one device allocation.
+struct Arena {
+    uint8_t *base = nullptr;
+    size_t used = 0, size = 0;
+    template <class T>
+    T *take(size_t count) {
+        const size_t off = used;
+        used = align_up(used + count * sizeof(T));
+        return base ? reinterpret_cast<T *>(base + off) : nullptr;
+    }
+};
+
+float normal_scale(double sigma) { return (float)(sigma * std::sqrt(3.0) / 16777216.0); }
+
+uint64_t stream_id(uint32_t layer, int kind) { return (uint64_t)layer * 16u + (uint64_t)kind; }
+
+size_t block_bytes(int quant) { return quant == UMSX_QUANT_MXFP4 ? 17 : 34; }
+
+}  // namespace
+
+// Per-call scratch: the router's dispatch state, the quantized activations,
+// the per-job expert outputs and forward_host staging.  A layer owns one; a
+// stack owns one shared by all of its layers (they run one after another).
+struct Workspace {
+    Dispatch disp{};
+    uint8_t *act_codes = nullptr;
+    float *act_scales = nullptr;
+    float *y = nullptr;
+    void *x_dev = nullptr;
+    float *out_dev = nullptr;
+    uint8_t *mem = nullptr;
+    int max_tokens = 0;
+};
+
+struct umsx_moe {
+    umsx_moe_desc d{};
+    int device = 0;
+    int e_lo = 0, e_local = 0;
+    float *router_w = nullptr, *router_b = nullptr;
+    Matrix gate_up, gate, up, down;
+    float *gu_bias = nullptr, *down_bias = nullptr;
+    uint8_t *weights_mem = nullptr;
+    Workspace ws;
+    std::mutex mu;
+};
+
+namespace {
+
+umsx_status validate_desc(const umsx_moe_desc *d) {
+    if (!d) return fail(UMSX_EINVAL, "null descriptor");
+    if (d->hidden <= 0 || d->hidden % 64 || d->intermediate <= 0 || d->intermediate % 64)
+        return fail(UMSX_EINVAL, "hidden and intermediate must be positive multiples of 64");
+    if (d->experts <= 0 || d->experts > 1024 || d->top_k <= 0 || d->top_k > 32 || d->top_k > d->experts)
+        return fail(UMSX_EINVAL, "need 1 <= top_k <= min(32, experts) and experts <= 1024");
+    if (d->quant != UMSX_QUANT_MXFP4 && d->quant != UMSX_QUANT_Q8_0) return fail(UMSX_EUNSUPPORTED, "quant must be MXFP4 or Q8_0");
+    if (d->routing < 0 || d->routing > 2) return fail(UMSX_EINVAL, "unknown routing mode");
+    if (d->activation != UMSX_ACT_SILU && d->activation != UMSX_ACT_SWIGLU_OAI) return fail(UMSX_EINVAL, "unknown activation");
+    if (d->max_tokens <= 0 || d->max_tokens > 65536) return fail(UMSX_EINVAL, "max_tokens must be in [1, 65536]");
+    const int world = d->ep_world <= 0 ? 1 : d->ep_world;
+    if (d->experts % world || d->ep_rank < 0 || d->ep_rank >= world)
+        return fail(UMSX_EINVAL, "experts must split evenly over ep_world and 0 <= ep_rank < ep_world");
+    if (world != 1) return fail(UMSX_EUNSUPPORTED, "expert-parallel handles are created per rank with ep_world == 1 in this build");
+    return UMSX_OK;
+}
+
+size_t weight_bytes(const umsx_moe *m, Arena &a) {
+    const auto &d = m->d;
+    const int H = d.hidden, I = d.intermediate, E = d.experts, EL = m->e_local;
+    a.take<float>((size_t)E * H);
+    if (d.has_router_bias) a.take<float>(E);
+    auto mat = [&](Matrix &mm, int rows, int cols) {
+        mm.rows = rows;
+        mm.cols = cols;
+        mm.quant = d.quant;
+        mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
+        mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
+    };
+    Matrix tmp;
+    if (d.fused_gate_up) mat(tmp, 2 * I, H);
+    else { mat(tmp, I, H); mat(tmp, I, H); }
+    mat(tmp, H, I);
+    if (d.has_bias) { a.take<float>((size_t)EL * 2 * I); a.take<float>((size_t)EL * H); }
+    return a.used;
+}
+
+void carve_weights(umsx_moe *m, Arena &a) {
+    const auto &d = m->d;
+    const int H = d.hidden, I = d.intermediate, E = d.experts, EL = m->e_local;
+    m->router_w = a.take<float>((size_t)E * H);
+    if (d.has_router_bias) m->router_b = a.take<float>(E);
+    auto mat = [&](Matrix &mm, int rows, int cols) {
+        mm.rows = rows;
+        mm.cols = cols;
+        mm.quant = d.quant;
+        mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
+        mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
+    };
+    if (d.fused_gate_up) mat(m->gate_up, 2 * I, H);
+    else { mat(m->gate, I, H); mat(m->up, I, H); }
+    mat(m->down, H, I);
+    if (d.has_bias) {
+        m->gu_bias = a.take<float>((size_t)EL * 2 * I);
+        m->down_bias = a.take<float>((size_t)EL * H);
+    }
+}
+
+void carve_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_tokens, Arena &a) {
+    const size_t T = max_tokens, K = d.top_k, E = d.experts, EL = e_local, H = d.hidden, I = d.intermediate;
+    Dispatch &p = w.disp;
+    p.logits = a.take<float>(T * E);
+    p.ids = a.take<int32_t>(T * K);
+    p.weights = a.take<float>(T * K);
+    p.token_done = a.take<uint32_t>(T);
+    p.all_done = a.take<uint32_t>(1);
+    p.counts = a.take<int32_t>(EL);
+    p.offsets = a.take<int32_t>(EL + 1);
+    p.active = a.take<int32_t>(EL);
+    p.n_active = a.take<int32_t>(1);
+    p.job_token = a.take<int32_t>(T * K);
+    p.job_rank = a.take<int32_t>(T * K);
+    p.xq_codes = a.take<uint8_t>(T * H);
+    p.xq_scales = a.take<float>(T * (H / 32));
+    w.act_codes = a.take<uint8_t>(T * K * I);
+    w.act_scales = a.take<float>(T * K * (I / 32));
+    w.y = a.take<float>(T * K * H);
+    w.x_dev = a.take<float>(T * H);
+    w.out_dev = a.take<float>(T * H);
+    w.max_tokens = max_tokens;
+}
+
+// Allocates and zeroes a workspace (the router's completion counters must start at zero).
+umsx_status alloc_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_tokens, size_t reserve) {
+    Arena probe;
+    carve_workspace(w, d, e_local, max_tokens, probe);
+    size_t free_b = 0, total_b = 0;
+    UMSX_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    if (free_b < reserve || probe.used + (64u << 20) > free_b - reserve)
+        return fail(UMSX_EOOM, "workspace of " + std::to_string(probe.used) + " bytes would violate the free-memory reserve");
+    UMSX_CUDA(cudaMalloc(&w.mem, probe.used));
+    Arena a{w.mem, 0, probe.used};
+    carve_workspace(w, d, e_local, max_tokens, a);
+    UMSX_CUDA(cudaMemset(w.mem, 0, probe.used));
+    return UMSX_OK;
+}
+
+umsx_status allocate(umsx_moe *m, size_t reserve) {
+    Arena wa;
+    const size_t wbytes = weight_bytes(m, wa);
+    size_t free_b = 0, total_b = 0;
+    UMSX_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    if (free_b < reserve || wbytes + (64u << 20) > free_b - reserve)
+        return fail(UMSX_EOOM, "allocation of " + std::to_string(wbytes) + " weight bytes would violate the " +
+                                   std::to_string(reserve) + "-byte free-memory reserve");
+    UMSX_CUDA(cudaMalloc(&m->weights_mem, wbytes));
+    Arena w2{m->weights_mem, 0, wbytes};
+    carve_weights(m, w2);
+    return alloc_workspace(m->ws, m->d, m->e_local, m->d.max_tokens, reserve);
+}
+
+umsx_status make_handle(const umsx_moe_desc *desc, int device, size_t reserve, umsx_moe **out) {
+    if (!out) return fail(UMSX_EINVAL, "null output handle pointer");
+    *out = nullptr;
+    if (umsx_status s = validate_desc(desc)) return s;
+    int count = 0;
+    UMSX_CUDA(cudaGetDeviceCount(&count));
+    if (device < 0 || device >= count) return fail(UMSX_EINVAL, "device index out of range");
+    UMSX_CUDA(cudaSetDevice(device));
+    auto *m = new umsx_moe();
+    m->d = *desc;
+    if (m->d.ep_world <= 0) m->d.ep_world = 1;
+    m->device = device;
+    m->e_local = desc->experts / m->d.ep_world;
+    m->e_lo = m->d.ep_rank * m->e_local;
+    if (umsx_status s = allocate(m, reserve)) {
+        umsx_moe_destroy(m);
+        return s;
+    }
+    *out = m;
+    return UMSX_OK;
+}
+
+// Upload expert `le` of a matrix from ggml-layout host bytes through a device staging buffer.
+umsx_status upload_matrix(Matrix &mm, const void *host_all, int e_global_lo, int e_local, uint8_t *staging) {
+    const size_t per = (size_t)mm.rows * (mm.cols / 32) * block_bytes(mm.quant);
+    for (int le = 0; le < e_local; ++le) {
+        const uint8_t *src = static_cast<const uint8_t *>(host_all) + (size_t)(e_global_lo + le) * per;
+        UMSX_CUDA(cudaMemcpy(staging, src, per, cudaMemcpyHostToDevice));
+        UMSX_LAUNCHED(launch_repack(mm, le, staging, 0));
+    }
+    return UMSX_OK;
+}
+
+umsx_status generate_matrix(Matrix &mm, uint64_t seed, uint64_t stream, int e_global_lo, int e_local, uint8_t *staging) {
+    const uint64_t nblk = (uint64_t)mm.rows * (mm.cols / 32);
+    for (int le = 0; le < e_local; ++le) {
+        UMSX_LAUNCHED(launch_gen_blocks(mm.quant, seed, stream, (uint64_t)(e_global_lo + le) * nblk, nblk, staging, 0));
+        UMSX_LAUNCHED(launch_repack(mm, le, staging, 0));
+    }
+    return UMSX_OK;
+}
+
+size_t max_expert_bytes(const umsx_moe *m) {
+    const auto &d = m->d;
+    const size_t bb = block_bytes(d.quant);
+    const size_t gu = (size_t)(d.fused_gate_up ? 2 : 1) * d.intermediate * (d.hidden / 32) * bb;
+    const size_t dn = (size_t)d.hidden * (d.intermediate / 32) * bb;
+    return std::max(gu, dn);
+}
+
+bool resident(const umsx_moe *m, int e) { return e >= m->e_lo && e < m->e_lo + m->e_local; }
+
+}  // namespace
+
+extern "C" {
+
+int umsx_version(void) { return UMSX_VERSION; }
+
+const char *umsx_last_error(void) { return g_error.c_str(); }
+
+uint64_t umsx_kernel_launches(void) { return g_launches; }
+
+umsx_status umsx_moe_create(const umsx_moe_desc *desc, const umsx_moe_weights *w, int device, size_t reserve_bytes,
+                            umsx_moe **out) {
+    if (!w || !w->router_w || !w->down || (desc && desc->fused_gate_up ? !w->gate_up : (!w->gate || !w->up)))
+        return fail(UMSX_EINVAL, "missing router, gate/up or down weights");
+    if (desc && desc->has_router_bias && !w->router_b) return fail(UMSX_EINVAL, "has_router_bias set but router_b is null");
+    if (desc && desc->has_bias && (!w->gate_up_bias || !w->down_bias)) return fail(UMSX_EINVAL, "has_bias set but biases are null");
+    umsx_moe *m = nullptr;
+    if (umsx_status s = make_handle(desc, device, reserve_bytes, &m)) return s;
+    const auto &d = m->d;
+    const int H = d.hidden, I = d.intermediate, E = d.experts;
+    uint8_t *staging = nullptr;
+    umsx_status st = UMSX_OK;
+    auto run = [&]() -> umsx_status {
+        UMSX_CUDA(cudaMemcpy(m->router_w, w->router_w, (size_t)E * H * sizeof(float), cudaMemcpyHostToDevice));
+        if (d.has_router_bias) UMSX_CUDA(cudaMemcpy(m->router_b, w->router_b, (size_t)E * sizeof(float), cudaMemcpyHostToDevice));
+        UMSX_CUDA(cudaMalloc(&staging, max_expert_bytes(m)));
+        if (d.fused_gate_up) {
+            if (umsx_status s = upload_matrix(m->gate_up, w->gate_up, m->e_lo, m->e_local, staging)) return s;
+        } else {
+            if (umsx_status s = upload_matrix(m->gate, w->gate, m->e_lo, m->e_local, staging)) return s;
+            if (umsx_status s = upload_matrix(m->up, w->up, m->e_lo, m->e_local, staging)) return s;
+        }
+        if (umsx_status s = upload_matrix(m->down, w->down, m->e_lo, m->e_local, staging)) return s;
+        if (d.has_bias) {
+            std::vector<float> gb((size_t)m->e_local * 2 * I), db((size_t)m->e_local * H);
+            for (size_t i = 0; i < gb.size(); ++i) {
+                const uint32_t bits = (uint32_t)w->gate_up_bias[(size_t)m->e_lo * 2 * I + i] << 16;
+                std::memcpy(&gb[i], &bits, 4);
+            }
+            for (size_t i = 0; i < db.size(); ++i) {
+                const uint32_t bits = (uint32_t)w->down_bias[(size_t)m->e_lo * H + i] << 16;
+                std::memcpy(&db[i], &bits, 4);
+            }
+            UMSX_CUDA(cudaMemcpy(m->gu_bias, gb.data(), gb.size() * 4, cudaMemcpyHostToDevice));
+            UMSX_CUDA(cudaMemcpy(m->down_bias, db.data(), db.size() * 4, cudaMemcpyHostToDevice));
+        }
+        UMSX_CUDA(cudaDeviceSynchronize());
+        return UMSX_OK;
+    };
+    st = run();
+    if (staging) cudaFree(staging);
+    if (st) { umsx_moe_destroy(m); return st; }
+    *out = m;
+    return UMSX_OK;
+}
+
+umsx_status umsx_moe_create_synthetic(const umsx_moe_desc *desc, uint64_t seed, uint32_t layer, float router_sigma,
+                                      float router_bias_sigma, float bias_sigma, int device, size_t reserve_bytes,
+                                      umsx_moe **out) {
+    umsx_moe *m = nullptr;
+    if (umsx_status s = make_handle(desc, device, reserve_bytes, &m)) return s;
+    const auto &d = m->d;
+    const int H = d.hidden, I = d.intermediate, E = d.experts;
+    uint8_t *staging = nullptr;
+    auto run = [&]() -> umsx_status {
+        UMSX_LAUNCHED(launch_gen_normal_f32(seed, stream_id(layer, 0), 0, (uint64_t)E * H, normal_scale(router_sigma), m->router_w, 0));
+        if (d.has_router_bias)
+            UMSX_LAUNCHED(launch_gen_normal_f32(seed, stream_id(layer, 1), 0, (uint64_t)E, normal_scale(router_bias_sigma), m->router_b, 0));
+        UMSX_CUDA(cudaMalloc(&staging, max_expert_bytes(m)));
+        if (d.fused_gate_up) {
+            if (umsx_status s = generate_matrix(m->gate_up, seed, stream_id(layer, 2), m->e_lo, m->e_local, staging)) return s;
+        } else {
+            if (umsx_status s = generate_matrix(m->gate, seed, stream_id(layer, 2), m->e_lo, m->e_local, staging)) return s;
+            if (umsx_status s = generate_matrix(m->up, seed, stream_id(layer, 3), m->e_lo, m->e_local, staging)) return s;
+        }
+        if (umsx_status s = generate_matrix(m->down, seed, stream_id(layer, 4), m->e_lo, m->e_local, staging)) return s;
+        if (d.has_bias) {
+            UMSX_LAUNCHED(launch_gen_normal_bf16_to_f32(seed, stream_id(layer, 5), (uint64_t)m->e_lo * 2 * I,
+                                                        (uint64_t)m->e_local * 2 * I, normal_scale(bias_sigma), m->gu_bias, 0));
+            UMSX_LAUNCHED(launch_gen_normal_bf16_to_f32(seed, stream_id(layer, 6), (uint64_t)m->e_lo * H,
+                                                        (uint64_t)m->e_local * H, normal_scale(bias_sigma), m->down_bias, 0));
+        }
+        UMSX_CUDA(cudaDeviceSynchronize());
+        return UMSX_OK;
+    };
+    const umsx_status st = run();
+    if (staging) cudaFree(staging);
+    if (st) { umsx_moe_destroy(m); return st; }
+    *out = m;
+    return UMSX_OK;
+}
+
+void umsx_moe_destroy(umsx_moe *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    cudaDeviceSynchronize();
+    if (m->weights_mem) cudaFree(m->weights_mem);
+    if (m->ws.mem) cudaFree(m->ws.mem);
+    delete m;
+}
+
+}  // extern "C"
+
+namespace {
+
+umsx_status check_call(umsx_moe *m, const void *x, int x_dtype, int tokens, int max_tokens) {
+    if (!m) return fail(UMSX_EINVAL, "null handle");
+    if (!x) return fail(UMSX_EINVAL, "null input");
+    if (x_dtype != UMSX_DTYPE_F32 && x_dtype != UMSX_DTYPE_BF16) return fail(UMSX_EINVAL, "x_dtype must be F32 or BF16");
+    if (tokens <= 0 || tokens > max_tokens) return fail(UMSX_EINVAL, "tokens must be in [1, max_tokens]");
+    return UMSX_OK;
+}
+
+umsx_status run_router(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, int rmsnorm, float eps,
+                       cudaStream_t s) {
+    RouterParams p{};
+    p.x = x;
+    p.x_dtype = x_dtype;
+    p.tokens = tokens;
+    p.hidden = m->d.hidden;
+    p.experts = m->d.experts;
+    p.top_k = m->d.top_k;
+    p.routing = m->d.routing;
+    p.routed_scale = m->d.routed_scale;
+    p.w = m->router_w;
+    p.b = m->router_b;
+    p.e_lo = m->e_lo;
+    p.e_local = m->e_local;
+    p.rmsnorm = rmsnorm;
+    p.eps = eps;
+    UMSX_LAUNCHED(launch_router(p, ws.disp, s));
+    return UMSX_OK;
+}
+
+// Records an optional timing event; inside stream capture it becomes an external
+// event-record node, so a replayed graph still timestamps the stage boundary.
+umsx_status mark(cudaEvent_t ev, cudaStream_t s) {
+    if (!ev) return UMSX_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    UMSX_CUDA(cudaStreamIsCapturing(s, &cs));
+    if (cs == cudaStreamCaptureStatusActive) UMSX_CUDA(cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal));
+    else UMSX_CUDA(cudaEventRecord(ev, s));
+    return UMSX_OK;
+}
+
+// router -> gate_up (+act, +Q8_0) -> down -> combine (+ optional residual).
+// ev: null or 5 events bracketing the four stages.
+umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
+                      const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev) {
+    const auto &d = m->d;
+    if (ev) if (umsx_status st = mark(ev[0], s)) return st;
+    if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s)) return st;
+    if (ev) if (umsx_status st = mark(ev[1], s)) return st;
+    const int slots = std::min(m->e_local, tokens * d.top_k);
+    GateUpParams g{};
+    g.gate_up = m->gate_up;
+    g.gate = m->gate;
+    g.up = m->up;
+    g.fused = d.fused_gate_up;
+    g.bias = m->gu_bias;
+    g.intermediate = d.intermediate;
+    g.hidden = d.hidden;
+    g.activation = d.activation;
+    g.alpha = d.swiglu_alpha;
+    g.limit = d.swiglu_limit;
+    g.act_codes = ws.act_codes;
+    g.act_scales = ws.act_scales;
+    UMSX_LAUNCHED(launch_gate_up(g, ws.disp, slots, tokens, s));
+    if (ev) if (umsx_status st = mark(ev[2], s)) return st;
+    GemvParams p{};
+    p.m = m->down;
+    p.bias = m->down_bias;
+    p.a_by_job = 1;
+    p.out = ws.y;
+    p.o_ts = d.top_k;
+    UMSX_LAUNCHED(launch_gemv_internal(p, ws.act_codes, ws.act_scales, ws.disp, slots, tokens, s));
+    if (ev) if (umsx_status st = mark(ev[3], s)) return st;
+    UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, s));
+    if (ev) if (umsx_status st = mark(ev[4], s)) return st;
+    return UMSX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+umsx_status umsx_moe_forward(umsx_moe *m, const void *x, int x_dtype, int tokens, float *out, int32_t *ids,
+                             float *weights, umsx_stream stream) {
+    if (umsx_status st = check_call(m, x, x_dtype, tokens, m ? m->d.max_tokens : 0)) return st;
+    if (!out) return fail(UMSX_EINVAL, "null output");
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (umsx_status st = run_layer(m, m->ws, x, x_dtype, tokens, out, nullptr, 0, 0.0f, s, nullptr)) return st;
+    const size_t n = (size_t)tokens * m->d.top_k;
+    if (ids) UMSX_CUDA(cudaMemcpyAsync(ids, m->ws.disp.ids, n * 4, cudaMemcpyDeviceToDevice, s));
+    if (weights) UMSX_CUDA(cudaMemcpyAsync(weights, m->ws.disp.weights, n * 4, cudaMemcpyDeviceToDevice, s));
+    return UMSX_OK;
+}
+
+umsx_status umsx_moe_forward_host(umsx_moe *m, const void *x, int x_dtype, int tokens, float *out, umsx_stream stream) {
+    if (umsx_status st = check_call(m, x, x_dtype, tokens, m ? m->d.max_tokens : 0)) return st;
+    if (!out) return fail(UMSX_EINVAL, "null output");
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t in_bytes = (size_t)tokens * m->d.hidden * (x_dtype == UMSX_DTYPE_BF16 ? 2 : 4);
+    const size_t out_bytes = (size_t)tokens * m->d.hidden * 4;
+    UMSX_CUDA(cudaMemcpyAsync(m->ws.x_dev, x, in_bytes, cudaMemcpyHostToDevice, s));
+    if (umsx_status st = run_layer(m, m->ws, m->ws.x_dev, x_dtype, tokens, m->ws.out_dev, nullptr, 0, 0.0f, s, nullptr))
+        return st;
+    UMSX_CUDA(cudaMemcpyAsync(out, m->ws.out_dev, out_bytes, cudaMemcpyDeviceToHost, s));
+    UMSX_CUDA(cudaStreamSynchronize(s));
+    return UMSX_OK;
+}
+
+umsx_status umsx_route(umsx_moe *m, const void *x, int x_dtype, int tokens, int32_t *ids, float *weights,
+                       int32_t *counts, umsx_stream stream) {
+    if (umsx_status st = check_call(m, x, x_dtype, tokens, m ? m->d.max_tokens : 0)) return st;
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (umsx_status st = run_router(m, m->ws, x, x_dtype, tokens, 0, 0.0f, s)) return st;
+    const Dispatch &d = m->ws.disp;
+    const size_t n = (size_t)tokens * m->d.top_k;
+    if (ids) UMSX_CUDA(cudaMemcpyAsync(ids, d.ids, n * 4, cudaMemcpyDeviceToDevice, s));
+    if (weights) UMSX_CUDA(cudaMemcpyAsync(weights, d.weights, n * 4, cudaMemcpyDeviceToDevice, s));
+    if (counts) UMSX_CUDA(cudaMemcpyAsync(counts, d.counts, (size_t)m->e_local * 4, cudaMemcpyDeviceToDevice, s));
+    return UMSX_OK;
+}
+
+umsx_status umsx_expert_down_q8(umsx_moe *m, const void *packed_q8, const int32_t *experts, int jobs, float *out,
+                                umsx_stream stream) {
+    if (!m) return fail(UMSX_EINVAL, "null handle");
+    if (jobs < 0 || jobs > m->d.max_tokens * m->d.top_k) return fail(UMSX_EINVAL, "invalid packed Q8 input shape");
+    if (jobs == 0) return UMSX_OK;
+    if (!packed_q8 || !experts || !out) return fail(UMSX_EINVAL, "null buffer");
+    std::vector<int32_t> counts(m->e_local, 0), offsets(m->e_local + 1, 0), active, token(jobs), rank(jobs, 0);
+    for (int j = 0; j < jobs; ++j) {
+        if (!resident(m, experts[j])) return fail(UMSX_ENOTRESIDENT, "MXFP4 GPU expert is out of range or not resident");
+        counts[experts[j] - m->e_lo]++;
+    }
+    int maxc = 0;
+    for (int e = 0; e < m->e_local; ++e) {
+        offsets[e + 1] = offsets[e] + counts[e];
+        if (counts[e]) active.push_back(e);
+        maxc = std::max(maxc, counts[e]);
+    }
+    std::vector<int32_t> fill(offsets.begin(), offsets.end() - 1);
+    for (int j = 0; j < jobs; ++j) token[fill[experts[j] - m->e_lo]++] = j;
+    const int n_active = (int)active.size();
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const Dispatch &d = m->ws.disp;
+    // pageable sources: each copy is staged before cudaMemcpyAsync returns
+    UMSX_CUDA(cudaMemcpyAsync(d.counts, counts.data(), counts.size() * 4, cudaMemcpyHostToDevice, s));
+    UMSX_CUDA(cudaMemcpyAsync(d.offsets, offsets.data(), offsets.size() * 4, cudaMemcpyHostToDevice, s));
+    UMSX_CUDA(cudaMemcpyAsync(d.active, active.data(), active.size() * 4, cudaMemcpyHostToDevice, s));
+    UMSX_CUDA(cudaMemcpyAsync(d.n_active, &n_active, 4, cudaMemcpyHostToDevice, s));
+    UMSX_CUDA(cudaMemcpyAsync(d.job_token, token.data(), token.size() * 4, cudaMemcpyHostToDevice, s));
+    UMSX_CUDA(cudaMemcpyAsync(d.job_rank, rank.data(), rank.size() * 4, cudaMemcpyHostToDevice, s));
+    GemvParams p{};
+    p.m = m->down;
+    p.bias = m->down_bias;
+    p.a_q8 = static_cast<const uint8_t *>(packed_q8);
+    p.a_ts = 1;
+    p.a_rs = 0;
+    p.out = out;
+    p.o_ts = 1;
+    UMSX_LAUNCHED(launch_gemv(p, d, n_active, maxc, s));
+    return UMSX_OK;
+}
+
+static const Matrix *projection(umsx_moe *m, int proj) {
+    switch (proj) {
+        case UMSX_PROJ_GATE_UP: return m->d.fused_gate_up ? &m->gate_up : nullptr;
+        case UMSX_PROJ_GATE: return m->d.fused_gate_up ? nullptr : &m->gate;
+        case UMSX_PROJ_UP: return m->d.fused_gate_up ? nullptr : &m->up;
+        case UMSX_PROJ_DOWN: return &m->down;
+        default: return nullptr;
+    }
+}
+
+umsx_status umsx_mul_mat_id(umsx_moe *m, int proj, const float *b, int n_b, const int32_t *ids, int n_ids, int tokens,
+                            float *dst, umsx_stream stream) {
+    if (!m || !b || !ids || !dst) return fail(UMSX_EINVAL, "null argument");
+    if (tokens <= 0 || n_ids <= 0 || n_ids > m->d.experts || (n_b != 1 && n_b != n_ids) ||
+        (size_t)tokens * n_ids > (size_t)m->d.max_tokens * m->d.top_k)
+        return fail(UMSX_EINVAL, "invalid MUL_MAT_ID shape");
+    const Matrix *mat = projection(m, proj);
+    if (!mat) return fail(UMSX_EINVAL, "projection not present in this layer");
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Dispatch d = m->ws.disp;
+    d.ids = const_cast<int32_t *>(ids);
+    UMSX_CUDA(cudaMemsetAsync(dst, 0, (size_t)tokens * n_ids * mat->rows * sizeof(float), s));
+    UMSX_LAUNCHED(launch_dispatch(d, tokens * n_ids, n_ids, m->e_lo, m->e_local, s));
+    GemvParams p{};
+    p.m = *mat;
+    p.a_f32 = b;
+    p.a_ts = n_b;
+    p.a_rs = n_b == 1 ? 0 : 1;
+    p.out = dst;
+    p.o_ts = n_ids;
+    UMSX_LAUNCHED(launch_gemv(p, d, std::min(m->e_local, tokens * n_ids), tokens, s));
+    return UMSX_OK;
+}
+
+umsx_status umsx_combine(const float *y, const float *weights, int tokens, int top_k, int width, float *out,
+                         umsx_stream stream) {
+    if (!y || !weights || !out || tokens <= 0 || top_k <= 0 || width <= 0 || width % 4)
+        return fail(UMSX_EINVAL, "invalid combine arguments (width must be a multiple of 4)");
+    UMSX_LAUNCHED(launch_combine(y, weights, tokens, top_k, width, nullptr, out, static_cast<cudaStream_t>(stream)));
+    return UMSX_OK;
+}
+
+umsx_status umsx_moe_export_expert(umsx_moe *m, int proj, int expert, void *host_out, size_t size) {
+    if (!m || !host_out) return fail(UMSX_EINVAL, "null argument");
+    const Matrix *mat = projection(m, proj);
+    if (!mat) return fail(UMSX_EINVAL, "projection not present in this layer");
+    if (!resident(m, expert)) return fail(UMSX_ENOTRESIDENT, "expert out of range or not resident");
+    const size_t per = (size_t)mat->rows * (mat->cols / 32) * block_bytes(mat->quant);
+    if (size != per) return fail(UMSX_EINVAL, "export buffer size mismatch");
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    uint8_t *tmp = nullptr;
+    UMSX_CUDA(cudaMalloc(&tmp, per));
+    umsx_status st = UMSX_OK;
+    g_launches += (uint64_t)launch_export(*mat, expert - m->e_lo, tmp, 0);
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) err = cudaMemcpy(host_out, tmp, per, cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) st = fail(UMSX_EDEVICE, std::string("export: ") + cudaGetErrorString(err));
+    cudaFree(tmp);
+    return st;
+}
+
+}  // extern "C"
+
+// ============================================================================
+// Layer stack: h <- h + MoE_l(RMSNorm(h)) for l = 0..L-1, replayed as one CUDA
+// graph per (token count, input dtype) on a library-owned stream.
+// ============================================================================
+
+struct umsx_stack {
+    std::vector<umsx_moe *> layers;
+    float eps = 1e-5f;
+    int device = 0;
+    int max_tokens = 0;
+    int hidden = 0;
+    Workspace ws;
+    float *h = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    std::vector<cudaEvent_t> stage;  // 5 per layer while timing is on
+    bool timing = false;
+    struct Graph { int tokens, dtype; bool timing; cudaGraphExec_t exec; uint64_t kernels; };
+    std::vector<Graph> graphs;
+    std::mutex mu;
+};
+
+namespace {
+
+void drop_graphs(umsx_stack *st) {
+    for (auto &g : st->graphs) cudaGraphExecDestroy(g.exec);
+    st->graphs.clear();
+}
+
+umsx_status record_stack(umsx_stack *st, int tokens, int dtype, cudaStream_t s) {
+    const int H = st->hidden;
+    if (dtype == UMSX_DTYPE_BF16)
+        UMSX_LAUNCHED(launch_bf16_to_f32(static_cast<const uint16_t *>(st->ws.x_dev), st->h, (size_t)tokens * H, s));
+    else
+        UMSX_CUDA(cudaMemcpyAsync(st->h, st->ws.x_dev, (size_t)tokens * H * 4, cudaMemcpyDeviceToDevice, s));
+    for (size_t l = 0; l < st->layers.size(); ++l) {
+        const cudaEvent_t *ev = st->timing ? &st->stage[5 * l] : nullptr;
+        if (umsx_status r = run_layer(st->layers[l], st->ws, st->h, UMSX_DTYPE_F32, tokens, st->h, st->h, 1, st->eps, s, ev))
+            return r;
+    }
+    return UMSX_OK;
+}
+
+umsx_status stack_graph(umsx_stack *st, int tokens, int dtype, umsx_stack::Graph **out) {
+    for (auto &g : st->graphs)
+        if (g.tokens == tokens && g.dtype == dtype && g.timing == st->timing) { *out = &g; return UMSX_OK; }
+    const uint64_t before = g_launches;
+    UMSX_CUDA(cudaStreamBeginCapture(st->stream, cudaStreamCaptureModeThreadLocal));
+    umsx_status r = record_stack(st, tokens, dtype, st->stream);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(st->stream, &graph);
+    if (r) { if (graph) cudaGraphDestroy(graph); return r; }
+    if (e != cudaSuccess) return fail(UMSX_EDEVICE, std::string("stack capture: ") + cudaGetErrorString(e));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return fail(UMSX_EDEVICE, std::string("stack instantiate: ") + cudaGetErrorString(ie));
+    const uint64_t kernels = g_launches - before;
+    g_launches = before;  // counted per replay instead
+    st->graphs.push_back({tokens, dtype, st->timing, exec, kernels});
+    *out = &st->graphs.back();
+    return UMSX_OK;
+}
+
+umsx_status stack_run(umsx_stack *st, const void *x, int dtype, int tokens, void *out, cudaMemcpyKind in_kind,
+                      cudaMemcpyKind out_kind, cudaStream_t caller) {
+    const size_t in_bytes = (size_t)tokens * st->hidden * (dtype == UMSX_DTYPE_BF16 ? 2 : 4);
+    const size_t out_bytes = (size_t)tokens * st->hidden * 4;
+    umsx_stack::Graph *g = nullptr;
+    if (umsx_status r = stack_graph(st, tokens, dtype, &g)) return r;
+    UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
+    UMSX_CUDA(cudaStreamWaitEvent(st->stream, st->ev_in, 0));
+    UMSX_CUDA(cudaMemcpyAsync(st->ws.x_dev, x, in_bytes, in_kind, st->stream));
+    UMSX_CUDA(cudaGraphLaunch(g->exec, st->stream));
+    g_launches += g->kernels;
+    UMSX_CUDA(cudaMemcpyAsync(out, st->h, out_bytes, out_kind, st->stream));
+    UMSX_CUDA(cudaEventRecord(st->ev_out, st->stream));
+    UMSX_CUDA(cudaStreamWaitEvent(caller, st->ev_out, 0));
+    return UMSX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+umsx_status umsx_stack_create(umsx_moe *const *layers, int n_layers, int max_tokens, float rms_eps, umsx_stack **out) {
+    if (!out || !layers || n_layers <= 0) return fail(UMSX_EINVAL, "need at least one layer");
+    *out = nullptr;
+    const umsx_moe *l0 = layers[0];
+    if (!l0) return fail(UMSX_EINVAL, "null layer");
+    for (int l = 0; l < n_layers; ++l) {
+        const umsx_moe *m = layers[l];
+        if (!m || m->device != l0->device || m->d.hidden != l0->d.hidden || m->d.top_k != l0->d.top_k ||
+            m->d.experts != l0->d.experts || m->d.intermediate != l0->d.intermediate || m->e_local != l0->e_local)
+            return fail(UMSX_EINVAL, "stack layers must share device and shape");
+    }
+    if (max_tokens <= 0 || max_tokens > 65535) return fail(UMSX_EINVAL, "max_tokens must be in [1, 65535]");
+    UMSX_CUDA(cudaSetDevice(l0->device));
+    auto *st = new umsx_stack();
+    st->layers.assign(layers, layers + n_layers);
+    st->eps = rms_eps;
+    st->device = l0->device;
+    st->max_tokens = max_tokens;
+    st->hidden = l0->d.hidden;
+    auto run = [&]() -> umsx_status {
+        if (umsx_status r = alloc_workspace(st->ws, l0->d, l0->e_local, max_tokens, 0)) return r;
+        UMSX_CUDA(cudaMalloc(&st->h, (size_t)max_tokens * st->hidden * 4));
+        UMSX_CUDA(cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking));
+        UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_in, cudaEventDisableTiming));
+        UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_out, cudaEventDisableTiming));
+        return UMSX_OK;
+    };
+    if (umsx_status r = run()) { umsx_stack_destroy(st); return r; }
+    *out = st;
+    return UMSX_OK;
+}
+
+void umsx_stack_destroy(umsx_stack *st) {
+    if (!st) return;
+    cudaSetDevice(st->device);
+    if (st->stream) cudaStreamSynchronize(st->stream);
+    drop_graphs(st);
+    for (auto e : st->stage) cudaEventDestroy(e);
+    if (st->ev_in) cudaEventDestroy(st->ev_in);
+    if (st->ev_out) cudaEventDestroy(st->ev_out);
+    if (st->stream) cudaStreamDestroy(st->stream);
+    if (st->h) cudaFree(st->h);
+    if (st->ws.mem) cudaFree(st->ws.mem);
+    delete st;
+}
+
+umsx_status umsx_stack_forward(umsx_stack *st, const void *x, int x_dtype, int tokens, float *out, umsx_stream stream) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    if (umsx_status r = check_call(st->layers[0], x, x_dtype, tokens, st->max_tokens)) return r;
+    if (!out) return fail(UMSX_EINVAL, "null output");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->device));
+    return stack_run(st, x, x_dtype, tokens, out, cudaMemcpyDeviceToDevice, cudaMemcpyDeviceToDevice,
+                     static_cast<cudaStream_t>(stream));
+}
+
+umsx_status umsx_stack_forward_host(umsx_stack *st, const void *x, int x_dtype, int tokens, float *out,
+                                    umsx_stream stream) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    if (umsx_status r = check_call(st->layers[0], x, x_dtype, tokens, st->max_tokens)) return r;
+    if (!out) return fail(UMSX_EINVAL, "null output");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (umsx_status r = stack_run(st, x, x_dtype, tokens, out, cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost, s))
+        return r;
+    UMSX_CUDA(cudaStreamSynchronize(s));
+    return UMSX_OK;
+}
+
+umsx_status umsx_stack_set_timing(umsx_stack *st, int enable) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->device));
+    st->timing = enable != 0;
+    if (st->timing && st->stage.empty()) {
+        st->stage.resize(5 * st->layers.size());
+        for (auto &e : st->stage) UMSX_CUDA(cudaEventCreate(&e));
+    }
+    return UMSX_OK;
+}
+
+umsx_status umsx_stack_stage_times(umsx_stack *st, float *ms, int n_stages) {
+    if (!st || !ms || n_stages != 4) return fail(UMSX_EINVAL, "need a stack and room for 4 stage times");
+    if (!st->timing) return fail(UMSX_EINVAL, "timing is not enabled on this stack");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->device));
+    UMSX_CUDA(cudaStreamSynchronize(st->stream));
+    for (int k = 0; k < 4; ++k) ms[k] = 0.0f;
+    for (size_t l = 0; l < st->layers.size(); ++l) {
+        for (int k = 0; k < 4; ++k) {
+            float t = 0.0f;
+            UMSX_CUDA(cudaEventElapsedTime(&t, st->stage[5 * l + k], st->stage[5 * l + k + 1]));
+            ms[k] += t;
+        }
+    }
+    return UMSX_OK;
+}
+
+}  // extern "C"

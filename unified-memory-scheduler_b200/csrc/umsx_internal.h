@@ -1,0 +1,107 @@
+// Internal structures of libumsx (not part of the C ABI).
+//
+// Device layout of an expert matrix (N rows x K columns, nb = K/32 blocks):
+// rows are taken eight at a time ("row group", rg) and blocks in groups of
+// four (MXFP4) or two (Q8_0).  One (row group, block group) is a 512-byte chunk
+// that one warp reads with one 16-byte load per lane; lane = 4*w + p serves
+// row w of the group and the lane pair (p, p+4) of the reference's eight-lane
+// dot (elements 4p..4p+3 and 16+4p..16+4p+3 of each block):
+//   MXFP4 code plane: chunk[((w*4+p)*nblk + j)*4 .. +4] = one 32-bit word per block:
+//          low 16 bits = codes of elements 4p..4p+3 (4 bits each),
+//          high 16 bits = codes of elements 16+4p..16+4p+3
+//   MXFP4 exponent plane: 8 bytes per block per row group: [w*nblk + j]
+//   Q8_0 code plane: chunk[((w*4+p)*2 + j)*8 .. +8] = codes 4p..4p+3 then 16+4p..16+4p+3
+//   Q8_0 scale plane: fp16 bits, [w*2 + j] within a 32-byte chunk per block pair
+// The last MXFP4 group of a row holds 2 blocks when nb % 4 == 2 (nb is even).
+// Both planes keep the ggml byte count (17 or 34 bytes per 32 weights).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/umsx.h"
+
+namespace umsx {
+
+struct Matrix {
+    uint8_t *codes = nullptr;   // code plane, all local experts
+    uint8_t *scales = nullptr;  // exponent / fp16-scale plane
+    int rows = 0;               // N per expert
+    int cols = 0;               // K
+    int quant = 0;
+    size_t code_bytes_per_expert() const { return (size_t)rows * (cols / 32) * (quant == UMSX_QUANT_MXFP4 ? 16 : 32); }
+    size_t scale_bytes_per_expert() const { return (size_t)rows * (cols / 32) * (quant == UMSX_QUANT_MXFP4 ? 1 : 2); }
+};
+
+// Routing/dispatch state that the router writes and the expert kernels read.
+struct Dispatch {
+    float *logits;       // [T][E]
+    int32_t *ids;        // [T][K]
+    float *weights;      // [T][K]
+    uint32_t *token_done;  // [T], zero between launches
+    uint32_t *all_done;    // [1], zero between launches
+    int32_t *counts;     // [E_local]
+    int32_t *offsets;    // [E_local + 1]
+    int32_t *active;     // [E_local] local expert index per active slot
+    int32_t *n_active;   // [1]
+    int32_t *job_token;  // [T*K] jobs grouped by expert, tokens ascending
+    int32_t *job_rank;   // [T*K]
+    uint8_t *xq_codes;   // [T][H/32][32] Q8_0 codes of x, lane-pair order
+    float *xq_scales;    // [T][H/32] fp16-rounded Q8_0 scales of x
+};
+
+struct RouterParams {
+    const void *x;
+    int x_dtype;
+    int tokens, hidden, experts, top_k, routing;
+    float routed_scale;
+    const float *w;   // [E][H]
+    const float *b;   // [E] or null
+    int e_lo, e_local;
+    int fuse_dispatch;  // the last finishing CTA builds the dispatch (small T*K)
+    int rmsnorm;        // normalise each input row (unit weight) before routing / quantizing
+    float eps;
+};
+
+struct GateUpParams {
+    Matrix gate_up;     // fused [2I][H] ...
+    Matrix gate, up;    // ... or separate [I][H]
+    int fused;
+    const float *bias;  // [E_local][2I] fp32 (gate then up) or null
+    int intermediate, hidden, activation;
+    float alpha, limit;
+    uint8_t *act_codes; // [T*K][I/32][32] Q8_0 codes of the activation, permuted job order, lane-pair order
+    float *act_scales;  // [T*K][I/32] fp16-rounded Q8_0 scales
+};
+
+struct GemvParams {
+    Matrix m;
+    const float *bias;      // [E_local][N] or null
+    const float *a_f32;     // activation rows to quantize, or null
+    const uint8_t *a_q8;    // ggml block_q8_0 rows, or null
+    int a_by_job;           // activation row = permuted job index
+    int a_ts, a_rs;         // else activation row = token*a_ts + rank*a_rs
+    float *out;             // output rows of N floats
+    int o_ts;               // output row = token*o_ts + rank
+};
+
+// Launchers (umsx_kernels.cu).  Each returns the number of kernels launched.
+int launch_router(const RouterParams &p, const Dispatch &d, cudaStream_t s);
+int launch_dispatch(const Dispatch &d, int entries, int top_k, int e_lo, int e_local, cudaStream_t s);
+int launch_gate_up(const GateUpParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
+int launch_gemv(const GemvParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
+int launch_gemv_internal(const GemvParams &p, const uint8_t *codes, const float *scales, const Dispatch &d,
+                         int max_slots, int max_per_expert, cudaStream_t s);
+int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *residual, float *out,
+                   cudaStream_t s);
+int launch_repack(const Matrix &m, int expert, const uint8_t *ggml, cudaStream_t s);
+int launch_export(const Matrix &m, int expert, uint8_t *ggml, cudaStream_t s);
+int launch_gen_blocks(int quant, uint64_t seed, uint64_t stream, uint64_t first_block, uint64_t nblocks,
+                      uint8_t *out, cudaStream_t s);
+int launch_gen_normal_f32(uint64_t seed, uint64_t stream, uint64_t first, uint64_t n, float scale, float *out,
+                          cudaStream_t s);
+int launch_gen_normal_bf16_to_f32(uint64_t seed, uint64_t stream, uint64_t first, uint64_t n, float scale,
+                                  float *out, cudaStream_t s);
+int launch_bf16_to_f32(const uint16_t *in, float *out, size_t n, cudaStream_t s);
+
+}  // namespace umsx
