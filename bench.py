@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--mode", choices=("decode", "prefill"), default="decode")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--experts", type=int, default=None,
+                    help="override the expert count (profiling runs that must hold only a few GB)")
     ap.add_argument("--impl", choices=("umsx", "reference"), default="umsx")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -91,7 +93,7 @@ class Clocks:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -116,7 +118,7 @@ class Clocks:
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
 
@@ -205,6 +207,9 @@ def gpu_arm(a):
     torch.cuda.set_device(dev)
     pkg = load_pkg()
     cfg = pkg.configs.GPT_OSS_120B
+    if a.experts:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, experts=a.experts)
     T = a.tokens
     layers = [pkg.MoeLayer(cfg.desc(max_tokens=1), synthetic=cfg.synthetic(layer=l), device=dev.index,
                            reserve_bytes=2 << 30) for l in range(a.layers)]
@@ -227,8 +232,7 @@ def gpu_arm(a):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # device-resident timed region
-    stack.set_timing(True)
+    # device-resident timed region (the stack replays one CUDA graph per step)
     for i in range(a.warmup):
         stack.forward(xs_dev[i % pool], out)
     torch.cuda.synchronize()
@@ -243,10 +247,21 @@ def gpu_arm(a):
         ev1.record(stream)
         torch.cuda.synchronize()
     launches = pkg.kernel_launches() - launches0
-    stages = stack.stage_times()  # the last replay, every layer, on the stack's launching stream
     barrier()
     torch.cuda.synchronize()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
+    # per-stage durations: the same steps again with CUDA events between the stages (the
+    # combine then runs as a kernel of its own so that every stage has a boundary)
+    stack.set_timing(True)
+    for i in range(a.warmup):
+        stack.forward(xs_dev[i % pool], out)
+    stage_sum = dict.fromkeys(stack.STAGES, 0.0)
+    for i in range(a.steps):
+        stack.forward(xs_dev[i % pool], out)
+        for k, v in stack.stage_times().items():
+            stage_sum[k] += v
+    stages = {k: v / a.steps for k, v in stage_sum.items()}
+    stack.set_timing(False)
     ms_step = ms / a.steps
     value = world * T * a.steps / (ms / 1e3)
     clocks = clk.summary()
@@ -292,7 +307,7 @@ def gpu_arm(a):
            "roofline": roof,
            "stack_roofline": {"bytes_per_step": stack_bytes, "achieved_gbs": stack_bytes / (ms_step / 1e3) / 1e9,
                               "frac": stack_bytes / (ms_step / 1e3) / 1e9 / peak},
-           "stages_ms_last_step": stages, "gpu_launches": launches, "clocks": clocks, "e2e": e2e}
+           "stages_ms_per_step": stages, "gpu_launches": launches, "clocks": clocks, "e2e": e2e}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
             res["cpu_baseline"] = {k: v for k, v in cpu_baseline(a, a.cpu_seconds).items() if k != "layer_ms"}

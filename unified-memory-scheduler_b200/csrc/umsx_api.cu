@@ -163,6 +163,8 @@ void carve_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_
     p.job_rank = a.take<int32_t>(T * K);
     p.xq_codes = a.take<uint8_t>(T * H);
     p.xq_scales = a.take<float>(T * (H / 32));
+    p.slots = a.take<int4>(EL);
+    p.tile_done = a.take<uint32_t>(T * (H / 32));
     w.act_codes = a.take<uint8_t>(T * K * I);
     w.act_scales = a.take<float>(T * K * (I / 32));
     w.y = a.take<float>(T * K * H);
@@ -195,6 +197,7 @@ umsx_status allocate(umsx_moe *m, size_t reserve) {
         return fail(UMSX_EOOM, "allocation of " + std::to_string(wbytes) + " weight bytes would violate the " +
                                    std::to_string(reserve) + "-byte free-memory reserve");
     UMSX_CUDA(cudaMalloc(&m->weights_mem, wbytes));
+    UMSX_CUDA(cudaMemset(m->weights_mem, 0, wbytes));  // defined padding bytes
     Arena w2{m->weights_mem, 0, wbytes};
     carve_weights(m, w2);
     return alloc_workspace(m->ws, m->d, m->e_local, m->d.max_tokens, reserve);
@@ -362,6 +365,7 @@ umsx_status check_call(umsx_moe *m, const void *x, int x_dtype, int tokens, int 
     if (!x) return fail(UMSX_EINVAL, "null input");
     if (x_dtype != UMSX_DTYPE_F32 && x_dtype != UMSX_DTYPE_BF16) return fail(UMSX_EINVAL, "x_dtype must be F32 or BF16");
     if (tokens <= 0 || tokens > max_tokens) return fail(UMSX_EINVAL, "tokens must be in [1, max_tokens]");
+    if (reinterpret_cast<uintptr_t>(x) % 16) return fail(UMSX_EINVAL, "x must be 16-byte aligned");
     return UMSX_OK;
 }
 
@@ -427,10 +431,22 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     p.a_by_job = 1;
     p.out = ws.y;
     p.o_ts = d.top_k;
+    if (!ev) {
+        // down + fused rank-order combine (+ residual); the down weights follow from the
+        // router's slot records, so their loads start before gate_up has finished
+        p.tile_done = ws.disp.tile_done;
+        p.route_w = ws.disp.weights;
+        p.residual = residual;
+        p.combine_out = out;
+        p.top_k = d.top_k;
+        p.prefetch_early = 1;
+    }
     UMSX_LAUNCHED(launch_gemv_internal(p, ws.act_codes, ws.act_scales, ws.disp, slots, tokens, s));
-    if (ev) if (umsx_status st = mark(ev[3], s)) return st;
-    UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, s));
-    if (ev) if (umsx_status st = mark(ev[4], s)) return st;
+    if (ev) {  // timed stages keep the combine a kernel of its own so that every stage has a boundary
+        if (umsx_status st = mark(ev[3], s)) return st;
+        UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, s));
+        if (umsx_status st = mark(ev[4], s)) return st;
+    }
     return UMSX_OK;
 }
 
@@ -503,6 +519,8 @@ umsx_status umsx_expert_down_q8(umsx_moe *m, const void *packed_q8, const int32_
     std::vector<int32_t> fill(offsets.begin(), offsets.end() - 1);
     for (int j = 0; j < jobs; ++j) token[fill[experts[j] - m->e_lo]++] = j;
     const int n_active = (int)active.size();
+    std::vector<int4> slot_rec(n_active);
+    for (int a = 0; a < n_active; ++a) slot_rec[a] = make_int4(active[a], offsets[active[a]], counts[active[a]], 0);
     std::lock_guard<std::mutex> lock(m->mu);
     UMSX_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -514,6 +532,7 @@ umsx_status umsx_expert_down_q8(umsx_moe *m, const void *packed_q8, const int32_
     UMSX_CUDA(cudaMemcpyAsync(d.n_active, &n_active, 4, cudaMemcpyHostToDevice, s));
     UMSX_CUDA(cudaMemcpyAsync(d.job_token, token.data(), token.size() * 4, cudaMemcpyHostToDevice, s));
     UMSX_CUDA(cudaMemcpyAsync(d.job_rank, rank.data(), rank.size() * 4, cudaMemcpyHostToDevice, s));
+    UMSX_CUDA(cudaMemcpyAsync(d.slots, slot_rec.data(), slot_rec.size() * sizeof(int4), cudaMemcpyHostToDevice, s));
     GemvParams p{};
     p.m = m->down;
     p.bias = m->down_bias;

@@ -1,19 +1,18 @@
 // Internal structures of libumsx (not part of the C ABI).
 //
 // Device layout of an expert matrix (N rows x K columns, nb = K/32 blocks):
-// rows are taken eight at a time ("row group", rg) and blocks in groups of
-// four (MXFP4) or two (Q8_0).  One (row group, block group) is a 512-byte chunk
-// that one warp reads with one 16-byte load per lane; lane = 4*w + p serves
-// row w of the group and the lane pair (p, p+4) of the reference's eight-lane
-// dot (elements 4p..4p+3 and 16+4p..16+4p+3 of each block):
-//   MXFP4 code plane: chunk[((w*4+p)*nblk + j)*4 .. +4] = one 32-bit word per block:
-//          low 16 bits = codes of elements 4p..4p+3 (4 bits each),
-//          high 16 bits = codes of elements 16+4p..16+4p+3
-//   MXFP4 exponent plane: 8 bytes per block per row group: [w*nblk + j]
-//   Q8_0 code plane: chunk[((w*4+p)*2 + j)*8 .. +8] = codes 4p..4p+3 then 16+4p..16+4p+3
-//   Q8_0 scale plane: fp16 bits, [w*2 + j] within a 32-byte chunk per block pair
-// The last MXFP4 group of a row holds 2 blocks when nb % 4 == 2 (nb is even).
-// Both planes keep the ggml byte count (17 or 34 bytes per 32 weights).
+//   MXFP4 code plane: rows in groups of 16, blocks in pairs; chunk (group, pair) is
+//     512 bytes, lane L = 16*h + r holds 16 bytes for row r and block 2*pair + h: four
+//     32-bit words, word p = codes of elements 4p..4p+3 (bits 0-15, 4 per element)
+//     and 16+4p..16+4p+3 (bits 16-31).  One warp-wide 16-byte load reads a chunk.
+//   MXFP4 exponent plane: chunk (group, pair quad) is 128 bytes, lane L holds the
+//     exponents of its (row, block) for four consecutive pairs (padded to a quad).
+//   Q8_0 code plane: rows in groups of 32; chunk (group, block) is 1 KB, lane r holds
+//     the 32 codes of row r in lane-pair order [p][4p..4p+3, 16+4p..16+4p+3].
+//   Q8_0 scale plane: chunk (group, block pair) is 128 bytes, lane r holds the two
+//     fp16 scales of row r.
+// The planes keep the ggml byte count (17 or 34 bytes per 32 weights), apart from
+// the MXFP4 exponent padding.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -30,7 +29,10 @@ struct Matrix {
     int cols = 0;               // K
     int quant = 0;
     size_t code_bytes_per_expert() const { return (size_t)rows * (cols / 32) * (quant == UMSX_QUANT_MXFP4 ? 16 : 32); }
-    size_t scale_bytes_per_expert() const { return (size_t)rows * (cols / 32) * (quant == UMSX_QUANT_MXFP4 ? 1 : 2); }
+    size_t scale_bytes_per_expert() const {
+        if (quant == UMSX_QUANT_MXFP4) return (size_t)(rows / 16) * (((cols / 64) + 3) / 4) * 128;
+        return (size_t)rows * (cols / 32) * 2;
+    }
 };
 
 // Routing/dispatch state that the router writes and the expert kernels read.
@@ -48,6 +50,8 @@ struct Dispatch {
     int32_t *job_rank;   // [T*K]
     uint8_t *xq_codes;   // [T][H/32][32] Q8_0 codes of x, lane-pair order
     float *xq_scales;    // [T][H/32] fp16-rounded Q8_0 scales of x
+    int4 *slots;         // [E_local] per active slot {local expert, segment start, count, -}; expert -1 past the last
+    uint32_t *tile_done; // [T][H/32] combine arrival counters, zero between launches
 };
 
 struct RouterParams {
@@ -83,6 +87,14 @@ struct GemvParams {
     int a_ts, a_rs;         // else activation row = token*a_ts + rank*a_rs
     float *out;             // output rows of N floats
     int o_ts;               // output row = token*o_ts + rank
+    // fused rank-order combine (layer path): the last of a token's top_k expert CTAs
+    // for a row tile writes combine_out[token] = residual + sum_r route_w[token][r] * out[token*top_k + r]
+    uint32_t *tile_done;    // [T][N / rows-per-CTA] arrival counters, zero between launches; null = no combine
+    const float *route_w;   // [T][top_k]
+    const float *residual;  // [T][N] or null
+    float *combine_out;     // [T][N]
+    int top_k;
+    int prefetch_early;     // the slot records were written two kernels back: prefetch weights before waiting
 };
 
 // Launchers (umsx_kernels.cu).  Each returns the number of kernels launched.

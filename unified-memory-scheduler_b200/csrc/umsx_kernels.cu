@@ -7,8 +7,9 @@
 // accumulates lane l of block b as fma(d_b, float(L), acc) in an even-block and
 // an odd-block chain, and sums lanes as ((l0+l4)+(l2+l6))+((l1+l5)+(l3+l7))
 // (tools/trace/compatible_down.cu:95-99, tools/trace/cpu_mxfp4_vnni.cpp:57-67).
-// Here one lane of a warp owns the lane pair (p, p+4) of one row, so the chain
-// order is the reference's and the final order is two xor shuffles.
+// Here a lane owns one row (Q8_0) or one of the two block chains of a row (MXFP4)
+// with all eight int lanes, so the chain order is the reference's and the final
+// order is computed in registers after one shuffle.
 #include <stdint.h>
 
 #include "umsx_device.cuh"
@@ -18,12 +19,20 @@ namespace umsx {
 
 // ============================================================================
 // Router: logits + softmax / top-k / weights + x -> Q8_0, and (small T*K) the
-// dispatch build, all in one launch.  grid = (ceil(E/8), T), block = 256.
+// dispatch build, all in one launch.  grid = (ceil(E/4), T), block = 128.
 // ============================================================================
 
-constexpr int kRouterWarps = 8;
+constexpr int kRouterWarps = 4;
 constexpr int kMaxExperts = 1024;
 constexpr int kFusedDispatchMax = 512;
+constexpr int kRouterRegs = 96;  // router-weight chain values a lane holds in registers (H <= 3072)
+
+// Programmatic dependent launch: the next kernel in the stream may start once
+// every CTA of this one has signalled; `pdl_wait` blocks until the previous
+// kernel has completed and its writes are visible.  Both are no-ops for
+// kernels launched without the PDL attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 __device__ __forceinline__ bool better(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
 
@@ -97,11 +106,13 @@ __device__ void select_token(const RouterParams &p, const Dispatch &d, int t, in
     }
 }
 
-// One CTA builds counts / offsets / active list / job lists for N = T*K entries.
+// One CTA builds counts / offsets / active list / slot records / job lists for
+// N = T*K entries.
 __device__ void build_dispatch_cta(const Dispatch &d, int entries, int K, int e_lo, int e_local) {
     __shared__ int cnt[kMaxExperts];
     __shared__ int off[kMaxExperts];
     __shared__ int ids_s[kFusedDispatchMax];
+    __shared__ int n_act_s;
     const int tid = threadIdx.x, nth = blockDim.x;
     for (int e = tid; e < e_local; e += nth) cnt[e] = 0;
     for (int j = tid; j < entries; j += nth) ids_s[j] = __ldcg(d.ids + j) - e_lo;
@@ -128,12 +139,17 @@ __device__ void build_dispatch_cta(const Dispatch &d, int entries, int K, int e_
             off[e] = base;
             d.offsets[e] = base;
             d.counts[e] = cnt[e];
-            if (cnt[e] > 0) d.active[abase++] = e;
+            if (cnt[e] > 0) {
+                d.active[abase] = e;
+                d.slots[abase] = make_int4(e, base, cnt[e], 0);
+                ++abase;
+            }
             base += cnt[e];
         }
-        if (tid == 31) { d.offsets[e_local] = ps; d.n_active[0] = pa; }
+        if (tid == 31) { d.offsets[e_local] = ps; d.n_active[0] = pa; n_act_s = pa; }
     }
     __syncthreads();
+    for (int sl = n_act_s + tid; sl < e_local; sl += nth) d.slots[sl] = make_int4(-1, 0, 0, 0);
     for (int j = tid; j < entries; j += nth) {
         const int e = ids_s[j];
         if (e < 0 || e >= e_local) continue;
@@ -145,21 +161,44 @@ __device__ void build_dispatch_cta(const Dispatch &d, int entries, int K, int e_
     }
 }
 
-__global__ void __launch_bounds__(256) k_router(RouterParams p, Dispatch d) {
+// grid = (ceil(E/4), T), block = 128: one warp per expert logit.
+template <bool REGS>
+__global__ void __launch_bounds__(128) k_router(RouterParams p, Dispatch d) {
     extern __shared__ float xs[];
+    __shared__ float inv_s;
+    __shared__ int last;
     const int t = blockIdx.y, H = p.hidden;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * kRouterWarps + warp;
+    const bool has_e = e < p.experts;
+    float wv[REGS ? kRouterRegs : 1];
+    if constexpr (REGS) {
+        // The router weights do not depend on the previous kernel: fetch this lane's
+        // chain (k = lane, lane+32, ...) before waiting on it.
+        const float *wr = p.w + (size_t)(has_e ? e : 0) * H;
+#pragma unroll
+        for (int i = 0; i < kRouterRegs; ++i) wv[i] = (lane + 32 * i < H) ? __ldg(wr + lane + 32 * i) : 0.0f;
+    }
+    pdl_wait();
+    pdl_launch_dependents();
     if (p.x_dtype == UMSX_DTYPE_BF16) {
-        const uint16_t *xb = static_cast<const uint16_t *>(p.x) + (size_t)t * H;
-        for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = bf16_bits_to_f32(xb[i]);
+        const uint2 *xb = reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p.x) + (size_t)t * H);
+#pragma unroll 8
+        for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+            const uint2 v = xb[i];
+            xs[4 * i + 0] = bf16_bits_to_f32(v.x & 0xffffu);
+            xs[4 * i + 1] = bf16_bits_to_f32(v.x >> 16);
+            xs[4 * i + 2] = bf16_bits_to_f32(v.y & 0xffffu);
+            xs[4 * i + 3] = bf16_bits_to_f32(v.y >> 16);
+        }
     } else {
-        const float *xf = static_cast<const float *>(p.x) + (size_t)t * H;
-        for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = xf[i];
+        const float4 *xf = reinterpret_cast<const float4 *>(static_cast<const float *>(p.x) + (size_t)t * H);
+#pragma unroll 8
+        for (int i = threadIdx.x; i < H / 4; i += blockDim.x) reinterpret_cast<float4 *>(xs)[i] = xf[i];
     }
     __syncthreads();
     if (p.rmsnorm) {
         // RMSNorm with unit weight: sum of squares in the shared strided order (orc_rmsnorm)
-        __shared__ float inv_s;
         if (warp == 0) {
             float acc = 0.0f;
             for (int k = lane; k < H; k += 32) acc = __fmaf_rn(xs[k], xs[k], acc);
@@ -181,17 +220,29 @@ __global__ void __launch_bounds__(256) k_router(RouterParams p, Dispatch d) {
         if (lane == 0) d.xq_scales[(size_t)t * nbH + b] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
     }
     // logits: 32 strided FMA chains, then the xor tree (orc_logit)
-    const int e = blockIdx.x * kRouterWarps + warp;
-    if (e < p.experts) {
-        const float *wr = p.w + (size_t)e * H;
+    if (has_e) {
         float acc = 0.0f;
-        for (int k = lane; k < H; k += 32) acc = __fmaf_rn(__ldg(wr + k), xs[k], acc);
+        if constexpr (REGS) {
+#pragma unroll
+            for (int i = 0; i < kRouterRegs; ++i)
+                if (lane + 32 * i < H) acc = __fmaf_rn(wv[i], xs[lane + 32 * i], acc);
+        } else {
+            const float *wr = p.w + (size_t)e * H;
+            constexpr int kRB = 16;
+            for (int k0 = lane; k0 < H; k0 += 32 * kRB) {
+                float w[kRB];
+#pragma unroll
+                for (int i = 0; i < kRB; ++i) w[i] = (k0 + 32 * i < H) ? __ldg(wr + k0 + 32 * i) : 0.0f;
+#pragma unroll
+                for (int i = 0; i < kRB; ++i)
+                    if (k0 + 32 * i < H) acc = __fmaf_rn(w[i], xs[k0 + 32 * i], acc);
+            }
+        }
         float l = warp_tree_sum(acc);
         if (p.b) l = __fadd_rn(l, __ldg(p.b + e));
         if (lane == 0) d.logits[(size_t)t * p.experts + e] = l;
     }
     // the last CTA of this token selects; the last token to finish builds the dispatch
-    __shared__ int last;
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) last = atomicAdd(d.token_done + t, 1u) == gridDim.x - 1;
@@ -201,14 +252,18 @@ __global__ void __launch_bounds__(256) k_router(RouterParams p, Dispatch d) {
     if (warp == 0) select_token(p, d, t, lane);
     if (threadIdx.x == 0) d.token_done[t] = 0;
     if (!p.fuse_dispatch) return;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(d.all_done, 1u) == gridDim.y - 1;
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
+    if (gridDim.y > 1) {
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last = atomicAdd(d.all_done, 1u) == gridDim.y - 1;
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+        if (threadIdx.x == 0) d.all_done[0] = 0;
+    } else {
+        __syncthreads();  // one token: this CTA selected it
+    }
     build_dispatch_cta(d, p.tokens * p.top_k, p.top_k, p.e_lo, p.e_local);
-    if (threadIdx.x == 0) d.all_done[0] = 0;
 }
 
 // Large T*K: one CTA per local expert.  Each CTA histograms every entry, scans,
@@ -219,30 +274,40 @@ __global__ void __launch_bounds__(256) k_dispatch(Dispatch d, int entries, int K
     __shared__ int base_s, off_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int me = blockIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
     for (int e = tid; e < e_local; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int j = tid; j < entries; j += blockDim.x) {
-        const int e = __ldg(d.ids + j) - e_lo;
+        const int e = __ldcg(d.ids + j) - e_lo;
         if (e >= 0 && e < e_local) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
     if (tid == 0) {
-        int s = 0, a = 0;
-        for (int e = 0; e < me; ++e) { s += cnt[e]; a += cnt[e] > 0; }
+        int s = 0, a = 0, z = 0, total = 0;
+        for (int e = 0; e < e_local; ++e) {
+            if (e < me) { s += cnt[e]; a += cnt[e] > 0; z += cnt[e] == 0; }
+            total += cnt[e] > 0;
+        }
         off_s = s;
         d.offsets[me] = s;
         d.counts[me] = cnt[me];
-        if (cnt[me] > 0) d.active[a] = me;
+        if (cnt[me] > 0) {
+            d.active[a] = me;
+            d.slots[a] = make_int4(me, s, cnt[me], 0);
+        } else {
+            d.slots[total + z] = make_int4(-1, 0, 0, 0);
+        }
         if (me == e_local - 1) {
             d.offsets[e_local] = s + cnt[me];
-            d.n_active[0] = a + (cnt[me] > 0);
+            d.n_active[0] = total;
         }
         base_s = 0;
     }
     __syncthreads();
     for (int j0 = 0; j0 < entries; j0 += blockDim.x) {
         const int j = j0 + tid;
-        const bool mine = j < entries && __ldg(d.ids + j) - e_lo == me;
+        const bool mine = j < entries && __ldcg(d.ids + j) - e_lo == me;
         const unsigned bal = __ballot_sync(kFull, mine);
         if (lane == 0) warp_tot[warp] = __popc(bal);
         __syncthreads();
@@ -264,200 +329,301 @@ __global__ void __launch_bounds__(256) k_dispatch(Dispatch d, int entries, int K
 }
 
 // ============================================================================
-// Exact quantized GEMV cores.  One warp = one row group (8 rows x 4 lanes).
-// Activations for up to MT jobs sit in shared memory as 32-byte lane-pair
-// blocks (lane p reads 8 bytes: elements 4p..4p+3 and 16+4p..16+4p+3) plus one
-// fp32 scale per block (the fp16 value, exactly widened).
+// Exact quantized GEMV cores.
+//
+// MXFP4: a warp covers 16 rows; lane L owns row L&15 and the even (L<16) or odd
+// (L>=16) block chain of that row, i.e. one of the reference's two FMA chains,
+// holding all eight int-lane accumulators of it.  Each block it reads 16 bytes
+// (32 codes) and forms the eight 4-product lane sums with prmt (magnitudes of
+// positive and of negative codes) and dp4a against staged activations and their
+// byte negations (VPSIGNB semantics).  The two chains meet in one xor-16 shuffle.
+// Q8_0: a warp covers 32 rows, one lane per row and one chain (the reference's
+// Q8_0 dot has no even/odd split); signed dp4a, with the exact VPSIGNB path only
+// for activation blocks that hold a -128 code.
+// The int lane sum becomes a float exactly by starting dp4a at 0x4B400000
+// (1.5*2^23) and subtracting 1.5*2^23: |sum| < 2^22 keeps it in one binade.
 // ============================================================================
 
+constexpr uint32_t kMagicI = 0x4B400000u;
+constexpr float kMagicF = 12582912.0f;
+__device__ __forceinline__ float lane_sum(int biased) { return __fsub_rn(__int_as_float(biased), kMagicF); }
+
+template <int QUANT>
+struct Geo;
+template <>
+struct Geo<UMSX_QUANT_MXFP4> {
+    static constexpr int kRowsPerWarp = 16;
+    static constexpr int kChains = 2;
+    static constexpr int kBatch = 8;  // block pairs per load batch
+};
+template <>
+struct Geo<UMSX_QUANT_Q8_0> {
+    static constexpr int kRowsPerWarp = 32;
+    static constexpr int kChains = 1;
+    static constexpr int kBatch = 4;  // blocks per load batch
+};
+
+// Staged activations of up to MT jobs: per (job, block) 4 x uint4 =
+// {a(4p..4p+3), a(16+4p..), -a(4p..), -a(16+4p..)} for p = 0..3, one fp32 scale
+// (the fp16 value widened) and, for Q8_0 weights, a "holds -128" flag.
+struct Staged {
+    const uint4 *q;
+    const float *sc;
+    const int *flag;
+};
+
 template <int MT>
-__device__ __forceinline__ void mx_block(uint32_t word, uint32_t e8, int b, int parity, const uint8_t *act_s,
-                                         const float *sc_s, int nb, int m, int p, float (&acc)[MT][4]) {
-    const uint32_t nword = word ^ 0x88888888u;
-    const uint32_t posL = prmt(kMagLo, kMagHi, word), negL = prmt(kMagLo, kMagHi, nword);
-    const uint32_t posH = prmt(kMagLo, kMagHi, word >> 16), negH = prmt(kMagLo, kMagHi, nword >> 16);
+__device__ __forceinline__ void mx_block(uint4 wq, uint32_t e8, int b, const Staged &a, int nb, int m,
+                                         float (&acc)[MT][8]) {
+    const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
+    uint32_t pl[4], nl[4], ph[4], nh[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t nw = wv[p] ^ 0x88888888u;
+        pl[p] = prmt(kMagLo, kMagHi, wv[p]);
+        nl[p] = prmt(kMagLo, kMagHi, nw);
+        ph[p] = prmt(kMagLo, kMagHi, wv[p] >> 16);
+        nh[p] = prmt(kMagLo, kMagHi, nw >> 16);
+    }
     const float eh = e8m0_half(e8);
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
         if (t < m) {
-            const uint2 av = *reinterpret_cast<const uint2 *>(act_s + ((size_t)t * nb + b) * 32 + p * 8);
-            const float d = __fmul_rn(sc_s[t * nb + b], eh);
-            const int lo = dp4a_ss(negL, neg8x4(av.x), dp4a_ss(posL, av.x, 0));
-            const int hi = dp4a_ss(negH, neg8x4(av.y), dp4a_ss(posH, av.y, 0));
-            acc[t][parity * 2 + 0] = __fmaf_rn(d, (float)lo, acc[t][parity * 2 + 0]);
-            acc[t][parity * 2 + 1] = __fmaf_rn(d, (float)hi, acc[t][parity * 2 + 1]);
+            const uint4 *aq = a.q + ((size_t)t * nb + b) * 4;
+            const float d = __fmul_rn(a.sc[t * nb + b], eh);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const uint4 av = aq[p];
+                const int lo = dp4a_ss(nl[p], av.z, dp4a_ss(pl[p], av.x, (int)kMagicI));
+                const int hi = dp4a_ss(nh[p], av.w, dp4a_ss(ph[p], av.y, (int)kMagicI));
+                acc[t][p] = __fmaf_rn(d, lane_sum(lo), acc[t][p]);
+                acc[t][p + 4] = __fmaf_rn(d, lane_sum(hi), acc[t][p + 4]);
+            }
         }
     }
 }
 
 template <int MT>
-__device__ __forceinline__ void q8_block(uint2 wq, uint32_t wsc, int b, const uint8_t *act_s, const float *sc_s,
-                                         int nb, int m, int p, float (&acc)[MT][4]) {
-    const uint32_t mL = __vcmplts4(wq.x, 0u), mH = __vcmplts4(wq.y, 0u);
-    const uint32_t posL = wq.x & ~mL, negL = neg8x4(wq.x) & mL;
-    const uint32_t posH = wq.y & ~mH, negH = neg8x4(wq.y) & mH;
-    const float wd = f16_bits_to_f32(wsc);
+__device__ __forceinline__ void q8_block(uint4 w01, uint4 w23, uint32_t ws16, int b, const Staged &a, int nb, int m,
+                                         float (&acc)[MT][8]) {
+    const uint32_t lo[4] = {w01.x, w01.z, w23.x, w23.z}, hi[4] = {w01.y, w01.w, w23.y, w23.w};
+    const float wd = f16_bits_to_f32(ws16);
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
         if (t < m) {
-            const uint2 av = *reinterpret_cast<const uint2 *>(act_s + ((size_t)t * nb + b) * 32 + p * 8);
-            const float d = __fmul_rn(wd, sc_s[t * nb + b]);
-            const int lo = dp4a_us(negL, neg8x4(av.x), dp4a_us(posL, av.x, 0));
-            const int hi = dp4a_us(negH, neg8x4(av.y), dp4a_us(posH, av.y, 0));
-            acc[t][0] = __fmaf_rn(d, (float)lo, acc[t][0]);
-            acc[t][1] = __fmaf_rn(d, (float)hi, acc[t][1]);
-        }
-    }
-}
-
-// Dot products of one row group against the staged activations.
-template <int QUANT, int MT>
-__device__ __forceinline__ void rowgroup_dot(const uint8_t *__restrict__ codes, const uint8_t *__restrict__ scales,
-                                             int nb, const uint8_t *act_s, const float *sc_s, int m, int lane,
-                                             float (&acc)[MT][4]) {
-    const int w = lane >> 2, p = lane & 3;
+            const uint4 *aq = a.q + ((size_t)t * nb + b) * 4;
+            const float d = __fmul_rn(wd, a.sc[t * nb + b]);
+            if (!a.flag[t * nb + b]) {
 #pragma unroll
-    for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-    if constexpr (QUANT == UMSX_QUANT_MXFP4) {
-        const int ng = nb >> 2;
-        int g = 0;
-        for (; g + 2 <= ng; g += 2) {
-            const uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(codes + (size_t)g * 512) + lane);
-            const uint4 w1 = __ldg(reinterpret_cast<const uint4 *>(codes + (size_t)(g + 1) * 512) + lane);
-            const uint32_t e0 = __ldg(reinterpret_cast<const uint32_t *>(scales + (size_t)g * 32) + w);
-            const uint32_t e1 = __ldg(reinterpret_cast<const uint32_t *>(scales + (size_t)(g + 1) * 32) + w);
-            mx_block<MT>(w0.x, e0 & 0xffu, 4 * g + 0, 0, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w0.y, (e0 >> 8) & 0xffu, 4 * g + 1, 1, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w0.z, (e0 >> 16) & 0xffu, 4 * g + 2, 0, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w0.w, e0 >> 24, 4 * g + 3, 1, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w1.x, e1 & 0xffu, 4 * g + 4, 0, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w1.y, (e1 >> 8) & 0xffu, 4 * g + 5, 1, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w1.z, (e1 >> 16) & 0xffu, 4 * g + 6, 0, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w1.w, e1 >> 24, 4 * g + 7, 1, act_s, sc_s, nb, m, p, acc);
-        }
-        if (g < ng) {
-            const uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(codes + (size_t)g * 512) + lane);
-            const uint32_t e0 = __ldg(reinterpret_cast<const uint32_t *>(scales + (size_t)g * 32) + w);
-            mx_block<MT>(w0.x, e0 & 0xffu, 4 * g + 0, 0, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w0.y, (e0 >> 8) & 0xffu, 4 * g + 1, 1, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w0.z, (e0 >> 16) & 0xffu, 4 * g + 2, 0, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w0.w, e0 >> 24, 4 * g + 3, 1, act_s, sc_s, nb, m, p, acc);
-            ++g;
-        }
-        if (nb & 2) {  // tail group of two blocks: 8 bytes per lane, 2 exponent bytes per row
-            const uint2 w0 = __ldg(reinterpret_cast<const uint2 *>(codes + (size_t)ng * 512) + lane);
-            const uint32_t e0 = __ldg(reinterpret_cast<const uint16_t *>(scales + (size_t)ng * 32) + w);
-            mx_block<MT>(w0.x, e0 & 0xffu, 4 * ng + 0, 0, act_s, sc_s, nb, m, p, acc);
-            mx_block<MT>(w0.y, e0 >> 8, 4 * ng + 1, 1, act_s, sc_s, nb, m, p, acc);
-        }
-    } else {
-        const int ng = nb >> 1;
-        int g = 0;
-        for (; g + 2 <= ng; g += 2) {
-            const uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(codes + (size_t)g * 512) + lane);
-            const uint4 w1 = __ldg(reinterpret_cast<const uint4 *>(codes + (size_t)(g + 1) * 512) + lane);
-            const uint32_t s0 = __ldg(reinterpret_cast<const uint32_t *>(scales + (size_t)g * 32) + w);
-            const uint32_t s1 = __ldg(reinterpret_cast<const uint32_t *>(scales + (size_t)(g + 1) * 32) + w);
-            q8_block<MT>(make_uint2(w0.x, w0.y), s0 & 0xffffu, 2 * g + 0, act_s, sc_s, nb, m, p, acc);
-            q8_block<MT>(make_uint2(w0.z, w0.w), s0 >> 16, 2 * g + 1, act_s, sc_s, nb, m, p, acc);
-            q8_block<MT>(make_uint2(w1.x, w1.y), s1 & 0xffffu, 2 * g + 2, act_s, sc_s, nb, m, p, acc);
-            q8_block<MT>(make_uint2(w1.z, w1.w), s1 >> 16, 2 * g + 3, act_s, sc_s, nb, m, p, acc);
-        }
-        if (g < ng) {
-            const uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(codes + (size_t)g * 512) + lane);
-            const uint32_t s0 = __ldg(reinterpret_cast<const uint32_t *>(scales + (size_t)g * 32) + w);
-            q8_block<MT>(make_uint2(w0.x, w0.y), s0 & 0xffffu, 2 * g + 0, act_s, sc_s, nb, m, p, acc);
-            q8_block<MT>(make_uint2(w0.z, w0.w), s0 >> 16, 2 * g + 1, act_s, sc_s, nb, m, p, acc);
+                for (int p = 0; p < 4; ++p) {
+                    const uint4 av = aq[p];
+                    acc[t][p] = __fmaf_rn(d, lane_sum(dp4a_ss(lo[p], av.x, (int)kMagicI)), acc[t][p]);
+                    acc[t][p + 4] = __fmaf_rn(d, lane_sum(dp4a_ss(hi[p], av.y, (int)kMagicI)), acc[t][p + 4]);
+                }
+            } else {  // |w| * (w<0 ? -a : a) with -(-128) = -128, as VPSIGNB computes it
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const uint4 av = aq[p];
+                    const uint32_t ml = __vcmplts4(lo[p], 0u), mh = __vcmplts4(hi[p], 0u);
+                    const int sl = dp4a_us(neg8x4(lo[p]) & ml, av.z, dp4a_us(lo[p] & ~ml, av.x, (int)kMagicI));
+                    const int sh = dp4a_us(neg8x4(hi[p]) & mh, av.w, dp4a_us(hi[p] & ~mh, av.y, (int)kMagicI));
+                    acc[t][p] = __fmaf_rn(d, lane_sum(sl), acc[t][p]);
+                    acc[t][p + 4] = __fmaf_rn(d, lane_sum(sh), acc[t][p + 4]);
+                }
+            }
         }
     }
 }
 
-// Final lane order of the reference: per lane pair t = l(p+4) + l(p); then
-// (t0+t2) and (t1+t3) by xor 2; then their sum by xor 1.  All four lanes of a
-// row end with the same bits.
+// One warp's weight stream: batches of Geo::kBatch steps (a step is a block pair
+// for MXFP4, 16 bytes per lane; a block for Q8_0, 32 bytes per lane), each batch
+// loaded with every load in flight at once.
 template <int QUANT>
-__device__ __forceinline__ float finish_row(const float (&a)[4]) {
-    float lp, lp4;
-    if constexpr (QUANT == UMSX_QUANT_MXFP4) {
-        lp = __fadd_rn(a[0], a[2]);   // even + odd, lane p
-        lp4 = __fadd_rn(a[1], a[3]);  // even + odd, lane p+4
-    } else {
-        lp = a[0];
-        lp4 = a[1];
+struct WBatch {
+    static constexpr int B = Geo<QUANT>::kBatch;
+    uint4 w[B][QUANT == UMSX_QUANT_MXFP4 ? 1 : 2];
+    uint32_t s[QUANT == UMSX_QUANT_MXFP4 ? B / 4 : B / 2];
+};
+
+template <int QUANT>
+struct WStream {
+    static constexpr int B = Geo<QUANT>::kBatch;
+    const uint4 *cp;
+    const uint32_t *sp;
+    int steps;
+    __device__ __forceinline__ void init(const uint8_t *codes, const uint8_t *scales, int nb, int lane) {
+        cp = reinterpret_cast<const uint4 *>(codes) + (QUANT == UMSX_QUANT_MXFP4 ? lane : 2 * lane);
+        sp = reinterpret_cast<const uint32_t *>(scales) + lane;
+        steps = QUANT == UMSX_QUANT_MXFP4 ? nb / 2 : nb;
     }
-    float t = __fadd_rn(lp4, lp);
-    t = __fadd_rn(t, __shfl_xor_sync(kFull, t, 2));
-    return __fadd_rn(t, __shfl_xor_sync(kFull, t, 1));
+    __device__ __forceinline__ void load(int s0, WBatch<QUANT> &b) const {
+        if constexpr (QUANT == UMSX_QUANT_MXFP4) {
+#pragma unroll
+            for (int i = 0; i < B; ++i)
+                if (s0 + i < steps) b.w[i][0] = __ldg(cp + (size_t)(s0 + i) * 32);
+#pragma unroll
+            for (int i = 0; i < B / 4; ++i)
+                if (s0 + 4 * i < steps) b.s[i] = __ldg(sp + (size_t)((s0 >> 2) + i) * 32);
+        } else {
+#pragma unroll
+            for (int i = 0; i < B; ++i)
+                if (s0 + i < steps) {
+                    b.w[i][0] = __ldg(cp + (size_t)(s0 + i) * 64);
+                    b.w[i][1] = __ldg(cp + (size_t)(s0 + i) * 64 + 1);
+                }
+#pragma unroll
+            for (int i = 0; i < B / 2; ++i)
+                if (s0 + 2 * i < steps) b.s[i] = __ldg(sp + (size_t)((s0 >> 1) + i) * 32);
+        }
+    }
+};
+
+// Dot products of one warp's rows against the staged activations.  `cur` holds
+// batch 0 already in flight; the next batch is loaded before the current one is
+// consumed.  Blocks are consumed strictly in order, as the FMA chains require.
+template <int QUANT, int MT>
+__device__ __forceinline__ void warp_dot(const WStream<QUANT> &ws, WBatch<QUANT> cur, int nb, const Staged &a, int m,
+                                         int lane, float (&acc)[MT][8]) {
+    constexpr int B = Geo<QUANT>::kBatch;
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int l = 0; l < 8; ++l) acc[t][l] = 0.0f;
+    const int half = lane >> 4;
+    for (int s0 = 0; s0 < ws.steps; s0 += B) {
+        WBatch<QUANT> nxt;
+        if (s0 + B < ws.steps) ws.load(s0 + B, nxt);
+#pragma unroll
+        for (int i = 0; i < B; ++i) {
+            if (s0 + i < ws.steps) {
+                if constexpr (QUANT == UMSX_QUANT_MXFP4)
+                    mx_block<MT>(cur.w[i][0], (cur.s[i >> 2] >> (8 * (i & 3))) & 0xffu, 2 * (s0 + i) + half, a, nb, m, acc);
+                else
+                    q8_block<MT>(cur.w[i][0], cur.w[i][1], (cur.s[i >> 1] >> (16 * (i & 1))) & 0xffffu, s0 + i, a, nb, m, acc);
+            }
+        }
+        cur = nxt;
+    }
 }
 
-__device__ __forceinline__ size_t plane_code_stride(int quant, int nb) { return (size_t)nb * (quant == UMSX_QUANT_MXFP4 ? 128 : 256); }
-__device__ __forceinline__ size_t plane_scale_stride(int quant, int nb) { return (size_t)nb * (quant == UMSX_QUANT_MXFP4 ? 8 : 16); }
-
-// Copy the internal-layout Q8 rows of the given jobs into shared memory.
-__device__ __forceinline__ void stage_q8_internal(const uint8_t *codes, const float *scales, const int *rows_s, int m,
-                                                  int nb, uint8_t *act_s, float *sc_s) {
-    const int per = nb * 2;  // uint4 per row
-    for (int i = threadIdx.x; i < m * per; i += blockDim.x) {
-        const int t = i / per, c = i - t * per;
-        reinterpret_cast<uint4 *>(act_s)[(size_t)t * per + c] =
-            __ldcg(reinterpret_cast<const uint4 *>(codes + (size_t)rows_s[t] * nb * 32) + c);
+// The reference's final order: lanes = even + odd (MXFP4), t_i = l(i+4) + l(i),
+// result = (t0 + t2) + (t1 + t3).  For MXFP4 both lanes of a row end equal.
+template <int QUANT>
+__device__ __forceinline__ float finish_row(const float (&a)[8]) {
+    float l[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if constexpr (QUANT == UMSX_QUANT_MXFP4) l[i] = __fadd_rn(a[i], __shfl_xor_sync(kFull, a[i], 16));
+        else l[i] = a[i];
     }
+    const float t0 = __fadd_rn(l[4], l[0]), t1 = __fadd_rn(l[5], l[1]);
+    const float t2 = __fadd_rn(l[6], l[2]), t3 = __fadd_rn(l[7], l[3]);
+    return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+}
+
+// Byte offsets of the planes of row group `rg` of local expert `e`.
+__device__ __forceinline__ size_t code_offset(int quant, int e, int nrg, int rg, int nb) {
+    return ((size_t)e * nrg + rg) * (size_t)nb * (quant == UMSX_QUANT_MXFP4 ? 256 : 1024);
+}
+__device__ __forceinline__ size_t scale_offset(int quant, int e, int nrg, int rg, int nb) {
+    const int chunks = quant == UMSX_QUANT_MXFP4 ? ((nb / 2) + 3) / 4 : nb / 2;
+    return ((size_t)e * nrg + rg) * (size_t)chunks * 128;
+}
+
+// Shared-memory bytes for MT staged jobs of nb blocks.
+__host__ __device__ constexpr size_t staged_bytes(int mt, int nb) { return (size_t)mt * nb * (64 + 4 + 4); }
+
+__device__ __forceinline__ Staged staged_view(uint8_t *smem, int mt, int nb) {
+    Staged s;
+    s.q = reinterpret_cast<const uint4 *>(smem);
+    s.sc = reinterpret_cast<const float *>(smem + (size_t)mt * nb * 64);
+    s.flag = reinterpret_cast<const int *>(smem + (size_t)mt * nb * 68);
+    return s;
+}
+
+// Stage internal-layout Q8 rows (lane-pair order codes + fp32 scales) of the given jobs.
+__device__ __forceinline__ void stage_internal(const uint8_t *codes, const float *scales, const int *rows_s, int m,
+                                               int nb, uint8_t *smem, int mt, bool flags) {
+    uint4 *q = reinterpret_cast<uint4 *>(smem);
+    float *sc = reinterpret_cast<float *>(smem + (size_t)mt * nb * 64);
+    int *fl = reinterpret_cast<int *>(smem + (size_t)mt * nb * 68);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < m * nb * 4; i += blockDim.x) {
+        const int t = i / (nb * 4), r = i - t * nb * 4, b = r >> 2, p = r & 3;
+        const uint2 v = __ldcg(reinterpret_cast<const uint2 *>(codes + ((size_t)rows_s[t] * nb + b) * 32 + p * 8));
+        q[((size_t)t * nb + b) * 4 + p] = make_uint4(v.x, v.y, neg8x4(v.x), neg8x4(v.y));
+    }
+#pragma unroll 2
     for (int i = threadIdx.x; i < m * nb; i += blockDim.x) {
         const int t = i / nb, b = i - t * nb;
-        sc_s[i] = __ldcg(scales + (size_t)rows_s[t] * nb + b);
+        sc[i] = __ldcg(scales + (size_t)rows_s[t] * nb + b);
+        if (flags) {
+            const uint4 *c = reinterpret_cast<const uint4 *>(codes + ((size_t)rows_s[t] * nb + b) * 32);
+            const uint4 c0 = __ldcg(c), c1 = __ldcg(c + 1);
+            const uint32_t any = __vcmpeq4(c0.x, 0x80808080u) | __vcmpeq4(c0.y, 0x80808080u) |
+                                 __vcmpeq4(c0.z, 0x80808080u) | __vcmpeq4(c0.w, 0x80808080u) |
+                                 __vcmpeq4(c1.x, 0x80808080u) | __vcmpeq4(c1.y, 0x80808080u) |
+                                 __vcmpeq4(c1.z, 0x80808080u) | __vcmpeq4(c1.w, 0x80808080u);
+            fl[i] = any != 0;
+        }
     }
 }
 
 // ============================================================================
 // gate_up (+bias, +activation, +Q8_0 of the activation): a CTA computes 32
-// intermediate values (4 gate row groups + 4 up row groups = 8 warps) for every
-// job of one expert, then quantizes that 32-value block.  grid = (I/32, slots).
+// intermediate values (their gate rows and up rows) for every job of one
+// expert, then quantizes that 32-value block.  grid = (I/32, slots).
 // ============================================================================
 
 template <int QUANT, int MT>
-__global__ void __launch_bounds__(256) k_gate_up(GateUpParams p, Dispatch d) {
+__global__ void __launch_bounds__(64 * Geo<QUANT>::kChains) k_gate_up(GateUpParams p, Dispatch d) {
+    constexpr int RPW = Geo<QUANT>::kRowsPerWarp, GW = 32 / RPW;  // warps per half (gate or up)
     extern __shared__ __align__(16) uint8_t smem[];
-    const int slot = blockIdx.y;
-    if (slot >= __ldg(d.n_active)) return;
-    const int e = __ldg(d.active + slot);
-    const int seg = __ldg(d.offsets + e), cnt = __ldg(d.counts + e);
+    __shared__ float res[MT][2][32];
+    __shared__ int rows_s[MT];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int4 rec = __ldcg(d.slots + blockIdx.y);
+    const int e = rec.x;
+    if (e < 0) return;
+    const int seg = rec.y, cnt = rec.z;
     const int H = p.hidden, I = p.intermediate, nb = H / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t *act_s = smem;
-    float *sc_s = reinterpret_cast<float *>(smem + (size_t)MT * nb * 32);
-    float *res = sc_s + MT * nb;              // [MT][2][32]
-    int *rows_s = reinterpret_cast<int *>(res + MT * 64);
-    const int half = warp >> 2, rgi = warp & 3;
-    const int rg_half = blockIdx.x * 4 + rgi;  // row group within gate (or up) rows
+    const int half = warp / GW, wi = warp % GW;
     const Matrix &mat = p.fused ? p.gate_up : (half ? p.up : p.gate);
-    const int rg = p.fused ? (half * (I / 8) + rg_half) : rg_half;
-    const int nrg = mat.rows / 8;
-    const uint8_t *codes = mat.codes + ((size_t)e * nrg + rg) * plane_code_stride(QUANT, nb);
-    const uint8_t *scales = mat.scales + ((size_t)e * nrg + rg) * plane_scale_stride(QUANT, nb);
-    const int row = rg_half * 8 + (lane >> 2);  // intermediate index of this lane's row
-    float bias = 0.0f;
-    if (p.bias) bias = __ldg(p.bias + (size_t)e * 2 * I + half * I + row);
+    const int nrg = mat.rows / RPW;
+    const int rg_half = blockIdx.x * GW + wi;  // row group within the gate (or up) rows
+    const int rg = p.fused ? half * (I / RPW) + rg_half : rg_half;
+    WStream<QUANT> ws;
+    ws.init(mat.codes + code_offset(QUANT, e, nrg, rg, nb), mat.scales + scale_offset(QUANT, e, nrg, rg, nb), nb, lane);
+    WBatch<QUANT> first;
+    ws.load(0, first);  // weights stream while the activations are staged
+    const int rrow = lane % RPW;            // row within this warp
+    const int row = rg_half * RPW + rrow;   // intermediate index
+    const float bias = p.bias ? __ldg(p.bias + (size_t)e * 2 * I + half * I + row) : 0.0f;
+    const Staged st = staged_view(smem, MT, nb);
     const int nbI = I / 32;
     for (int c0 = 0; c0 < cnt; c0 += MT) {
         const int m = min(MT, cnt - c0);
+        if (c0 > 0) ws.load(0, first);
         __syncthreads();
-        if (threadIdx.x < m) rows_s[threadIdx.x] = __ldg(d.job_token + seg + c0 + threadIdx.x);
+        if (threadIdx.x < m) rows_s[threadIdx.x] = __ldcg(d.job_token + seg + c0 + threadIdx.x);
         __syncthreads();
-        stage_q8_internal(d.xq_codes, d.xq_scales, rows_s, m, nb, act_s, sc_s);
+        stage_internal(d.xq_codes, d.xq_scales, rows_s, m, nb, smem, MT, QUANT == UMSX_QUANT_Q8_0);
         __syncthreads();
-        float acc[MT][4];
-        rowgroup_dot<QUANT, MT>(codes, scales, nb, act_s, sc_s, m, lane, acc);
+        float acc[MT][8];
+        warp_dot<QUANT, MT>(ws, first, nb, st, m, lane, acc);
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
             if (t < m) {
                 const float v = __fadd_rn(finish_row<QUANT>(acc[t]), bias);
-                if ((lane & 3) == 0) res[(t * 2 + half) * 32 + rgi * 8 + (lane >> 2)] = v;
+                if (lane < RPW) res[t][half][wi * RPW + rrow] = v;
             }
         }
         __syncthreads();
-        // activation + Q8_0: warp t quantizes the 32 values of job t
-        for (int t = warp; t < m; t += 8) {
-            const float g = res[(t * 2 + 0) * 32 + lane], u = res[(t * 2 + 1) * 32 + lane];
+        // activation + Q8_0: warp w quantizes the 32 values of jobs w, w + nwarps, ...
+        for (int t = warp; t < m; t += 2 * GW) {
+            const float g = res[t][0][lane], u = res[t][1][lane];
             const float a = p.activation == UMSX_ACT_SWIGLU_OAI ? swiglu_oai(g, u, p.alpha, p.limit) : silu_mul(g, u);
             const float amax = warp_max(fabsf(a));
             const float inv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
@@ -471,7 +637,7 @@ __global__ void __launch_bounds__(256) k_gate_up(GateUpParams p, Dispatch d) {
 
 // ============================================================================
 // Generic expert GEMV: out[row(job)][n] = dot(W_e[n], act(job)) (+ bias).
-// One CTA = W row groups of one expert; grid = (N / (8W), slots).
+// One CTA = W warps of one expert; grid = (N / (W*rows-per-warp), slots).
 // Activation sources: 0 = internal Q8 (codes + fp32 scales), 1 = ggml block_q8_0
 // rows, 2 = fp32 rows quantized here with the x86 Q8_0 rule.
 // ============================================================================
@@ -483,68 +649,134 @@ struct GemvSrc {
     const float *f32;
 };
 
-template <int QUANT, int W, int MT, int SRC>
+template <int QUANT, int W, int MT, int SRC, int COMBINE>
 __global__ void __launch_bounds__(W * 32) k_gemv(GemvParams p, GemvSrc src, Dispatch d) {
+    constexpr int RPW = Geo<QUANT>::kRowsPerWarp;
     extern __shared__ __align__(16) uint8_t smem[];
-    const int slot = blockIdx.y;
-    if (slot >= __ldg(d.n_active)) return;
-    const int e = __ldg(d.active + slot);
-    const int seg = __ldg(d.offsets + e), cnt = __ldg(d.counts + e);
-    const int N = p.m.rows, nb = p.m.cols / 32, nrg = N / 8;
+    __shared__ int rows_s[MT], outs_s[MT], last_s[MT];
+    if (!p.prefetch_early) {
+        pdl_wait();
+        pdl_launch_dependents();
+    }
+    const int4 rec = __ldcg(d.slots + blockIdx.y);
+    const int e = rec.x;
+    if (e < 0) return;
+    const int seg = rec.y, cnt = rec.z;
+    const int N = p.m.rows, nb = p.m.cols / 32, nrg = N / RPW;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t *act_s = smem;
-    float *sc_s = reinterpret_cast<float *>(smem + (size_t)MT * nb * 32);
-    int *rows_s = reinterpret_cast<int *>(sc_s + MT * nb);
-    int *outs_s = rows_s + MT;
     const int rg = blockIdx.x * W + warp;
     const bool active_warp = rg < nrg;
-    const uint8_t *codes = p.m.codes + ((size_t)e * nrg + (active_warp ? rg : 0)) * plane_code_stride(QUANT, nb);
-    const uint8_t *scales = p.m.scales + ((size_t)e * nrg + (active_warp ? rg : 0)) * plane_scale_stride(QUANT, nb);
-    const int n = rg * 8 + (lane >> 2);
+    WStream<QUANT> ws;
+    ws.init(p.m.codes + code_offset(QUANT, e, nrg, active_warp ? rg : 0, nb),
+            p.m.scales + scale_offset(QUANT, e, nrg, active_warp ? rg : 0, nb), nb, lane);
+    WBatch<QUANT> first;
+    if (active_warp) ws.load(0, first);
+    if (p.prefetch_early) {  // the weights were chosen two kernels back; the activations come from the last one
+        pdl_wait();
+        pdl_launch_dependents();
+    }
+    const int n = rg * RPW + lane % RPW;
     const float bias = (p.bias && active_warp) ? __ldg(p.bias + (size_t)e * N + n) : 0.0f;
+    const Staged st = staged_view(smem, MT, nb);
+    uint4 *sq = reinterpret_cast<uint4 *>(smem);
+    float *ssc = reinterpret_cast<float *>(smem + (size_t)MT * nb * 64);
+    int *sfl = reinterpret_cast<int *>(smem + (size_t)MT * nb * 68);
     for (int c0 = 0; c0 < cnt; c0 += MT) {
         const int m = min(MT, cnt - c0);
+        if (c0 > 0 && active_warp) ws.load(0, first);
         __syncthreads();
         if (threadIdx.x < m) {
             const int j = seg + c0 + threadIdx.x;
-            const int tok = __ldg(d.job_token + j), rank = __ldg(d.job_rank + j);
+            const int tok = __ldcg(d.job_token + j), rank = __ldcg(d.job_rank + j);
             rows_s[threadIdx.x] = p.a_by_job ? j : tok * p.a_ts + rank * p.a_rs;
             outs_s[threadIdx.x] = tok * p.o_ts + rank;
         }
         __syncthreads();
         if constexpr (SRC == 0) {
-            stage_q8_internal(src.q8_codes, src.q8_scales, rows_s, m, nb, act_s, sc_s);
+            stage_internal(src.q8_codes, src.q8_scales, rows_s, m, nb, smem, MT, QUANT == UMSX_QUANT_Q8_0);
         } else if constexpr (SRC == 1) {
-            for (int i = threadIdx.x; i < m * nb * 32; i += blockDim.x) {
-                const int t = i / (nb * 32), r = i - t * nb * 32, b = r >> 5, k = r & 31;
-                act_s[((size_t)t * nb + b) * 32 + lane_pair_offset(k)] = src.ggml[((size_t)rows_s[t] * nb + b) * 34 + 2 + k];
+            for (int i = threadIdx.x; i < m * nb * 4; i += blockDim.x) {
+                const int t = i / (nb * 4), r = i - t * nb * 4, b = r >> 2, pp = r & 3;
+                const uint8_t *blk = src.ggml + ((size_t)rows_s[t] * nb + b) * 34 + 2;
+                uint32_t lo = 0, hi = 0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    lo |= (uint32_t)blk[4 * pp + k] << (8 * k);
+                    hi |= (uint32_t)blk[16 + 4 * pp + k] << (8 * k);
+                }
+                sq[((size_t)t * nb + b) * 4 + pp] = make_uint4(lo, hi, neg8x4(lo), neg8x4(hi));
             }
             for (int i = threadIdx.x; i < m * nb; i += blockDim.x) {
                 const int t = i / nb, b = i - t * nb;
                 const uint8_t *blk = src.ggml + ((size_t)rows_s[t] * nb + b) * 34;
-                sc_s[i] = f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+                ssc[i] = f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+                if (QUANT == UMSX_QUANT_Q8_0) {
+                    int any = 0;
+                    for (int k = 0; k < 32; ++k) any |= blk[2 + k] == 0x80;
+                    sfl[i] = any;
+                }
             }
         } else {
+            uint8_t *sb = smem;
             for (int i = warp; i < m * nb; i += W) {
                 const int t = i / nb, b = i - t * nb;
                 const float v = __ldg(src.f32 + (size_t)rows_s[t] * p.m.cols + b * 32 + lane);
                 const float amax = warp_max(fabsf(v));
                 const float inv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-                act_s[((size_t)t * nb + b) * 32 + lane_pair_offset(lane)] = (uint8_t)(int8_t)q8_code(v, inv);
-                if (lane == 0) sc_s[i] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+                const int q = q8_code(v, inv);
+                // code byte of element `lane` into the a(...) words of lane pair (lane%16)/4
+                sb[((size_t)i * 4 + ((lane & 15) >> 2)) * 16 + (lane >> 4) * 4 + (lane & 3)] = (uint8_t)(int8_t)q;
+                __syncwarp();
+                if (lane < 4) {
+                    uint4 *slot4 = sq + (size_t)i * 4 + lane;
+                    const uint4 cur = *slot4;
+                    *slot4 = make_uint4(cur.x, cur.y, neg8x4(cur.x), neg8x4(cur.y));
+                }
+                const unsigned has = __ballot_sync(kFull, q == -128);
+                if (lane == 0) {
+                    ssc[i] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+                    sfl[i] = has != 0;
+                }
             }
         }
         __syncthreads();
         if (active_warp) {
-            float acc[MT][4];
-            rowgroup_dot<QUANT, MT>(codes, scales, nb, act_s, sc_s, m, lane, acc);
+            float acc[MT][8];
+            warp_dot<QUANT, MT>(ws, first, nb, st, m, lane, acc);
 #pragma unroll
             for (int t = 0; t < MT; ++t) {
                 if (t < m) {
                     float v = finish_row<QUANT>(acc[t]);
                     if (p.bias) v = __fadd_rn(v, bias);
-                    if ((lane & 3) == 0) p.out[(size_t)outs_s[t] * N + n] = v;
+                    if (lane < RPW) p.out[(size_t)outs_s[t] * N + n] = v;
                 }
+            }
+        }
+        if constexpr (COMBINE) {
+            // Rank-order combine (+ residual) of this CTA's rows, done by whichever of the
+            // K expert CTAs of a token finishes last: no CTA waits for another.
+            __threadfence();  // every writer of this CTA's rows publishes them at device scope
+            __syncthreads();
+            if (threadIdx.x < m) {
+                const int tok = outs_s[threadIdx.x] / p.top_k;
+                const unsigned prev = atomicAdd(p.tile_done + (size_t)tok * gridDim.x + blockIdx.x, 1u);
+                last_s[threadIdx.x] = prev == (unsigned)(p.top_k - 1) ? tok : -1;
+            }
+            __syncthreads();
+            for (int t = 0; t < m; ++t) {
+                const int tok = last_s[t];
+                if (tok < 0) continue;
+                __threadfence();
+                const int K = p.top_k, n0 = blockIdx.x * W * RPW;
+                for (int i = threadIdx.x; i < W * RPW && n0 + i < N; i += blockDim.x) {
+                    float acc = 0.0f;
+                    for (int r = 0; r < K; ++r)
+                        acc = __fadd_rn(acc, __fmul_rn(__ldcg(p.route_w + (size_t)tok * K + r),
+                                                       __ldcg(p.out + ((size_t)tok * K + r) * N + n0 + i)));
+                    if (p.residual) acc = __fadd_rn(p.residual[(size_t)tok * N + n0 + i], acc);
+                    p.combine_out[(size_t)tok * N + n0 + i] = acc;
+                }
+                if (threadIdx.x == 0) p.tile_done[(size_t)tok * gridDim.x + blockIdx.x] = 0;
             }
         }
     }
@@ -586,23 +818,21 @@ __global__ void k_combine(const float *__restrict__ y, const float *__restrict__
 
 template <bool TO_TILE>
 __global__ void k_layout(Matrix m, int expert, uint8_t *ggml) {
-    const int nb = m.cols / 32, nrg = m.rows / 8;
+    const int nb = m.cols / 32;
     const size_t total = (size_t)m.rows * nb;
     const bool mx = m.quant == UMSX_QUANT_MXFP4;
     const size_t bb = mx ? 17 : 34;
+    const int rpw = mx ? 16 : 32, nrg = m.rows / rpw;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int row = (int)(i / nb), b = (int)(i - (size_t)row * nb);
-        const int rg = row >> 3, w = row & 7;
+        const int rg = row / rpw, r = row % rpw;
         uint8_t *blk = ggml + i * bb;
-        uint8_t *cbase = m.codes + ((size_t)expert * nrg + rg) * (size_t)nb * (mx ? 128 : 256);
-        uint8_t *sbase = m.scales + ((size_t)expert * nrg + rg) * (size_t)nb * (mx ? 8 : 16);
         if (mx) {
-            const int g = b >> 2, j = b & 3, nblk = (g < (nb >> 2)) ? 4 : 2;
-            uint8_t *chunk = cbase + (size_t)g * 512;
-            uint8_t *sc = sbase + (size_t)g * 32 + w * nblk + j;
-            if (TO_TILE) *sc = blk[0]; else blk[0] = *sc;
+            const int np = nb / 2, nq = (np + 3) / 4, bp = b >> 1, h = b & 1, L = h * 16 + r;
+            uint32_t *words = reinterpret_cast<uint32_t *>(m.codes + (((size_t)expert * nrg + rg) * np + bp) * 512 + L * 16);
+            uint8_t *ex = m.scales + (((size_t)expert * nrg + rg) * nq + (bp >> 2)) * 128 + L * 4 + (bp & 3);
+            if (TO_TILE) *ex = blk[0]; else blk[0] = *ex;
             for (int pp = 0; pp < 4; ++pp) {
-                uint32_t *word = reinterpret_cast<uint32_t *>(chunk + ((w * 4 + pp) * nblk + j) * 4);
                 if (TO_TILE) {
                     uint32_t v = 0;
                     for (int q = 0; q < 4; ++q) {
@@ -610,23 +840,21 @@ __global__ void k_layout(Matrix m, int expert, uint8_t *ggml) {
                         v |= (byte & 15u) << (4 * q);
                         v |= (byte >> 4) << (16 + 4 * q);
                     }
-                    *word = v;
+                    words[pp] = v;
                 } else {
-                    const uint32_t v = *word;
+                    const uint32_t v = words[pp];
                     for (int q = 0; q < 4; ++q)
                         blk[1 + 4 * pp + q] = (uint8_t)(((v >> (4 * q)) & 15u) | (((v >> (16 + 4 * q)) & 15u) << 4));
                 }
             }
         } else {
-            const int g = b >> 1, j = b & 1;
-            uint8_t *chunk = cbase + (size_t)g * 512;
-            uint8_t *sc = sbase + (size_t)g * 32 + (w * 2 + j) * 2;
+            uint8_t *dst = m.codes + (((size_t)expert * nrg + rg) * nb + b) * 1024 + r * 32;
+            uint8_t *sc = m.scales + (((size_t)expert * nrg + rg) * (nb / 2) + (b >> 1)) * 128 + r * 4 + (b & 1) * 2;
             if (TO_TILE) { sc[0] = blk[0]; sc[1] = blk[1]; } else { blk[0] = sc[0]; blk[1] = sc[1]; }
             for (int pp = 0; pp < 4; ++pp) {
-                uint8_t *dst = chunk + ((w * 4 + pp) * 2 + j) * 8;
                 for (int q = 0; q < 4; ++q) {
-                    if (TO_TILE) { dst[q] = blk[2 + 4 * pp + q]; dst[4 + q] = blk[2 + 16 + 4 * pp + q]; }
-                    else { blk[2 + 4 * pp + q] = dst[q]; blk[2 + 16 + 4 * pp + q] = dst[4 + q]; }
+                    if (TO_TILE) { dst[pp * 8 + q] = blk[2 + 4 * pp + q]; dst[pp * 8 + 4 + q] = blk[2 + 16 + 4 * pp + q]; }
+                    else { blk[2 + 4 * pp + q] = dst[pp * 8 + q]; blk[2 + 16 + 4 * pp + q] = dst[pp * 8 + 4 + q]; }
                 }
             }
         }
@@ -689,31 +917,49 @@ static inline int grid_for(size_t n, int threads, int cap = 148 * 16) {
     return (int)(g > (size_t)cap ? cap : g);
 }
 
+// Launch with the programmatic-stream-serialization attribute (PDL).
+template <class... KArgs, class... Args>
+static void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 int launch_router(const RouterParams &p, const Dispatch &d, cudaStream_t s) {
     dim3 grid((p.experts + kRouterWarps - 1) / kRouterWarps, p.tokens);
     RouterParams q = p;
     q.fuse_dispatch = p.tokens * p.top_k <= kFusedDispatchMax;
-    k_router<<<grid, 256, (size_t)p.hidden * sizeof(float), s>>>(q, d);
+    const size_t smem = (size_t)p.hidden * sizeof(float);
+    if (p.hidden <= 32 * kRouterRegs) launch_pdl(k_router<true>, grid, dim3(kRouterWarps * 32), smem, s, q, d);
+    else launch_pdl(k_router<false>, grid, dim3(kRouterWarps * 32), smem, s, q, d);
     int launched = 1;
     if (!q.fuse_dispatch) {
-        k_dispatch<<<p.e_local, 256, 0, s>>>(d, p.tokens * p.top_k, p.top_k, p.e_lo, p.e_local);
+        launch_pdl(k_dispatch, dim3(p.e_local), dim3(256), 0, s, d, p.tokens * p.top_k, p.top_k, p.e_lo, p.e_local);
         ++launched;
     }
     return launched;
 }
 
 int launch_dispatch(const Dispatch &d, int entries, int top_k, int e_lo, int e_local, cudaStream_t s) {
-    k_dispatch<<<e_local, 256, 0, s>>>(d, entries, top_k, e_lo, e_local);
+    launch_pdl(k_dispatch, dim3(e_local), dim3(256), 0, s, d, entries, top_k, e_lo, e_local);
     return 1;
 }
 
 template <int QUANT, int MT>
 static void gate_up_mt(const GateUpParams &p, const Dispatch &d, int slots, cudaStream_t s) {
     const int nb = p.hidden / 32;
-    const size_t smem = (size_t)MT * nb * 36 + MT * 64 * sizeof(float) + 64;
+    const size_t smem = staged_bytes(MT, nb);
     auto kern = k_gate_up<QUANT, MT>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<dim3(p.intermediate / 32, slots), 256, smem, s>>>(p, d);
+    launch_pdl(kern, dim3(p.intermediate / 32, slots), dim3(64 * Geo<QUANT>::kChains), smem, s, p, d);
 }
 
 int launch_gate_up(const GateUpParams &p, const Dispatch &d, int slots, int max_per_expert, cudaStream_t s) {
@@ -728,23 +974,23 @@ int launch_gate_up(const GateUpParams &p, const Dispatch &d, int slots, int max_
     return 1;
 }
 
-template <int QUANT, int MT, int SRC>
+template <int QUANT, int MT, int SRC, int COMBINE>
 static void gemv_mt(const GemvParams &p, const GemvSrc &src, const Dispatch &d, int slots, cudaStream_t s) {
     constexpr int W = 4;
     const int nb = p.m.cols / 32;
-    const size_t smem = (size_t)MT * nb * 36 + 2 * MT * sizeof(int) + 16;
-    auto kern = k_gemv<QUANT, W, MT, SRC>;
+    const size_t smem = staged_bytes(MT, nb);
+    auto kern = k_gemv<QUANT, W, MT, SRC, COMBINE>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const int tiles = (p.m.rows / 8 + W - 1) / W;
-    kern<<<dim3(tiles, slots), W * 32, smem, s>>>(p, src, d);
+    const int tiles = (p.m.rows / Geo<QUANT>::kRowsPerWarp + W - 1) / W;
+    launch_pdl(kern, dim3(tiles, slots), dim3(W * 32), smem, s, p, src, d);
 }
 
-template <int QUANT, int SRC>
+template <int QUANT, int SRC, int COMBINE>
 static void gemv_src(const GemvParams &p, const GemvSrc &src, const Dispatch &d, int slots, int mpe, cudaStream_t s) {
-    if (mpe <= 1) gemv_mt<QUANT, 1, SRC>(p, src, d, slots, s);
-    else if (mpe <= 2) gemv_mt<QUANT, 2, SRC>(p, src, d, slots, s);
-    else if (mpe <= 4) gemv_mt<QUANT, 4, SRC>(p, src, d, slots, s);
-    else gemv_mt<QUANT, 8, SRC>(p, src, d, slots, s);
+    if (mpe <= 1) gemv_mt<QUANT, 1, SRC, COMBINE>(p, src, d, slots, s);
+    else if (mpe <= 2) gemv_mt<QUANT, 2, SRC, COMBINE>(p, src, d, slots, s);
+    else if (mpe <= 4) gemv_mt<QUANT, 4, SRC, COMBINE>(p, src, d, slots, s);
+    else gemv_mt<QUANT, 8, SRC, COMBINE>(p, src, d, slots, s);
 }
 
 int launch_gemv(const GemvParams &p, const Dispatch &d, int slots, int max_per_expert, cudaStream_t s) {
@@ -753,11 +999,11 @@ int launch_gemv(const GemvParams &p, const Dispatch &d, int slots, int max_per_e
     src.f32 = p.a_f32;
     const bool ggml = p.a_q8 != nullptr;
     if (p.m.quant == UMSX_QUANT_MXFP4) {
-        if (ggml) gemv_src<UMSX_QUANT_MXFP4, 1>(p, src, d, slots, max_per_expert, s);
-        else gemv_src<UMSX_QUANT_MXFP4, 2>(p, src, d, slots, max_per_expert, s);
+        if (ggml) gemv_src<UMSX_QUANT_MXFP4, 1, 0>(p, src, d, slots, max_per_expert, s);
+        else gemv_src<UMSX_QUANT_MXFP4, 2, 0>(p, src, d, slots, max_per_expert, s);
     } else {
-        if (ggml) gemv_src<UMSX_QUANT_Q8_0, 1>(p, src, d, slots, max_per_expert, s);
-        else gemv_src<UMSX_QUANT_Q8_0, 2>(p, src, d, slots, max_per_expert, s);
+        if (ggml) gemv_src<UMSX_QUANT_Q8_0, 1, 0>(p, src, d, slots, max_per_expert, s);
+        else gemv_src<UMSX_QUANT_Q8_0, 2, 0>(p, src, d, slots, max_per_expert, s);
     }
     return 1;
 }
@@ -767,8 +1013,13 @@ int launch_gemv_internal(const GemvParams &p, const uint8_t *codes, const float 
     GemvSrc src{};
     src.q8_codes = codes;
     src.q8_scales = scales;
-    if (p.m.quant == UMSX_QUANT_MXFP4) gemv_src<UMSX_QUANT_MXFP4, 0>(p, src, d, slots, max_per_expert, s);
-    else gemv_src<UMSX_QUANT_Q8_0, 0>(p, src, d, slots, max_per_expert, s);
+    if (p.tile_done) {
+        if (p.m.quant == UMSX_QUANT_MXFP4) gemv_src<UMSX_QUANT_MXFP4, 0, 1>(p, src, d, slots, max_per_expert, s);
+        else gemv_src<UMSX_QUANT_Q8_0, 0, 1>(p, src, d, slots, max_per_expert, s);
+    } else {
+        if (p.m.quant == UMSX_QUANT_MXFP4) gemv_src<UMSX_QUANT_MXFP4, 0, 0>(p, src, d, slots, max_per_expert, s);
+        else gemv_src<UMSX_QUANT_Q8_0, 0, 0>(p, src, d, slots, max_per_expert, s);
+    }
     return 1;
 }
 
