@@ -168,6 +168,23 @@ umsx_status umsx_stack_forward_host(umsx_stack *stack, const void *x, int x_dtyp
 umsx_status umsx_stack_set_timing(umsx_stack *stack, int enable);
 umsx_status umsx_stack_stage_times(umsx_stack *stack, float *ms, int n_stages);
 
+/* The router of umsx_route without a handle and without allocating anything (no counterpart
+ * in the reference).  For callers that cannot call cudaMalloc: an operator inside a framework
+ * that plans every buffer ahead and hands it only its own tensors, or a process whose device
+ * memory budget is spent.  The caller passes device buffers: x [T][H] (fp32 or bf16, 16-byte
+ * aligned), router_w [E][H] fp32, router_b [E] fp32 or NULL, and receives ids [T][k] int32,
+ * weights [T][k] fp32 and, if counts is not NULL, counts [E] int32; results equal umsx_route's.
+ * The kernel's scratch (logits, completion counters, dispatch lists, quantized x) is a fixed
+ * 512 KiB array inside this library that every GPU loading it holds until the process exits;
+ * limits: T <= 64, E <= 256, k <= min(8, E), H a multiple of 64 up to 4096 (UMSX_EINVAL
+ * beyond).  It runs on the calling thread's current device; the first call on a device looks
+ * up the array's device address, so make that first call before any stream capture.  All calls
+ * on a device share the array: calls that overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller.  Errors read back through umsx_last_error(). */
+umsx_status umsx_route_static(const void *x, int x_dtype, int tokens, const float *router_w, const float *router_b,
+                              int hidden, int experts, int top_k, int routing, float routed_scale, int32_t *ids,
+                              float *weights, int32_t *counts, umsx_stream stream);
+
 /* Number of this library's kernels launched by the calling thread since load (graph replays count
  * every kernel they contain). */
 uint64_t umsx_kernel_launches(void);

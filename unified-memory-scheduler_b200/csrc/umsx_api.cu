@@ -61,6 +61,11 @@ size_t block_bytes(int quant) { return quant == UMSX_QUANT_MXFP4 ? 17 : 34; }
 
 }  // namespace
 
+namespace umsx {
+void record_error(const char *msg) { g_error = msg; }
+void record_launches(uint64_t kernels) { g_launches += kernels; }
+}  // namespace umsx
+
 // Per-call scratch: the router's dispatch state, the quantized activations,
 // the per-job expert outputs and forward_host staging.  A layer owns one; a
 // stack owns one shared by all of its layers (they run one after another).

@@ -97,6 +97,10 @@ struct GemvParams {
     int prefetch_early;     // the slot records were written two kernels back: prefetch weights before waiting
 };
 
+// Thread-local status channel shared by every translation unit (umsx_api.cu).
+void record_error(const char *msg);      // the message umsx_last_error() returns
+void record_launches(uint64_t kernels);  // adds to umsx_kernel_launches()
+
 // Launchers (umsx_kernels.cu).  Each returns the number of kernels launched.
 int launch_router(const RouterParams &p, const Dispatch &d, cudaStream_t s);
 int launch_dispatch(const Dispatch &d, int entries, int top_k, int e_lo, int e_local, cudaStream_t s);

@@ -33,8 +33,8 @@ BLOCK_BYTES = {QUANT_Q8_0: 34, QUANT_MXFP4: 17}
 EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "umsx_moe_forward",
            "umsx_moe_forward_host", "umsx_route", "umsx_expert_down_q8", "umsx_mul_mat_id", "umsx_combine",
            "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_destroy", "umsx_stack_forward",
-           "umsx_stack_forward_host", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_kernel_launches",
-           "umsx_last_error", "umsx_version"]
+           "umsx_stack_forward_host", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_route_static",
+           "umsx_kernel_launches", "umsx_last_error", "umsx_version"]
 
 
 class UmsxError(RuntimeError):
@@ -86,6 +86,7 @@ def lib():
         "umsx_stack_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
         "umsx_stack_set_timing": (i32, [vp, i32]),
         "umsx_stack_stage_times": (i32, [vp, C.POINTER(C.c_float), i32]),
+        "umsx_route_static": (i32, [vp, i32, i32, vp, vp, i32, i32, i32, i32, C.c_float, vp, vp, vp, vp]),
         "umsx_kernel_launches": (u64, []),
         "umsx_last_error": (C.c_char_p, []),
         "umsx_version": (i32, []),
@@ -138,6 +139,23 @@ def combine(y, weights, out=None, stream=None):
     out = out if out is not None else torch.empty((T, W), dtype=torch.float32, device=y.device)
     check(lib().umsx_combine(_ptr(y), _ptr(weights), T, K, W, _ptr(out), _stream(stream)))
     return out
+
+
+def route_static(x, router_w, router_b, experts: int, top_k: int, routing: int, routed_scale: float = 1.0,
+                 stream=None):
+    """umsx_route_static: routing without a layer handle, using only the library's fixed scratch.
+
+    For callers that may not allocate device memory.  The output tensors here are
+    allocated by torch for convenience; the C entry point itself allocates nothing.
+    Calls that overlap on the GPU share the scratch and race."""
+    import torch
+    T, H = x.shape
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
+    counts = torch.empty(experts, dtype=torch.int32, device=x.device)
+    check(lib().umsx_route_static(_ptr(x), _dtype_code(x), T, _ptr(router_w), _ptr(router_b), H, experts, top_k,
+                                  routing, routed_scale, _ptr(ids), _ptr(w), _ptr(counts), _stream(stream)))
+    return ids, w, counts
 
 
 class MoeLayer:
