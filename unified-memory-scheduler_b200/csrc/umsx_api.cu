@@ -73,6 +73,10 @@ struct Workspace {
     Dispatch disp{};
     uint8_t *act_codes = nullptr;
     float *act_scales = nullptr;
+    float *act_f32 = nullptr;
+    uint8_t *act_rec = nullptr;
+    float *act_sc = nullptr;
+    uint32_t *act_done = nullptr;
     float *y = nullptr;
     void *x_dev = nullptr;
     float *out_dev = nullptr;
@@ -172,6 +176,15 @@ void carve_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_
     p.tile_done = a.take<uint32_t>(T * (H / 32));
     w.act_codes = a.take<uint8_t>(T * K * I);
     w.act_scales = a.take<float>(T * K * (I / 32));
+    const bool mx = d.quant == UMSX_QUANT_MXFP4;
+    const size_t nbH = H / 32, nbI = I / 32;
+    w.act_f32 = mx ? a.take<float>(T * K * I) : nullptr;
+    w.act_rec = mx ? a.take<uint8_t>(T * K * nbI * 64) : nullptr;
+    w.act_sc = mx ? a.take<float>(T * K * ((nbI + 3) & ~size_t(3))) : nullptr;
+    w.act_done = mx ? a.take<uint32_t>(T * K * nbI) : nullptr;
+    p.xr = mx ? a.take<uint8_t>(T * nbH * 64) : nullptr;
+    p.xr_sc = mx ? a.take<float>(T * ((nbH + 3) & ~size_t(3))) : nullptr;
+    p.err = a.take<uint32_t>(1);
     w.y = a.take<float>(T * K * H);
     w.x_dev = a.take<float>(T * H);
     w.out_dev = a.take<float>(T * H);
@@ -375,7 +388,7 @@ umsx_status check_call(umsx_moe *m, const void *x, int x_dtype, int tokens, int 
 }
 
 umsx_status run_router(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, int rmsnorm, float eps,
-                       cudaStream_t s) {
+                       cudaStream_t s, int skip_counts = 0) {
     RouterParams p{};
     p.x = x;
     p.x_dtype = x_dtype;
@@ -391,6 +404,8 @@ umsx_status run_router(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, i
     p.e_local = m->e_local;
     p.rmsnorm = rmsnorm;
     p.eps = eps;
+    p.skip_counts = skip_counts;
+    p.mx_records = m->d.quant == UMSX_QUANT_MXFP4;
     UMSX_LAUNCHED(launch_router(p, ws.disp, s));
     return UMSX_OK;
 }
@@ -412,7 +427,7 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
                       const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev) {
     const auto &d = m->d;
     if (ev) if (umsx_status st = mark(ev[0], s)) return st;
-    if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s)) return st;
+    if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s, 1)) return st;
     if (ev) if (umsx_status st = mark(ev[1], s)) return st;
     const int slots = std::min(m->e_local, tokens * d.top_k);
     GateUpParams g{};
@@ -428,6 +443,10 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     g.limit = d.swiglu_limit;
     g.act_codes = ws.act_codes;
     g.act_scales = ws.act_scales;
+    g.act_f32 = ws.act_f32;
+    g.act_rec = ws.act_rec;
+    g.act_sc = ws.act_sc;
+    g.act_done = ws.act_done;
     UMSX_LAUNCHED(launch_gate_up(g, ws.disp, slots, tokens, s));
     if (ev) if (umsx_status st = mark(ev[2], s)) return st;
     GemvParams p{};
@@ -446,7 +465,9 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
         p.top_k = d.top_k;
         p.prefetch_early = 1;
     }
-    UMSX_LAUNCHED(launch_gemv_internal(p, ws.act_codes, ws.act_scales, ws.disp, slots, tokens, s));
+    if (d.quant == UMSX_QUANT_MXFP4) { p.a_rec = ws.act_rec; p.a_rsc = ws.act_sc; }  // bulk-copied records
+    else { p.a_codes = ws.act_codes; p.a_scales = ws.act_scales; }
+    UMSX_LAUNCHED(launch_gemv(p, ws.disp, slots, tokens, s));
     if (ev) {  // timed stages keep the combine a kernel of its own so that every stage has a boundary
         if (umsx_status st = mark(ev[3], s)) return st;
         UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, s));

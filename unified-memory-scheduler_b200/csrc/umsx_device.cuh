@@ -119,6 +119,46 @@ __device__ __forceinline__ int q8_code(float v, float inv) {
 // GEMV kernels use: [p = (i%16)/4][half = i/16][i%4].
 __device__ __forceinline__ int lane_pair_offset(int i) { return ((i & 15) >> 2) * 8 + (i >> 4) * 4 + (i & 3); }
 
+// ---- bulk copies into shared memory, completed on an mbarrier ----------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// cp.async.bulk global -> shared; src, dst 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase with the given parity, giving up after `limit_cycles`
+// (clock64); returns false on time-out so the caller can report and stop.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, long long limit_cycles) {
+    const long long t0 = clock64();
+    while (!mbar_test(bar, parity))
+        if (clock64() - t0 > limit_cycles) return false;
+    return true;
+}
+
 // ---- counter-based generator (identical to the oracle's orc_rng) -------------
 
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {

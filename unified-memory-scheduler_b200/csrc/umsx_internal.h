@@ -2,9 +2,10 @@
 //
 // Device layout of an expert matrix (N rows x K columns, nb = K/32 blocks):
 //   MXFP4 code plane: rows in groups of 16, blocks in pairs; chunk (group, pair) is
-//     512 bytes, lane L = 16*h + r holds 16 bytes for row r and block 2*pair + h: four
-//     32-bit words, word p = codes of elements 4p..4p+3 (bits 0-15, 4 per element)
-//     and 16+4p..16+4p+3 (bits 16-31).  One warp-wide 16-byte load reads a chunk.
+//     512 bytes = [lane half lh][L = 16*h + r][8 bytes] for row r and block 2*pair + h:
+//     two 32-bit words, word w = sel(2w) | sel(2w+1) << 16, sel(p) = the four 4-bit
+//     codes of elements 4p..4p+3 (lh 0) or 16+4p..16+4p+3 (lh 1).  A warp-wide 8-byte
+//     load reads one lane half of a chunk.
 //   MXFP4 exponent plane: chunk (group, pair quad) is 128 bytes, lane L holds the
 //     exponents of its (row, block) for four consecutive pairs (padded to a quad).
 //   Q8_0 code plane: rows in groups of 32; chunk (group, block) is 1 KB, lane r holds
@@ -52,6 +53,9 @@ struct Dispatch {
     float *xq_scales;    // [T][H/32] fp16-rounded Q8_0 scales of x
     int4 *slots;         // [E_local] per active slot {local expert, segment start, count, -}; expert -1 past the last
     uint32_t *tile_done; // [T][H/32] combine arrival counters, zero between launches
+    uint8_t *xr;         // [T][H/32][64] x as MXFP4 staging records (MXFP4 layers)
+    float *xr_sc;        // [T][pad4(H/32)] their scales
+    uint32_t *err;       // [1] set by a kernel whose bounded wait timed out (never cleared by kernels)
 };
 
 struct RouterParams {
@@ -65,6 +69,8 @@ struct RouterParams {
     int fuse_dispatch;  // the last finishing CTA builds the dispatch (small T*K)
     int rmsnorm;        // normalise each input row (unit weight) before routing / quantizing
     float eps;
+    int skip_counts;    // the caller needs only slot records and job lists (per-expert counts unwritten)
+    int mx_records;     // write x as MXFP4 staging records (Dispatch::xr) instead of lane-pair Q8 rows
 };
 
 struct GateUpParams {
@@ -76,6 +82,10 @@ struct GateUpParams {
     float alpha, limit;
     uint8_t *act_codes; // [T*K][I/32][32] Q8_0 codes of the activation, permuted job order, lane-pair order
     float *act_scales;  // [T*K][I/32] fp16-rounded Q8_0 scales
+    float *act_f32;     // [T*K][I] activation values before quantization (MXFP4 path)
+    uint8_t *act_rec;   // [T*K][I/32][64] quantized activations as MXFP4 staging records
+    float *act_sc;      // [T*K][pad4(I/32)] their scales
+    uint32_t *act_done; // [T*K][I/32] arrival counters of the two CTAs of each 32-value block
 };
 
 struct GemvParams {
@@ -83,6 +93,10 @@ struct GemvParams {
     const float *bias;      // [E_local][N] or null
     const float *a_f32;     // activation rows to quantize, or null
     const uint8_t *a_q8;    // ggml block_q8_0 rows, or null
+    const uint8_t *a_codes; // internal Q8 rows (lane-pair codes) when a_f32, a_q8 and a_rec are null
+    const float *a_scales;
+    const uint8_t *a_rec;   // MXFP4 staging records [row][nb][64] + scales [row][pad4(nb)], bulk-copied
+    const float *a_rsc;
     int a_by_job;           // activation row = permuted job index
     int a_ts, a_rs;         // else activation row = token*a_ts + rank*a_rs
     float *out;             // output rows of N floats
@@ -106,8 +120,7 @@ int launch_router(const RouterParams &p, const Dispatch &d, cudaStream_t s);
 int launch_dispatch(const Dispatch &d, int entries, int top_k, int e_lo, int e_local, cudaStream_t s);
 int launch_gate_up(const GateUpParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
 int launch_gemv(const GemvParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
-int launch_gemv_internal(const GemvParams &p, const uint8_t *codes, const float *scales, const Dispatch &d,
-                         int max_slots, int max_per_expert, cudaStream_t s);
+
 int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *residual, float *out,
                    cudaStream_t s);
 int launch_repack(const Matrix &m, int expert, const uint8_t *ggml, cudaStream_t s);

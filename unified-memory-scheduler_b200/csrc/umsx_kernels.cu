@@ -37,7 +37,7 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 __device__ __forceinline__ bool better(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
 
 // Warp-wide selection for one token (all 32 lanes participate).
-__device__ void select_token(const RouterParams &p, const Dispatch &d, int t, int lane) {
+__device__ int select_token(const RouterParams &p, const Dispatch &d, int t, int lane) {
     const int E = p.experts, K = p.top_k;
     float v[kMaxExperts / 32];
     const float *lg = d.logits + (size_t)t * E;
@@ -104,6 +104,7 @@ __device__ void select_token(const RouterParams &p, const Dispatch &d, int t, in
         d.ids[(size_t)t * K + lane] = my_sel;
         d.weights[(size_t)t * K + lane] = w;
     }
+    return my_sel;  // lane r < K: the expert of rank r
 }
 
 // One CTA builds counts / offsets / active list / slot records / job lists for
@@ -161,6 +162,22 @@ __device__ void build_dispatch_cta(const Dispatch &d, int entries, int K, int e_
     }
 }
 
+constexpr long long kWaitLimitCycles = 4000000;  // ~2 ms: bounded waits on mbarriers
+__host__ __device__ constexpr int pad4(int n) { return (n + 3) & ~3; }
+
+// One warp holds the 32 Q8_0 codes of a block (code of element `lane`); writes the
+// block's MXFP4 staging record: for lane half lh and lane p, at
+// ((lh*2 + p/2)*16 + (p%2)*8) the code word a(lh, p) and its byte negation.
+__device__ __forceinline__ void write_mx_record(int code, uint8_t *rec, int lane) {
+    const uint32_t c = (uint32_t)code & 0xffu;
+    const uint32_t w = c | (__shfl_down_sync(kFull, c, 1) << 8) | (__shfl_down_sync(kFull, c, 2) << 16) |
+                       (__shfl_down_sync(kFull, c, 3) << 24);
+    if ((lane & 3) == 0) {
+        const int lh = lane >> 4, p = (lane & 15) >> 2;
+        *reinterpret_cast<uint2 *>(rec + (lh * 2 + (p >> 1)) * 16 + (p & 1) * 8) = make_uint2(w, neg8x4(w));
+    }
+}
+
 // grid = (ceil(E/4), T), block = 128: one warp per expert logit.
 template <bool REGS>
 __global__ void __launch_bounds__(128) k_router(RouterParams p, Dispatch d) {
@@ -197,27 +214,39 @@ __global__ void __launch_bounds__(128) k_router(RouterParams p, Dispatch d) {
         for (int i = threadIdx.x; i < H / 4; i += blockDim.x) reinterpret_cast<float4 *>(xs)[i] = xf[i];
     }
     __syncthreads();
+    float inv = 1.0f;  // x * 1 is exact: without RMSNorm the products below leave x unchanged
     if (p.rmsnorm) {
         // RMSNorm with unit weight: sum of squares in the shared strided order (orc_rmsnorm)
         if (warp == 0) {
             float acc = 0.0f;
-            for (int k = lane; k < H; k += 32) acc = __fmaf_rn(xs[k], xs[k], acc);
+            if constexpr (REGS) {
+#pragma unroll
+                for (int i = 0; i < kRouterRegs; ++i)
+                    if (lane + 32 * i < H) acc = __fmaf_rn(xs[lane + 32 * i], xs[lane + 32 * i], acc);
+            } else {
+                for (int k = lane; k < H; k += 32) acc = __fmaf_rn(xs[k], xs[k], acc);
+            }
             const float ss = warp_tree_sum(acc);
             if (lane == 0) inv_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), p.eps)));
         }
         __syncthreads();
-        const float inv = inv_s;
-        for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = __fmul_rn(xs[i], inv);
-        __syncthreads();
+        inv = inv_s;
     }
     // x -> Q8_0 (one warp per 32-element block), spread over this token's CTAs.
     const int nbH = H / 32;
     for (int b = blockIdx.x * kRouterWarps + warp; b < nbH; b += gridDim.x * kRouterWarps) {
-        const float v = xs[b * 32 + lane];
+        const float v = __fmul_rn(xs[b * 32 + lane], inv);
         const float amax = warp_max(fabsf(v));
-        const float inv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        d.xq_codes[((size_t)t * nbH + b) * 32 + lane_pair_offset(lane)] = (uint8_t)(int8_t)q8_code(v, inv);
-        if (lane == 0) d.xq_scales[(size_t)t * nbH + b] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+        const float qinv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const int code = q8_code(v, qinv);
+        const float qs = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+        if (p.mx_records) {
+            write_mx_record(code, d.xr + ((size_t)t * nbH + b) * 64, lane);
+            if (lane == 0) d.xr_sc[(size_t)t * pad4(nbH) + b] = qs;
+        } else {
+            d.xq_codes[((size_t)t * nbH + b) * 32 + lane_pair_offset(lane)] = (uint8_t)(int8_t)code;
+            if (lane == 0) d.xq_scales[(size_t)t * nbH + b] = qs;
+        }
     }
     // logits: 32 strided FMA chains, then the xor tree (orc_logit)
     if (has_e) {
@@ -225,7 +254,7 @@ __global__ void __launch_bounds__(128) k_router(RouterParams p, Dispatch d) {
         if constexpr (REGS) {
 #pragma unroll
             for (int i = 0; i < kRouterRegs; ++i)
-                if (lane + 32 * i < H) acc = __fmaf_rn(wv[i], xs[lane + 32 * i], acc);
+                if (lane + 32 * i < H) acc = __fmaf_rn(wv[i], __fmul_rn(xs[lane + 32 * i], inv), acc);
         } else {
             const float *wr = p.w + (size_t)e * H;
             constexpr int kRB = 16;
@@ -235,7 +264,7 @@ __global__ void __launch_bounds__(128) k_router(RouterParams p, Dispatch d) {
                 for (int i = 0; i < kRB; ++i) w[i] = (k0 + 32 * i < H) ? __ldg(wr + k0 + 32 * i) : 0.0f;
 #pragma unroll
                 for (int i = 0; i < kRB; ++i)
-                    if (k0 + 32 * i < H) acc = __fmaf_rn(w[i], xs[k0 + 32 * i], acc);
+                    if (k0 + 32 * i < H) acc = __fmaf_rn(w[i], __fmul_rn(xs[k0 + 32 * i], inv), acc);
             }
         }
         float l = warp_tree_sum(acc);
@@ -249,9 +278,33 @@ __global__ void __launch_bounds__(128) k_router(RouterParams p, Dispatch d) {
     __syncthreads();
     if (!last) return;
     __threadfence();
-    if (warp == 0) select_token(p, d, t, lane);
+    int sel = -1;
+    if (warp == 0) sel = select_token(p, d, t, lane);
     if (threadIdx.x == 0) d.token_done[t] = 0;
     if (!p.fuse_dispatch) return;
+    if (gridDim.y == 1 && p.skip_counts) {
+        // One token: the slot records follow from the selection itself (experts in
+        // ascending order, one job each); counts / offsets / active are not written.
+        if (warp == 0) {
+            const int K = p.top_k, e = sel - p.e_lo;
+            const bool res = lane < K && e >= 0 && e < p.e_local;
+            int pos = 0;
+            for (int j = 0; j < K; ++j) {
+                const int ej = __shfl_sync(kFull, e, j);
+                const bool rj = __shfl_sync(kFull, (int)res, j) != 0;
+                pos += rj && ej < e;
+            }
+            const int nres = __popc(__ballot_sync(kFull, res));
+            if (res) {
+                d.slots[pos] = make_int4(e, pos, 1, 0);
+                d.job_token[pos] = 0;
+                d.job_rank[pos] = lane;
+            }
+            if (lane >= nres && lane < min(p.e_local, K)) d.slots[lane] = make_int4(-1, 0, 0, 0);
+            if (lane == 0) d.n_active[0] = nres;
+        }
+        return;
+    }
     if (gridDim.y > 1) {
         __threadfence();
         __syncthreads();
@@ -370,6 +423,7 @@ struct Staged {
     const uint4 *q;
     const float *sc;
     const int *flag;
+    int scs;  // scale stride per job
 };
 
 template <int MT>
@@ -538,6 +592,7 @@ __device__ __forceinline__ Staged staged_view(uint8_t *smem, int mt, int nb) {
     s.q = reinterpret_cast<const uint4 *>(smem);
     s.sc = reinterpret_cast<const float *>(smem + (size_t)mt * nb * 64);
     s.flag = reinterpret_cast<const int *>(smem + (size_t)mt * nb * 68);
+    s.scs = nb;
     return s;
 }
 
@@ -783,6 +838,429 @@ __global__ void __launch_bounds__(W * 32) k_gemv(GemvParams p, GemvSrc src, Disp
 }
 
 // ============================================================================
+// MXFP4 expert GEMVs (4 threads per row).
+//
+// A row is shared by four threads: block chain h (even / odd blocks, the
+// reference's two FMA chains) x lane half lh (int lanes 0-3 = the low-nibble
+// elements 4p..4p+3, or lanes 4-7 = the high-nibble elements 16+4p..16+4p+3).
+// A warp holds 16 rows x 2 chains of one lane half; a row group of 16 rows is a
+// warp pair.  Per block a thread loads 8 bytes (two words, each the selectors
+// of two of its lanes) and forms 4 lane sums with prmt + dp4a.  Chains meet by an
+// xor-16 shuffle, lane halves through shared memory, then the reference's
+// order t_i = l(i+4) + l(i), (t0 + t2) + (t1 + t3).
+// Code-plane chunk (row group, block pair) = 512 bytes: [lh][L = 16h + r][word0, word1],
+// word0 = sel(p0) | sel(p1) << 16, word1 = sel(p2) | sel(p3) << 16, sel(p) = the
+// four 4-bit codes of lane p of this lane half.
+// Staged activations per (job, block): 4 uint4 [lh*2 + q] =
+// {a(lh, 2q), -a(lh, 2q), a(lh, 2q+1), -a(lh, 2q+1)}, a(lh, p) = its 4 code bytes.
+// ============================================================================
+
+constexpr int kMxBatch = 8;  // block pairs per load batch
+
+struct MxBatch {
+    uint2 w[kMxBatch];
+    uint32_t e[kMxBatch / 4];
+};
+
+struct MxStream {
+    const uint2 *cp;
+    const uint32_t *ep;
+    int steps;
+    __device__ __forceinline__ void init(const uint8_t *codes, const uint8_t *scales, int nb, int lane, int lh) {
+        cp = reinterpret_cast<const uint2 *>(codes + lh * 256) + lane;
+        ep = reinterpret_cast<const uint32_t *>(scales) + lane;
+        steps = nb / 2;
+    }
+    template <bool GUARD>
+    __device__ __forceinline__ void load(int s0, MxBatch &b) const {
+#pragma unroll
+        for (int i = 0; i < kMxBatch; ++i)
+            if (!GUARD || s0 + i < steps) b.w[i] = __ldg(cp + (size_t)(s0 + i) * 64);
+#pragma unroll
+        for (int i = 0; i < kMxBatch / 4; ++i)
+            if (!GUARD || s0 + 4 * i < steps) b.e[i] = __ldg(ep + (size_t)((s0 >> 2) + i) * 32);
+    }
+};
+
+template <int MT>
+__device__ __forceinline__ void mx_half(uint2 wq, uint32_t e8, const uint4 *aq, const float *sc, int nb, int scs,
+                                        int m, float (&acc)[MT][4]) {
+    uint32_t pos[4], neg[4];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const uint32_t w = q ? wq.y : wq.x, n = w ^ 0x88888888u;
+        pos[2 * q] = prmt(kMagLo, kMagHi, w);
+        neg[2 * q] = prmt(kMagLo, kMagHi, n);
+        pos[2 * q + 1] = prmt(kMagLo, kMagHi, w >> 16);
+        neg[2 * q + 1] = prmt(kMagLo, kMagHi, n >> 16);
+    }
+    const float eh = e8m0_half(e8);
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+        if (t < m) {
+            const float d = __fmul_rn(sc[t * scs], eh);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const uint4 av = aq[(size_t)t * nb * 4 + q];
+                const int l0 = dp4a_ss(neg[2 * q], av.y, dp4a_ss(pos[2 * q], av.x, (int)kMagicI));
+                const int l1 = dp4a_ss(neg[2 * q + 1], av.w, dp4a_ss(pos[2 * q + 1], av.z, (int)kMagicI));
+                acc[t][2 * q] = __fmaf_rn(d, lane_sum(l0), acc[t][2 * q]);
+                acc[t][2 * q + 1] = __fmaf_rn(d, lane_sum(l1), acc[t][2 * q + 1]);
+            }
+        }
+    }
+}
+
+// acc[t][p] = lane lh*4+p of this thread's chain, over all blocks of the chain.
+template <int MT>
+__device__ __forceinline__ void mx_warp_dot(const MxStream &ws, MxBatch cur, int lh, const Staged &a, int nb, int m,
+                                            int lane, float (&acc)[MT][4]) {
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int l = 0; l < 4; ++l) acc[t][l] = 0.0f;
+    const int half = lane >> 4;
+    const uint4 *aq = a.q + half * 4 + lh * 2;  // block b = 2*pair + half: record (t*nb + b)*4
+    const float *sc = a.sc + half;
+    int s0 = 0;
+    for (; s0 + kMxBatch < ws.steps; s0 += kMxBatch) {  // full batches, next one in flight
+        MxBatch nxt;
+        if (s0 + 2 * kMxBatch <= ws.steps) ws.load<false>(s0 + kMxBatch, nxt);
+        else ws.load<true>(s0 + kMxBatch, nxt);
+#pragma unroll
+        for (int i = 0; i < kMxBatch; ++i)
+            mx_half<MT>(cur.w[i], (cur.e[i >> 2] >> (8 * (i & 3))) & 0xffu, aq + (size_t)(s0 + i) * 8,
+                        sc + 2 * (s0 + i), nb, a.scs, m, acc);
+        cur = nxt;
+    }
+#pragma unroll
+    for (int i = 0; i < kMxBatch; ++i)  // last (possibly partial) batch
+        if (s0 + i < ws.steps)
+            mx_half<MT>(cur.w[i], (cur.e[i >> 2] >> (8 * (i & 3))) & 0xffu, aq + (size_t)(s0 + i) * 8,
+                        sc + 2 * (s0 + i), nb, a.scs, m, acc);
+}
+
+// Staging by bulk copy of precomputed records: job t's records (nb * 64 bytes) and
+// scales (pad4(nb) floats) land at smem + t*nb*64 and at the scale area + t*pad4(nb).
+// Returns false (after flagging `err`) if the copies did not complete in time.
+__device__ __forceinline__ bool stage_mx_bulk(const uint8_t *rec, const float *rsc, const int *rows_s, int m, int nb,
+                                              uint8_t *smem, int mt, uint64_t *bar, uint32_t &phase, uint32_t *err) {
+    const int nbp = pad4(nb);
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(bar, (uint32_t)m * (uint32_t)(nb * 64 + nbp * 4));
+        for (int t = 0; t < m; ++t) {
+            bulk_g2s(smem + (size_t)t * nb * 64, rec + (size_t)rows_s[t] * nb * 64, nb * 64, bar);
+            bulk_g2s(smem + (size_t)mt * nb * 64 + (size_t)t * nbp * 4, rsc + (size_t)rows_s[t] * nbp, nbp * 4, bar);
+        }
+    }
+    const bool ok = mbar_wait_bounded(bar, phase, kWaitLimitCycles);
+    // one decision for the whole CTA, so that no thread leaves while others wait at a barrier
+    const bool failed = __syncthreads_or(!ok) != 0;
+    if (failed) {
+        if (threadIdx.x == 0) atomicOr(err, 1u);
+        mbar_wait_bounded(bar, phase, kWaitLimitCycles);  // let copies in flight land before leaving
+    }
+    phase ^= 1u;
+    return !failed;
+}
+
+__device__ __forceinline__ Staged staged_bulk_view(uint8_t *smem, int mt, int nb) {
+    Staged s;
+    s.q = reinterpret_cast<const uint4 *>(smem);
+    s.sc = reinterpret_cast<const float *>(smem + (size_t)mt * nb * 64);
+    s.flag = nullptr;
+    s.scs = pad4(nb);
+    return s;
+}
+
+__host__ __device__ constexpr size_t bulk_staged_bytes(int mt, int nb) { return (size_t)mt * nb * 64 + (size_t)mt * pad4(nb) * 4; }
+
+// Staging into the MXFP4 record layout from internal Q8 rows (lane-pair order).
+__device__ __forceinline__ void stage_mx_internal(const uint8_t *codes, const float *scales, const int *rows_s, int m,
+                                                  int nb, uint8_t *smem, int mt) {
+    uint4 *q = reinterpret_cast<uint4 *>(smem);
+    float *sc = reinterpret_cast<float *>(smem + (size_t)mt * nb * 64);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < m * nb * 4; i += blockDim.x) {
+        const int t = i / (nb * 4), r = i - t * nb * 4, b = r >> 2, lh = (r >> 1) & 1, qq = r & 1;
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(codes + ((size_t)rows_s[t] * nb + b) * 32);
+        const uint32_t a0 = __ldcg(src + (2 * qq) * 2 + lh), a1 = __ldcg(src + (2 * qq + 1) * 2 + lh);
+        q[((size_t)t * nb + b) * 4 + lh * 2 + qq] = make_uint4(a0, neg8x4(a0), a1, neg8x4(a1));
+    }
+#pragma unroll 2
+    for (int i = threadIdx.x; i < m * nb; i += blockDim.x) {
+        const int t = i / nb, b = i - t * nb;
+        sc[i] = __ldcg(scales + (size_t)rows_s[t] * nb + b);
+    }
+}
+
+// From ggml block_q8_0 rows (34-byte blocks).
+__device__ __forceinline__ void stage_mx_ggml(const uint8_t *ggml, const int *rows_s, int m, int nb, uint8_t *smem,
+                                              int mt) {
+    uint4 *q = reinterpret_cast<uint4 *>(smem);
+    float *sc = reinterpret_cast<float *>(smem + (size_t)mt * nb * 64);
+    for (int i = threadIdx.x; i < m * nb * 4; i += blockDim.x) {
+        const int t = i / (nb * 4), r = i - t * nb * 4, b = r >> 2, lh = (r >> 1) & 1, qq = r & 1;
+        const uint8_t *blk = ggml + ((size_t)rows_s[t] * nb + b) * 34 + 2 + lh * 16;
+        uint32_t a0 = 0, a1 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            a0 |= (uint32_t)blk[4 * (2 * qq) + k] << (8 * k);
+            a1 |= (uint32_t)blk[4 * (2 * qq + 1) + k] << (8 * k);
+        }
+        q[((size_t)t * nb + b) * 4 + lh * 2 + qq] = make_uint4(a0, neg8x4(a0), a1, neg8x4(a1));
+    }
+    for (int i = threadIdx.x; i < m * nb; i += blockDim.x) {
+        const int t = i / nb, b = i - t * nb;
+        const uint8_t *blk = ggml + ((size_t)rows_s[t] * nb + b) * 34;
+        sc[i] = f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+    }
+}
+
+// From fp32 rows, quantized here with the x86 Q8_0 rule (one warp per 32-value block).
+__device__ __forceinline__ void stage_mx_f32(const float *f32, int cols, const int *rows_s, int m, int nb,
+                                             uint8_t *smem, int mt) {
+    constexpr int U = 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float *sc = reinterpret_cast<float *>(smem + (size_t)mt * nb * 64);
+    // element `lane` of a block: lane half lh = lane/16, lane p = (lane%16)/4, byte j = lane%4
+    const int off = ((lane >> 4) * 2 + ((lane & 15) >> 3)) * 16 + (((lane & 15) >> 2) & 1) * 8 + (lane & 3);
+    for (int i0 = warp; i0 < m * nb; i0 += nw * U) {
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = i0 + u * nw;
+            if (i < m * nb) {
+                const int t = i / nb, b = i - t * nb;
+                v[u] = __ldcg(f32 + (size_t)rows_s[t] * cols + b * 32 + lane);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = i0 + u * nw;
+            if (i < m * nb) {
+                const float amax = warp_max(fabsf(v[u]));
+                const float inv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                uint8_t *rec = smem + (size_t)i * 64;
+                rec[off] = (uint8_t)(int8_t)q8_code(v[u], inv);
+                __syncwarp();
+                if (lane < 8) {  // word k: lane half k/4, lane p = k%4
+                    uint32_t *wa = reinterpret_cast<uint32_t *>(rec + ((lane >> 2) * 2 + ((lane & 3) >> 1)) * 16 + (lane & 1) * 8);
+                    wa[1] = neg8x4(wa[0]);
+                }
+                if (lane == 0) sc[i] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+                __syncwarp();
+            }
+        }
+    }
+}
+
+// Completes rows from the four partial lane sets: v = chain-combined lanes of this
+// thread's half.  Returns the row dot on lanes < 16 of the lh = 0 warp.
+template <int MT>
+__device__ __forceinline__ void mx_chain_combine(float (&acc)[MT][4]) {
+#pragma unroll
+    for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) acc[t][p] = __fadd_rn(acc[t][p], __shfl_xor_sync(kFull, acc[t][p], 16));
+}
+
+__device__ __forceinline__ float mx_row_total(const float (&lo)[4], const float *hi) {
+    const float t0 = __fadd_rn(hi[0], lo[0]), t1 = __fadd_rn(hi[1], lo[1]);
+    const float t2 = __fadd_rn(hi[2], lo[2]), t3 = __fadd_rn(hi[3], lo[3]);
+    return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+}
+
+// gate_up for MXFP4: a CTA computes 16 intermediate values (warps: gate lh0, gate
+// lh1, up lh0, up lh1) for every job of one expert and writes the activated fp32
+// values; the down kernel quantizes them.  grid = (I/16, slots).
+template <int MT>
+__global__ void __launch_bounds__(128) k_gate_up_mx(GateUpParams p, Dispatch d) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float xch[MT][2][16][4];
+    __shared__ float res[MT][2][16];
+    __shared__ int rows_s[MT], last_s[MT];
+    __shared__ __align__(8) uint64_t bar;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int4 rec = __ldcg(d.slots + blockIdx.y);
+    const int e = rec.x;
+    if (e < 0) return;
+    const int seg = rec.y, cnt = rec.z;
+    const int H = p.hidden, I = p.intermediate, nb = H / 32, nbI = I / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int half = warp >> 1, lh = warp & 1;
+    const Matrix &mat = p.fused ? p.gate_up : (half ? p.up : p.gate);
+    const int nrg = mat.rows / 16;
+    const int rg = p.fused ? half * (I / 16) + blockIdx.x : blockIdx.x;
+    MxStream ws;
+    ws.init(mat.codes + code_offset(UMSX_QUANT_MXFP4, e, nrg, rg, nb),
+            mat.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, rg, nb), nb, lane, lh);
+    MxBatch first;
+    ws.load<true>(0, first);  // weights stream while the activations are copied in
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    uint32_t phase = 0;
+    const int r = lane & 15;
+    const float bias = p.bias ? __ldg(p.bias + (size_t)e * 2 * I + half * I + blockIdx.x * 16 + r) : 0.0f;
+    const Staged st = staged_bulk_view(smem, MT, nb);
+    for (int c0 = 0; c0 < cnt; c0 += MT) {
+        const int m = min(MT, cnt - c0);
+        if (c0 > 0) ws.load<true>(0, first);
+        __syncthreads();
+        if (threadIdx.x < m) rows_s[threadIdx.x] = __ldcg(d.job_token + seg + c0 + threadIdx.x);
+        __syncthreads();
+        if (!stage_mx_bulk(d.xr, d.xr_sc, rows_s, m, nb, smem, MT, &bar, phase, d.err)) return;
+        float acc[MT][4];
+        mx_warp_dot<MT>(ws, first, lh, st, nb, m, lane, acc);
+        mx_chain_combine<MT>(acc);
+        if (lh == 1 && lane < 16)
+#pragma unroll
+            for (int t = 0; t < MT; ++t)
+                if (t < m)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) xch[t][half][r][q] = acc[t][q];
+        __syncthreads();
+        if (lh == 0 && lane < 16)
+#pragma unroll
+            for (int t = 0; t < MT; ++t)
+                if (t < m) res[t][half][r] = __fadd_rn(mx_row_total(acc[t], xch[t][half][r]), bias);
+        __syncthreads();
+        for (int i = threadIdx.x; i < m * 16; i += blockDim.x) {
+            const int t = i >> 4, k = i & 15;
+            const float g = res[t][0][k], u = res[t][1][k];
+            const float a = p.activation == UMSX_ACT_SWIGLU_OAI ? swiglu_oai(g, u, p.alpha, p.limit) : silu_mul(g, u);
+            p.act_f32[(size_t)(seg + c0 + t) * I + blockIdx.x * 16 + k] = a;
+        }
+        // The two CTAs of a 32-value block: the one finishing second quantizes it
+        // into the down kernel's staging record.  No CTA waits for the other.
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x < m) {
+            const unsigned prev = atomicAdd(p.act_done + (size_t)(seg + c0 + threadIdx.x) * nbI + (blockIdx.x >> 1), 1u);
+            last_s[threadIdx.x] = prev == 1u;
+        }
+        __syncthreads();
+        for (int t = warp; t < m; t += 4) {
+            if (!last_s[t]) continue;
+            __threadfence();
+            const size_t job = (size_t)(seg + c0 + t), blk = blockIdx.x >> 1;
+            const float a = __ldcg(p.act_f32 + job * I + blk * 32 + lane);
+            const float amax = warp_max(fabsf(a));
+            const float qinv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            write_mx_record(q8_code(a, qinv), p.act_rec + (job * nbI + blk) * 64, lane);
+            if (lane == 0) {
+                p.act_sc[job * pad4(nbI) + blk] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+                p.act_done[job * nbI + blk] = 0;
+            }
+        }
+    }
+}
+
+// Generic MXFP4 GEMV: W row groups (2W warps) of one expert; grid = (N/(16W), slots).
+// Sources as k_gemv: 0 internal Q8, 1 ggml block_q8_0, 2 fp32 (quantized here).
+template <int W, int MT, int SRC, int COMBINE>
+__global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, Dispatch d) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float xch[MT][W][16][4];
+    __shared__ int rows_s[MT], outs_s[MT], last_s[MT];
+    __shared__ __align__(8) uint64_t bar;
+    if (!p.prefetch_early) {
+        pdl_wait();
+        pdl_launch_dependents();
+    }
+    const int4 rec = __ldcg(d.slots + blockIdx.y);
+    const int e = rec.x;
+    if (e < 0) return;
+    const int seg = rec.y, cnt = rec.z;
+    const int N = p.m.rows, nb = p.m.cols / 32, nrg = N / 16;
+    uint32_t phase = 0;
+    if (SRC == 3 && threadIdx.x == 0) mbar_init(&bar, 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rgl = warp >> 1, lh = warp & 1;
+    const int rg = blockIdx.x * W + rgl;
+    const bool active_rg = rg < nrg;
+    MxStream ws;
+    ws.init(p.m.codes + code_offset(UMSX_QUANT_MXFP4, e, nrg, active_rg ? rg : 0, nb),
+            p.m.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, active_rg ? rg : 0, nb), nb, lane, lh);
+    MxBatch first;
+    if (active_rg) ws.load<true>(0, first);
+    if (p.prefetch_early) {  // the weights were chosen two kernels back; the activations come from the last one
+        pdl_wait();
+        pdl_launch_dependents();
+    }
+    const int r = lane & 15;
+    const int n = rg * 16 + r;
+    const float bias = (p.bias && active_rg) ? __ldg(p.bias + (size_t)e * N + n) : 0.0f;
+    const Staged st = SRC == 3 ? staged_bulk_view(smem, MT, nb) : staged_view(smem, MT, nb);
+    for (int c0 = 0; c0 < cnt; c0 += MT) {
+        const int m = min(MT, cnt - c0);
+        if (c0 > 0 && active_rg) ws.load<true>(0, first);
+        __syncthreads();
+        if (threadIdx.x < m) {
+            const int j = seg + c0 + threadIdx.x;
+            const int tok = __ldcg(d.job_token + j), rank = __ldcg(d.job_rank + j);
+            rows_s[threadIdx.x] = p.a_by_job ? j : tok * p.a_ts + rank * p.a_rs;
+            outs_s[threadIdx.x] = tok * p.o_ts + rank;
+        }
+        __syncthreads();
+        if constexpr (SRC == 0) stage_mx_internal(src.q8_codes, src.q8_scales, rows_s, m, nb, smem, MT);
+        else if constexpr (SRC == 1) stage_mx_ggml(src.ggml, rows_s, m, nb, smem, MT);
+        else if constexpr (SRC == 2) stage_mx_f32(src.f32, p.m.cols, rows_s, m, nb, smem, MT);
+        else if (!stage_mx_bulk(p.a_rec, p.a_rsc, rows_s, m, nb, smem, MT, &bar, phase, d.err)) return;
+        __syncthreads();
+        float acc[MT][4];
+        if (active_rg) {
+            mx_warp_dot<MT>(ws, first, lh, st, nb, m, lane, acc);
+            mx_chain_combine<MT>(acc);
+            if (lh == 1 && lane < 16)
+#pragma unroll
+                for (int t = 0; t < MT; ++t)
+                    if (t < m)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) xch[t][rgl][r][q] = acc[t][q];
+        }
+        __syncthreads();
+        if (active_rg && lh == 0 && lane < 16) {
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+                if (t < m) {
+                    float v = mx_row_total(acc[t], xch[t][rgl][r]);
+                    if (p.bias) v = __fadd_rn(v, bias);
+                    p.out[(size_t)outs_s[t] * N + n] = v;
+                }
+            }
+        }
+        if constexpr (COMBINE) {
+            // Rank-order combine (+ residual) of this CTA's rows, done by whichever of the
+            // K expert CTAs of a token finishes last: no CTA waits for another.
+            __threadfence();
+            __syncthreads();
+            if (threadIdx.x < m) {
+                const int tok = outs_s[threadIdx.x] / p.top_k;
+                const unsigned prev = atomicAdd(p.tile_done + (size_t)tok * gridDim.x + blockIdx.x, 1u);
+                last_s[threadIdx.x] = prev == (unsigned)(p.top_k - 1) ? tok : -1;
+            }
+            __syncthreads();
+            for (int t = 0; t < m; ++t) {
+                const int tok = last_s[t];
+                if (tok < 0) continue;
+                __threadfence();
+                const int K = p.top_k, n0 = blockIdx.x * W * 16;
+                for (int i = threadIdx.x; i < W * 16 && n0 + i < N; i += blockDim.x) {
+                    float acc2 = 0.0f;
+                    for (int rr = 0; rr < K; ++rr)
+                        acc2 = __fadd_rn(acc2, __fmul_rn(__ldcg(p.route_w + (size_t)tok * K + rr),
+                                                         __ldcg(p.out + ((size_t)tok * K + rr) * N + n0 + i)));
+                    if (p.residual) acc2 = __fadd_rn(p.residual[(size_t)tok * N + n0 + i], acc2);
+                    p.combine_out[(size_t)tok * N + n0 + i] = acc2;
+                }
+                if (threadIdx.x == 0) p.tile_done[(size_t)tok * gridDim.x + blockIdx.x] = 0;
+            }
+        }
+    }
+}
+
+// ============================================================================
 // Combine: out[t][i] = ((0 + w0*y0) + w1*y1) + ... (expert_dispatch.cpp:77-87).
 // ============================================================================
 
@@ -829,22 +1307,29 @@ __global__ void k_layout(Matrix m, int expert, uint8_t *ggml) {
         uint8_t *blk = ggml + i * bb;
         if (mx) {
             const int np = nb / 2, nq = (np + 3) / 4, bp = b >> 1, h = b & 1, L = h * 16 + r;
-            uint32_t *words = reinterpret_cast<uint32_t *>(m.codes + (((size_t)expert * nrg + rg) * np + bp) * 512 + L * 16);
+            uint8_t *chunk = m.codes + (((size_t)expert * nrg + rg) * np + bp) * 512;
             uint8_t *ex = m.scales + (((size_t)expert * nrg + rg) * nq + (bp >> 2)) * 128 + L * 4 + (bp & 3);
             if (TO_TILE) *ex = blk[0]; else blk[0] = *ex;
-            for (int pp = 0; pp < 4; ++pp) {
-                if (TO_TILE) {
-                    uint32_t v = 0;
-                    for (int q = 0; q < 4; ++q) {
-                        const uint32_t byte = blk[1 + 4 * pp + q];
-                        v |= (byte & 15u) << (4 * q);
-                        v |= (byte >> 4) << (16 + 4 * q);
+            for (int lh = 0; lh < 2; ++lh) {
+                uint32_t *words = reinterpret_cast<uint32_t *>(chunk + lh * 256 + L * 8);
+                for (int w = 0; w < 2; ++w) {
+                    if (TO_TILE) {
+                        uint32_t v = 0;
+                        for (int pp = 0; pp < 2; ++pp)
+                            for (int q = 0; q < 4; ++q) {
+                                const uint32_t byte = blk[1 + 4 * (2 * w + pp) + q];
+                                v |= (lh ? (byte >> 4) : (byte & 15u)) << (16 * pp + 4 * q);
+                            }
+                        words[w] = v;
+                    } else {
+                        const uint32_t v = words[w];
+                        for (int pp = 0; pp < 2; ++pp)
+                            for (int q = 0; q < 4; ++q) {
+                                const uint32_t code = (v >> (16 * pp + 4 * q)) & 15u;
+                                uint8_t &byte = blk[1 + 4 * (2 * w + pp) + q];
+                                byte = lh ? (uint8_t)((byte & 15u) | (code << 4)) : (uint8_t)((byte & 0xf0u) | code);
+                            }
                     }
-                    words[pp] = v;
-                } else {
-                    const uint32_t v = words[pp];
-                    for (int q = 0; q < 4; ++q)
-                        blk[1 + 4 * pp + q] = (uint8_t)(((v >> (4 * q)) & 15u) | (((v >> (16 + 4 * q)) & 15u) << 4));
                 }
             }
         } else {
@@ -911,6 +1396,10 @@ __global__ void k_bf16_to_f32(const uint16_t *in, float *out, size_t n) {
 // Launchers
 // ============================================================================
 
+// Dynamic shared memory plus a kernel's static shared memory (at most this much here) above
+// 48 KiB needs the per-kernel opt-in.
+constexpr size_t kStaticSmemMargin = 8192;
+
 static inline int grid_for(size_t n, int threads, int cap = 148 * 16) {
     size_t g = (n + threads - 1) / threads;
     if (g < 1) g = 1;
@@ -958,18 +1447,34 @@ static void gate_up_mt(const GateUpParams &p, const Dispatch &d, int slots, cuda
     const int nb = p.hidden / 32;
     const size_t smem = staged_bytes(MT, nb);
     auto kern = k_gate_up<QUANT, MT>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem + kStaticSmemMargin > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     launch_pdl(kern, dim3(p.intermediate / 32, slots), dim3(64 * Geo<QUANT>::kChains), smem, s, p, d);
+}
+
+template <int MT>
+static void gate_up_mx_mt(const GateUpParams &p, const Dispatch &d, int slots, cudaStream_t s) {
+    const int nb = p.hidden / 32;
+    const size_t smem = bulk_staged_bytes(MT, nb);
+    auto kern = k_gate_up_mx<MT>;
+    if (smem + kStaticSmemMargin > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    launch_pdl(kern, dim3(p.intermediate / 16, slots), dim3(128), smem, s, p, d);
 }
 
 int launch_gate_up(const GateUpParams &p, const Dispatch &d, int slots, int max_per_expert, cudaStream_t s) {
     const int q = p.fused ? p.gate_up.quant : p.gate.quant;
+    if (q == UMSX_QUANT_MXFP4) {
+        if (max_per_expert <= 1) gate_up_mx_mt<1>(p, d, slots, s);
+        else if (max_per_expert <= 2) gate_up_mx_mt<2>(p, d, slots, s);
+        else if (max_per_expert <= 4) gate_up_mx_mt<4>(p, d, slots, s);
+        else gate_up_mx_mt<8>(p, d, slots, s);
+        return 1;
+    }
 #define UMSX_GU(QQ)                                                          \
     if (max_per_expert <= 1) gate_up_mt<QQ, 1>(p, d, slots, s);             \
     else if (max_per_expert <= 2) gate_up_mt<QQ, 2>(p, d, slots, s);        \
     else if (max_per_expert <= 4) gate_up_mt<QQ, 4>(p, d, slots, s);        \
     else gate_up_mt<QQ, 8>(p, d, slots, s);
-    if (q == UMSX_QUANT_MXFP4) { UMSX_GU(UMSX_QUANT_MXFP4) } else { UMSX_GU(UMSX_QUANT_Q8_0) }
+    UMSX_GU(UMSX_QUANT_Q8_0)
 #undef UMSX_GU
     return 1;
 }
@@ -980,13 +1485,32 @@ static void gemv_mt(const GemvParams &p, const GemvSrc &src, const Dispatch &d, 
     const int nb = p.m.cols / 32;
     const size_t smem = staged_bytes(MT, nb);
     auto kern = k_gemv<QUANT, W, MT, SRC, COMBINE>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem + kStaticSmemMargin > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int tiles = (p.m.rows / Geo<QUANT>::kRowsPerWarp + W - 1) / W;
     launch_pdl(kern, dim3(tiles, slots), dim3(W * 32), smem, s, p, src, d);
 }
 
+template <int MT, int SRC, int COMBINE>
+static void gemv_mx_mt(const GemvParams &p, const GemvSrc &src, const Dispatch &d, int slots, cudaStream_t s) {
+    constexpr int W = 2;
+    const int nb = p.m.cols / 32;
+    const size_t smem = SRC == 3 ? bulk_staged_bytes(MT, nb) : staged_bytes(MT, nb);
+    auto kern = k_gemv_mx<W, MT, SRC, COMBINE>;
+    if (smem + kStaticSmemMargin > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int tiles = (p.m.rows / 16 + W - 1) / W;
+    launch_pdl(kern, dim3(tiles, slots), dim3(W * 64), smem, s, p, src, d);
+}
+
 template <int QUANT, int SRC, int COMBINE>
 static void gemv_src(const GemvParams &p, const GemvSrc &src, const Dispatch &d, int slots, int mpe, cudaStream_t s) {
+    if constexpr (QUANT == UMSX_QUANT_MXFP4) {
+        if (mpe <= 1) gemv_mx_mt<1, SRC, COMBINE>(p, src, d, slots, s);
+        else if (mpe <= 2) gemv_mx_mt<2, SRC, COMBINE>(p, src, d, slots, s);
+        else if (mpe <= 4) gemv_mx_mt<4, SRC, COMBINE>(p, src, d, slots, s);
+        else gemv_mx_mt<8, SRC, COMBINE>(p, src, d, slots, s);
+        return;
+    }
+    if constexpr (SRC == 3) return;  // records exist for MXFP4 only
     if (mpe <= 1) gemv_mt<QUANT, 1, SRC, COMBINE>(p, src, d, slots, s);
     else if (mpe <= 2) gemv_mt<QUANT, 2, SRC, COMBINE>(p, src, d, slots, s);
     else if (mpe <= 4) gemv_mt<QUANT, 4, SRC, COMBINE>(p, src, d, slots, s);
@@ -995,31 +1519,25 @@ static void gemv_src(const GemvParams &p, const GemvSrc &src, const Dispatch &d,
 
 int launch_gemv(const GemvParams &p, const Dispatch &d, int slots, int max_per_expert, cudaStream_t s) {
     GemvSrc src{};
+    src.q8_codes = p.a_codes;
+    src.q8_scales = p.a_scales;
     src.ggml = p.a_q8;
     src.f32 = p.a_f32;
-    const bool ggml = p.a_q8 != nullptr;
+    const int mode = p.a_q8 ? 1 : (p.a_f32 ? 2 : (p.a_rec ? 3 : 0));
+    const bool comb = p.tile_done != nullptr;
+#define UMSX_GV(QQ)                                                                          \
+    if (mode == 0) { if (comb) gemv_src<QQ, 0, 1>(p, src, d, slots, max_per_expert, s);        \
+                     else gemv_src<QQ, 0, 0>(p, src, d, slots, max_per_expert, s); }          \
+    else if (mode == 1) gemv_src<QQ, 1, 0>(p, src, d, slots, max_per_expert, s);              \
+    else { if (comb) gemv_src<QQ, 2, 1>(p, src, d, slots, max_per_expert, s);                  \
+           else gemv_src<QQ, 2, 0>(p, src, d, slots, max_per_expert, s); }
     if (p.m.quant == UMSX_QUANT_MXFP4) {
-        if (ggml) gemv_src<UMSX_QUANT_MXFP4, 1, 0>(p, src, d, slots, max_per_expert, s);
-        else gemv_src<UMSX_QUANT_MXFP4, 2, 0>(p, src, d, slots, max_per_expert, s);
-    } else {
-        if (ggml) gemv_src<UMSX_QUANT_Q8_0, 1, 0>(p, src, d, slots, max_per_expert, s);
-        else gemv_src<UMSX_QUANT_Q8_0, 2, 0>(p, src, d, slots, max_per_expert, s);
-    }
-    return 1;
-}
-
-int launch_gemv_internal(const GemvParams &p, const uint8_t *codes, const float *scales, const Dispatch &d,
-                         int slots, int max_per_expert, cudaStream_t s) {
-    GemvSrc src{};
-    src.q8_codes = codes;
-    src.q8_scales = scales;
-    if (p.tile_done) {
-        if (p.m.quant == UMSX_QUANT_MXFP4) gemv_src<UMSX_QUANT_MXFP4, 0, 1>(p, src, d, slots, max_per_expert, s);
-        else gemv_src<UMSX_QUANT_Q8_0, 0, 1>(p, src, d, slots, max_per_expert, s);
-    } else {
-        if (p.m.quant == UMSX_QUANT_MXFP4) gemv_src<UMSX_QUANT_MXFP4, 0, 0>(p, src, d, slots, max_per_expert, s);
-        else gemv_src<UMSX_QUANT_Q8_0, 0, 0>(p, src, d, slots, max_per_expert, s);
-    }
+        if (mode == 3) {  // staging records, only the MXFP4 layer path produces them
+            if (comb) gemv_src<UMSX_QUANT_MXFP4, 3, 1>(p, src, d, slots, max_per_expert, s);
+            else gemv_src<UMSX_QUANT_MXFP4, 3, 0>(p, src, d, slots, max_per_expert, s);
+        } else { UMSX_GV(UMSX_QUANT_MXFP4) }
+    } else { UMSX_GV(UMSX_QUANT_Q8_0) }
+#undef UMSX_GV
     return 1;
 }
 
