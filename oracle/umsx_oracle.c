@@ -299,8 +299,8 @@ void orc_route(int routing, int experts, int top_k, int hidden, float routed_sca
         for (int e = 0; e < experts; ++e) {
             float l = orc_logit(router_w + (size_t)e * hidden, xt, hidden);
             if (router_b) l = l + router_b[e];
-            logits[e] = l;
             if (logits_out) logits_out[(size_t)t * experts + e] = l;
+            logits[e] = l != l ? -INFINITY : l;  /* NaN ranks lowest: every pick is a valid expert */
         }
         int32_t *sel = ids + (size_t)t * top_k;
         float *wt = weights + (size_t)t * top_k;

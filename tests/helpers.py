@@ -65,3 +65,14 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
 
 def x_bits(orc, cfg, tokens: int, stream: int = 0xFFFF0, sigma: float = 1.0) -> np.ndarray:
     return orc.gen_normal_bf16(cfg.seed, stream, 0, tokens * cfg.hidden, sigma).reshape(tokens, cfg.hidden)
+
+
+def bits(a) -> np.ndarray:
+    """fp32 values as their bit patterns (bit-exact comparisons)."""
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def to_cuda_bf16(xb: np.ndarray):
+    """bf16 bit patterns (uint16) -> a bf16 CUDA tensor."""
+    import torch
+    return torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).cuda()

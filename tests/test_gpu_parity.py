@@ -8,20 +8,13 @@ import os
 import numpy as np
 import pytest
 
-from tests.helpers import U, bf16_bits_to_f32, host_weights, oracle_desc, small_config, weights_dict, x_bits
+from tests.helpers import (U, bf16_bits_to_f32, bits, host_weights, oracle_desc, small_config, to_cuda_bf16,
+                           weights_dict, x_bits)
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-
-
-def bits(a):
-    return np.ascontiguousarray(a, np.float32).view(np.uint32)
-
-
-def to_cuda_bf16(xb):
-    return torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).cuda()
 
 
 def down_only_layer(down_blocks, hidden, inter, experts, quant=U.QUANT_MXFP4, down_bias=None):

@@ -111,3 +111,15 @@ def test_dequant_matches_gguf(oracle, seed):
     got = oracle.dequant(8, q8, 256 * 32)
     ref = dequantize(q8.reshape(1, -1), QT.Q8_0).reshape(-1).astype(np.float32)
     np.testing.assert_array_equal(bits(got), bits(ref))
+
+
+def test_oracle_nan_logits_pick_lowest_experts(oracle):
+    """NaN logits rank lowest: a token whose logits are all NaN goes to experts 0..k-1."""
+    from tests.helpers import host_weights, oracle_desc, small_config
+    cfg = small_config()
+    w = host_weights(oracle, cfg)
+    x = np.ones((2, cfg.hidden), np.float32)
+    x[0, 5] = np.nan
+    ids, _, _ = oracle.route(oracle_desc(cfg), w, x)
+    np.testing.assert_array_equal(ids[0], np.arange(cfg.top_k))
+    assert ((ids[1] >= 0) & (ids[1] < cfg.experts)).all()

@@ -80,6 +80,7 @@ struct Workspace {
     float *y = nullptr;
     void *x_dev = nullptr;
     float *out_dev = nullptr;
+    unsigned *bar = nullptr;  // grid barrier counter of the persistent decode kernel
     uint8_t *mem = nullptr;
     int max_tokens = 0;
 };
@@ -188,6 +189,7 @@ void carve_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_
     w.y = a.take<float>(T * K * H);
     w.x_dev = a.take<float>(T * H);
     w.out_dev = a.take<float>(T * H);
+    w.bar = a.take<unsigned>(1);
     w.max_tokens = max_tokens;
 }
 
@@ -421,6 +423,83 @@ umsx_status mark(cudaEvent_t ev, cudaStream_t s) {
     return UMSX_OK;
 }
 
+// The persistent decode kernel serves a call when every layer is an MXFP4
+// fused-gate_up layer with all experts local and the token count is small.
+bool decode_eligible(const umsx_moe *m, int tokens, int n_layers) {
+    const auto &d = m->d;
+    return d.quant == UMSX_QUANT_MXFP4 && d.fused_gate_up && m->e_local == d.experts &&
+           decode_supported(tokens, d.hidden, d.intermediate, d.experts, d.top_k, n_layers);
+}
+
+DecodeLayer decode_layer(const umsx_moe *m) {
+    DecodeLayer L{};
+    L.router_w = m->router_w;
+    L.router_b = m->router_b;
+    L.gu_codes = m->gate_up.codes;
+    L.gu_scales = m->gate_up.scales;
+    L.gu_bias = m->gu_bias;
+    L.dn_codes = m->down.codes;
+    L.dn_scales = m->down.scales;
+    L.dn_bias = m->down_bias;
+    return L;
+}
+
+DecodeParams decode_params(const umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out) {
+    const auto &d = m->d;
+    DecodeParams p{};
+    p.n_layers = 1;
+    p.layer[0] = decode_layer(m);
+    p.tokens = tokens;
+    p.hidden = d.hidden;
+    p.inter = d.intermediate;
+    p.experts = d.experts;
+    p.top_k = d.top_k;
+    p.routing = d.routing;
+    p.activation = d.activation;
+    p.routed_scale = d.routed_scale;
+    p.alpha = d.swiglu_alpha;
+    p.limit = d.swiglu_limit;
+    p.x = x;
+    p.x_dtype = x_dtype;
+    p.out = out;
+    p.logits = ws.disp.logits;
+    p.act = ws.act_f32;
+    p.y = ws.y;
+    p.xr = ws.disp.xr;
+    p.xr_sc = ws.disp.xr_sc;
+    p.act_rec = ws.act_rec;
+    p.act_sc = ws.act_sc;
+    p.act_done = ws.act_done;
+    p.bar = ws.bar;
+    p.err = ws.disp.err;
+    return p;
+}
+
+// Launches the persistent kernel; false if this device cannot hold it resident
+// (the caller then takes the per-stage path).
+bool try_decode(const DecodeParams &p, cudaStream_t s) {
+    if (launch_decode(p, s) < 0) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    g_launches += 1;
+    return true;
+}
+
+// Reads and clears the device error flag after a synchronised call.
+umsx_status check_device_flag(Workspace &ws, cudaStream_t s) {
+    uint32_t flag = 0;
+    UMSX_CUDA(cudaMemcpyAsync(&flag, ws.disp.err, 4, cudaMemcpyDeviceToHost, s));
+    UMSX_CUDA(cudaStreamSynchronize(s));
+    if (!flag) return UMSX_OK;
+    UMSX_CUDA(cudaMemsetAsync(ws.disp.err, 0, 4, s));
+    UMSX_CUDA(cudaStreamSynchronize(s));
+    return fail(UMSX_ETIMEOUT, "a bounded device wait gave up (flag " + std::to_string(flag) + ")");
+}
+
+// One layer, out = MoE(x): the persistent kernel for small T, else the per-stage kernels.
+umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, float *out, cudaStream_t s);
+
 // router -> gate_up (+act, +Q8_0) -> down -> combine (+ optional residual).
 // ev: null or 5 events bracketing the four stages.
 umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
@@ -476,6 +555,16 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     return UMSX_OK;
 }
 
+umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, float *out, cudaStream_t s) {
+    if (decode_eligible(m, tokens, 1)) {
+        DecodeParams p = decode_params(m, m->ws, x, x_dtype, tokens, out);
+        p.ids_out = m->ws.disp.ids;
+        p.w_out = m->ws.disp.weights;
+        if (try_decode(p, s)) return UMSX_OK;
+    }
+    return run_layer(m, m->ws, x, x_dtype, tokens, out, nullptr, 0, 0.0f, s, nullptr);
+}
+
 }  // namespace
 
 extern "C" {
@@ -487,7 +576,7 @@ umsx_status umsx_moe_forward(umsx_moe *m, const void *x, int x_dtype, int tokens
     std::lock_guard<std::mutex> lock(m->mu);
     UMSX_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (umsx_status st = run_layer(m, m->ws, x, x_dtype, tokens, out, nullptr, 0, 0.0f, s, nullptr)) return st;
+    if (umsx_status st = forward_layer(m, x, x_dtype, tokens, out, s)) return st;
     const size_t n = (size_t)tokens * m->d.top_k;
     if (ids) UMSX_CUDA(cudaMemcpyAsync(ids, m->ws.disp.ids, n * 4, cudaMemcpyDeviceToDevice, s));
     if (weights) UMSX_CUDA(cudaMemcpyAsync(weights, m->ws.disp.weights, n * 4, cudaMemcpyDeviceToDevice, s));
@@ -503,11 +592,9 @@ umsx_status umsx_moe_forward_host(umsx_moe *m, const void *x, int x_dtype, int t
     const size_t in_bytes = (size_t)tokens * m->d.hidden * (x_dtype == UMSX_DTYPE_BF16 ? 2 : 4);
     const size_t out_bytes = (size_t)tokens * m->d.hidden * 4;
     UMSX_CUDA(cudaMemcpyAsync(m->ws.x_dev, x, in_bytes, cudaMemcpyHostToDevice, s));
-    if (umsx_status st = run_layer(m, m->ws, m->ws.x_dev, x_dtype, tokens, m->ws.out_dev, nullptr, 0, 0.0f, s, nullptr))
-        return st;
+    if (umsx_status st = forward_layer(m, m->ws.x_dev, x_dtype, tokens, m->ws.out_dev, s)) return st;
     UMSX_CUDA(cudaMemcpyAsync(out, m->ws.out_dev, out_bytes, cudaMemcpyDeviceToHost, s));
-    UMSX_CUDA(cudaStreamSynchronize(s));
-    return UMSX_OK;
+    return check_device_flag(m->ws, s);
 }
 
 umsx_status umsx_route(umsx_moe *m, const void *x, int x_dtype, int tokens, int32_t *ids, float *weights,
@@ -705,13 +792,28 @@ umsx_status stack_run(umsx_stack *st, const void *x, int dtype, int tokens, void
                       cudaMemcpyKind out_kind, cudaStream_t caller) {
     const size_t in_bytes = (size_t)tokens * st->hidden * (dtype == UMSX_DTYPE_BF16 ? 2 : 4);
     const size_t out_bytes = (size_t)tokens * st->hidden * 4;
-    umsx_stack::Graph *g = nullptr;
-    if (umsx_status r = stack_graph(st, tokens, dtype, &g)) return r;
     UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
     UMSX_CUDA(cudaStreamWaitEvent(st->stream, st->ev_in, 0));
     UMSX_CUDA(cudaMemcpyAsync(st->ws.x_dev, x, in_bytes, in_kind, st->stream));
-    UMSX_CUDA(cudaGraphLaunch(g->exec, st->stream));
-    g_launches += g->kernels;
+    const int L = (int)st->layers.size();
+    bool done = false;
+    bool eligible = !st->timing;
+    for (int l = 0; l < L && eligible; ++l) eligible = decode_eligible(st->layers[l], tokens, L);
+    if (eligible) {
+        DecodeParams p = decode_params(st->layers[0], st->ws, st->ws.x_dev, dtype, tokens, st->h);
+        p.n_layers = L;
+        for (int l = 0; l < L; ++l) p.layer[l] = decode_layer(st->layers[l]);
+        p.rmsnorm = 1;
+        p.residual = 1;
+        p.eps = st->eps;
+        done = try_decode(p, st->stream);
+    }
+    if (!done) {
+        umsx_stack::Graph *g = nullptr;
+        if (umsx_status r = stack_graph(st, tokens, dtype, &g)) return r;
+        UMSX_CUDA(cudaGraphLaunch(g->exec, st->stream));
+        g_launches += g->kernels;
+    }
     UMSX_CUDA(cudaMemcpyAsync(out, st->h, out_bytes, out_kind, st->stream));
     UMSX_CUDA(cudaEventRecord(st->ev_out, st->stream));
     UMSX_CUDA(cudaStreamWaitEvent(caller, st->ev_out, 0));
@@ -788,8 +890,7 @@ umsx_status umsx_stack_forward_host(umsx_stack *st, const void *x, int x_dtype, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (umsx_status r = stack_run(st, x, x_dtype, tokens, out, cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost, s))
         return r;
-    UMSX_CUDA(cudaStreamSynchronize(s));
-    return UMSX_OK;
+    return check_device_flag(st->ws, s);
 }
 
 umsx_status umsx_stack_set_timing(umsx_stack *st, int enable) {

@@ -1,0 +1,499 @@
+// Persistent decode kernel: a whole stack of MoE layers (or one layer) for a few
+// tokens in ONE cooperative launch with one CTA per SM.
+//
+// Per layer, between grid-wide barriers:
+//   R  every CTA folds the previous layer's expert outputs into its own copy of
+//      the residual stream h (rank order, tools/engine/expert_dispatch.cpp:77-87),
+//      normalises it (RMSNorm, unit weight) and quantizes it to Q8_0 records;
+//      CTA c computes the router logits of experts c, c + #CTAs, ...
+//   S  every CTA selects the top-k experts of every token from the logits itself
+//      (identical inputs and code, so identical choices) and builds the slot list
+//      (distinct experts, ascending) and the per-slot job lists.
+//   G  gate_up units = (slot, 16 rows of gate + the matching 16 rows of up), a
+//      contiguous share per CTA, five units at a time (4 warps each): exact
+//      MXFP4 x Q8_0 row dots, bias, SwiGLU-OAI / SiLU -> fp32 activations; the
+//      second of the two units of a 32-value block quantizes it to a Q8_0 record.
+//   D  down units = (slot, 16 rows of down), ten at a time (2 warps each), over
+//      the activation records -> per-job outputs y.
+// Every warp streams its weight rows through its own cp.async ring in shared
+// memory, several stages ahead, so that enough bytes are in flight per SM.
+// The arithmetic of every value is the per-stage path's (umsx_kernels.cu), so
+// both paths produce the same bits; this one only removes the kernel boundaries,
+// the single-CTA selection and the second wave of CTAs.
+//
+// Grid barriers are a monotonic counter with bounded spins: a CTA that waits
+// longer than kGridWaitCycles (or sees the error flag) sets `err` and returns,
+// so a fault elsewhere cannot keep the kernel alive.
+#include <stdint.h>
+
+#include "umsx_device.cuh"
+#include "umsx_internal.h"
+#include "umsx_mx.cuh"
+
+namespace umsx {
+
+namespace {
+
+constexpr int kDecThreads = 640;                 // 20 warps
+constexpr int kGuGroups = kDecThreads / 128;     // concurrent gate_up units (4 warps each)
+constexpr int kDnGroups = kDecThreads / 64;      // concurrent down units (2 warps each)
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr long long kGridWaitCycles = 40000000;  // ~20 ms at 2 GHz
+constexpr int kMaxEntries = kDecodeMaxTokens * kDecodeMaxTopK;
+constexpr int kDecodeMaxExperts = 256;
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void group_bar(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// All CTAs arrive; returns false (uniformly within the CTA) if the wait ran out
+// or another CTA reported an error.
+__device__ bool grid_sync(unsigned *bar, unsigned target, uint32_t *err, int *ok_s) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // release: this CTA's writes (ordered before by the barrier above) become visible with the arrival
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+        int ok = 1;
+        const long long t0 = clock64();
+        for (unsigned it = 0; ld_acquire_gpu(bar) < target; ++it) {
+            if ((it & 63u) == 63u) {
+                if (*reinterpret_cast<volatile uint32_t *>(err)) { ok = 0; break; }
+                if (clock64() - t0 > kGridWaitCycles) { atomicOr(err, 2u); ok = 0; break; }
+            }
+        }
+        *ok_s = ok;
+    }
+    __syncthreads();
+    return *ok_s != 0;
+}
+
+struct DecSmem {
+    float *wrow;    // [kDecRouterRows][H] router rows of this CTA's experts (bulk-copied a layer ahead)
+    float *hs;      // [T][H] residual stream (this CTA's copy)
+    uint8_t *xrec;  // [T][nb][64] Q8_0 records of the normalised h
+    float *xsc;     // [T][pad4(nb)]
+    uint8_t *arec;  // [2T][nbI][64] Q8_0 records of the activations this CTA's down units read
+    float *asc;     // [2T][pad4(nbI)]
+    uint8_t *ring;  // [warps][S][kRingStageBytes] weight stream rings
+};
+
+constexpr int kDecRouterRows = 2;  // experts <= 2 * #CTAs
+
+// Ring stages per warp: deep for one token, where the weight stream is the bottleneck;
+// shallower when more tokens need more staging room.
+__host__ __device__ constexpr int ring_stages(int T) { return T == 1 ? 5 : 2; }
+
+__host__ __device__ inline size_t decode_smem_layout(int T, int H, int I, size_t off[7]) {
+    const size_t nb = H / 32, nbI = I / 32;
+    size_t o = 0;
+    off[0] = o; o += (size_t)kDecRouterRows * H * 4;
+    off[1] = o; o += (size_t)T * H * 4;
+    off[2] = o; o += (size_t)T * nb * 64;
+    off[3] = o; o += (size_t)T * pad4((int)nb) * 4;
+    off[4] = o; o += (size_t)2 * T * nbI * 64;
+    off[5] = o; o += (size_t)2 * T * pad4((int)nbI) * 4;
+    off[6] = o; o += (size_t)kDecWarps * ring_stages(T) * kRingStageBytes;
+    return o;
+}
+
+// Q8_0 of 32 values held one per lane, written as an MXFP4 staging record.
+__device__ __forceinline__ void quantize_record(float v, uint8_t *rec, float *scale, int lane) {
+    const float amax = warp_max(fabsf(v));
+    const float qinv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    write_mx_record(q8_code(v, qinv), rec, lane);
+    if (lane == 0) *scale = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+}
+
+// Thread 0: bulk-copies the router rows of experts c, c + nC, ... (n_rows of them) into smem.
+__device__ __forceinline__ void load_router_rows(const float *router_w, int c, int nC, int n_rows, int H, float *wrow,
+                                                 uint64_t *bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier generic reads of wrow come first
+    mbar_expect_tx(bar, (uint32_t)(n_rows * H * 4));
+    for (int j = 0; j < n_rows; ++j) bulk_g2s(wrow + (size_t)j * H, router_w + (size_t)(c + j * nC) * H, H * 4, bar);
+}
+
+// out4[i] = (residual ? h4[i] : 0) + sum_r w[t][r] * y[t*K + r] over float4 columns, rank order;
+// the loads of four ranks are in flight together.
+__device__ __forceinline__ float4 fold4(const float4 *y4, const float *w, int t, int K, int H4, int n4, float4 h,
+                                        int residual) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int r0 = 0; r0 < K; r0 += 4) {
+        float4 yv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            if (r0 + r < K) yv[r] = __ldcg(y4 + (size_t)(t * K + r0 + r) * H4 + n4);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            if (r0 + r < K) {
+                const float wr = w[t * K + r0 + r];
+                acc.x = __fadd_rn(acc.x, __fmul_rn(wr, yv[r].x));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(wr, yv[r].y));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(wr, yv[r].z));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(wr, yv[r].w));
+            }
+        }
+    }
+    if (!residual) return acc;
+    return make_float4(__fadd_rn(h.x, acc.x), __fadd_rn(h.y, acc.y), __fadd_rn(h.z, acc.z), __fadd_rn(h.w, acc.w));
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant__ DecodeParams p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float inv_s[kDecodeMaxTokens];
+    __shared__ int sel_e[kMaxEntries];
+    __shared__ float sel_w[kMaxEntries];
+    __shared__ int n_slots_s;
+    __shared__ int slot_e[kMaxEntries], slot_cnt[kMaxEntries], slot_first[kMaxEntries];
+    __shared__ int job_j[kMaxEntries];  // entries t*K + r grouped by slot, ascending within a slot
+    __shared__ float xch_g[kGuGroups][MT][2][16][4];
+    __shared__ float res_g[kGuGroups][MT][2][16];
+    __shared__ float xch_d[kDnGroups][MT][16][4];
+    __shared__ int ok_s, late_s;
+    __shared__ int last_g[kGuGroups][MT];
+    __shared__ __align__(8) uint64_t wbar;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nC = gridDim.x, c = blockIdx.x;
+    const int T = p.tokens, H = p.hidden, I = p.inter, E = p.experts, K = p.top_k;
+    const int nb = H / 32, nbI = I / 32, N = T * K, H4 = H / 4;
+    const int G1 = I / 16, G2 = H / 16;
+    const int my_e = c < E ? (E - 1 - c) / nC + 1 : 0;  // router rows of this CTA (<= kDecRouterRows)
+    const int n_lw = my_e * T;                          // warps computing logits; the others quantize h
+    constexpr int S = ring_stages(MT);
+    size_t off[7];
+    decode_smem_layout(T, H, I, off);
+    DecSmem sm{reinterpret_cast<float *>(smem + off[0]), reinterpret_cast<float *>(smem + off[1]), smem + off[2],
+               reinterpret_cast<float *>(smem + off[3]), smem + off[4], reinterpret_cast<float *>(smem + off[5]),
+               smem + off[6]};
+    uint8_t *my_ring = sm.ring + (size_t)warp * S * kRingStageBytes;
+    unsigned target = 0;
+    uint32_t wphase = 0;
+
+    if (tid == 0) {
+        mbar_init(&wbar, 1);
+        late_s = 0;
+        if (my_e > 0) load_router_rows(p.layer[0].router_w, c, nC, my_e, H, sm.wrow, &wbar);
+    }
+    // h <- x
+    if (p.x_dtype == UMSX_DTYPE_BF16) {
+        const uint16_t *xb = static_cast<const uint16_t *>(p.x);
+        for (int i = tid; i < T * H; i += kDecThreads) sm.hs[i] = bf16_bits_to_f32(xb[i]);
+    } else {
+        const float4 *xf = static_cast<const float4 *>(p.x);
+        for (int i = tid; i < T * H4; i += kDecThreads) reinterpret_cast<float4 *>(sm.hs)[i] = xf[i];
+    }
+
+    for (int l = 0; l < p.n_layers; ++l) {
+        const DecodeLayer &Ld = p.layer[l];
+        // ---- R: fold in the previous layer, normalise, logits, x records ----------
+        if (l > 0) {
+            float4 *h4 = reinterpret_cast<float4 *>(sm.hs);
+            const float4 *y4 = reinterpret_cast<const float4 *>(p.y);
+            for (int i = tid; i < T * H4; i += kDecThreads) {
+                const int t = i / H4;
+                h4[i] = fold4(y4, sel_w, t, K, H4, i - t * H4, h4[i], p.residual);
+            }
+        }
+        __syncthreads();
+        if (warp < T) {
+            float inv = 1.0f;  // x * 1 is exact: without RMSNorm the products below leave h unchanged
+            if (p.rmsnorm) {
+                const float *ht = sm.hs + (size_t)warp * H;
+                float a = 0.0f;
+                for (int k0 = lane; k0 < H; k0 += 32 * 8) {
+                    float v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] = k0 + 32 * j < H ? ht[k0 + 32 * j] : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (k0 + 32 * j < H) a = __fmaf_rn(v[j], v[j], a);
+                }
+                const float ss = warp_tree_sum(a);
+                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), p.eps)));
+            }
+            if (lane == 0) inv_s[warp] = inv;
+        }
+        __syncthreads();
+        if (warp < n_lw) {
+            // logits of (expert, token) pairs: 32 strided FMA chains, then the xor tree
+            const float rb = Ld.router_b ? __ldg(Ld.router_b + c + nC * (warp / T)) : 0.0f;  // in flight meanwhile
+            if (!mbar_wait_bounded(&wbar, wphase, kWaitLimitCycles) && lane == 0) late_s = 1;
+            for (int q = warp; q < n_lw; q += kDecWarps) {
+                const int j = q / T, t = q - j * T, e = c + nC * j;
+                const float *wr = sm.wrow + (size_t)j * H;
+                const float *ht = sm.hs + (size_t)t * H;
+                const float inv = inv_s[t];
+                float acc = 0.0f;
+                for (int k0 = lane; k0 < H; k0 += 32 * 8) {
+                    float w[8], x[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        w[i] = k0 + 32 * i < H ? wr[k0 + 32 * i] : 0.0f;
+                        x[i] = k0 + 32 * i < H ? ht[k0 + 32 * i] : 0.0f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        if (k0 + 32 * i < H) acc = __fmaf_rn(w[i], __fmul_rn(x[i], inv), acc);
+                }
+                float lg = warp_tree_sum(acc);
+                if (Ld.router_b) lg = __fadd_rn(lg, q == warp ? rb : __ldg(Ld.router_b + e));
+                if (lane == 0) __stcg(p.logits + (size_t)t * E + e, lg);
+            }
+        } else {
+            // Q8_0 records of the normalised rows (the gate_up activations): blocks c, c + #CTAs, ...
+            // here, all of them copied back by every CTA after the barrier
+            for (int it = c + nC * (warp - n_lw); it < T * nb; it += nC * (kDecWarps - n_lw)) {
+                const int t = it / nb, b = it - t * nb;
+                const float v = __fmul_rn(sm.hs[(size_t)t * H + b * 32 + lane], inv_s[t]);
+                quantize_record(v, p.xr + ((size_t)t * nb + b) * 64, p.xr_sc + (size_t)t * pad4(nb) + b, lane);
+            }
+        }
+        wphase ^= 1u;
+        __syncthreads();
+        if (late_s) {  // the router rows never arrived: report, let the copy land, stop
+            if (tid == 0) atomicOr(p.err, 4u);
+            mbar_wait_bounded(&wbar, wphase ^ 1u, kWaitLimitCycles);
+            return;
+        }
+        target += nC;
+        if (!grid_sync(p.bar, target, p.err, &ok_s)) return;
+
+        // ---- S: selection and slots (every CTA) -----------------------------------
+        if (warp < T) {
+            int sel;
+            float w;
+            select_topk<kDecodeMaxExperts / 32>(p.logits + (size_t)warp * E, E, K, p.routing, p.routed_scale, lane, sel, w);
+            if (lane < K) { sel_e[warp * K + lane] = sel; sel_w[warp * K + lane] = w; }
+        } else {
+            const int tt = tid - T * 32, nt = kDecThreads - T * 32;
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.xr);
+            for (int i = tt; i < T * nb * 4; i += nt) reinterpret_cast<uint4 *>(sm.xrec)[i] = __ldcg(src + i);
+            for (int i = tt; i < T * pad4(nb); i += nt) sm.xsc[i] = __ldcg(p.xr_sc + i);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const bool has = lane < N;
+            int ej = has ? sel_e[lane] : 0x7fffffff;
+            if (has && (ej < 0 || ej >= E)) {  // cannot happen (selection always picks a valid expert); never index with it
+                atomicOr(p.err, 8u);
+                ej = 0;
+            }
+            int same_before = 0, cnt = 0, less = 0;
+            for (int j = 0; j < N; ++j) {
+                const int o = __shfl_sync(kFull, ej, j);
+                same_before += (o == ej && j < lane);
+                cnt += o == ej;
+                less += o < ej;
+            }
+            const bool first = has && same_before == 0;
+            const unsigned firsts = __ballot_sync(kFull, first);
+            int slot = 0;
+            for (int j = 0; j < N; ++j) {
+                const int o = __shfl_sync(kFull, ej, j);
+                slot += ((firsts >> j) & 1u) && o < ej;
+            }
+            if (first) { slot_e[slot] = ej; slot_cnt[slot] = cnt; slot_first[slot] = less; }
+            if (has) job_j[less + same_before] = lane;
+            if (lane == 0) n_slots_s = __popc(firsts);
+            if (c == 0 && l == p.n_layers - 1 && p.ids_out && has) {
+                p.ids_out[lane] = ej;
+                p.w_out[lane] = sel_w[lane];
+            }
+        }
+        __syncthreads();
+        const int n_slots = n_slots_s;
+        const int U1 = n_slots * G1, U2 = n_slots * G2;
+        const int u_lo = (int)((long long)c * U1 / nC), u_hi = (int)((long long)(c + 1) * U1 / nC);
+        const int v_lo = (int)((long long)c * U2 / nC), v_hi = (int)((long long)(c + 1) * U2 / nC);
+        // ---- G: gate_up units ------------------------------------------------------
+        {
+            const int gi = warp >> 2, wg = warp & 3, half = wg >> 1, lh = wg & 1, gt = tid & 127;
+            const int r = lane & 15;
+            Staged xs;
+            xs.q = reinterpret_cast<const uint4 *>(sm.xrec);
+            xs.sc = sm.xsc;
+            xs.flag = nullptr;
+            xs.scs = pad4(nb);
+            for (int u = u_lo + gi; u < u_hi; u += kGuGroups) {
+                const int s = u / G1, g = u - s * G1;
+                const int e = slot_e[s], cnt = slot_cnt[s], jf = slot_first[s];
+                const int rg = half * G1 + g;
+                MxRing ws;
+                ws.init(Ld.gu_codes + code_offset(UMSX_QUANT_MXFP4, e, 2 * G1, rg, nb),
+                        Ld.gu_scales + scale_offset(UMSX_QUANT_MXFP4, e, 2 * G1, rg, nb), nb, lh, my_ring);
+                const float bias = Ld.gu_bias ? __ldg(Ld.gu_bias + (size_t)e * 2 * I + half * I + g * 16 + r) : 0.0f;
+                for (int c0 = 0; c0 < cnt; c0 += MT) {
+                    const int m = min(MT, cnt - c0);
+                    int trow[MT];
+#pragma unroll
+                    for (int t = 0; t < MT; ++t) trow[t] = t < m ? job_j[jf + c0 + t] / K : 0;
+                    float acc[MT][4];
+                    mx_warp_dot_ring<MT, S>(ws, lh, xs, nb, m, lane, acc, trow);
+                    mx_chain_combine<MT>(acc);
+                    if (lh == 1 && lane < 16)
+#pragma unroll
+                        for (int t = 0; t < MT; ++t)
+                            if (t < m)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) xch_g[gi][t][half][r][q] = acc[t][q];
+                    group_bar(1 + gi, 128);
+                    if (lh == 0 && lane < 16)
+#pragma unroll
+                        for (int t = 0; t < MT; ++t)
+                            if (t < m) res_g[gi][t][half][r] = __fadd_rn(mx_row_total(acc[t], xch_g[gi][t][half][r]), bias);
+                    group_bar(1 + gi, 128);
+                    for (int i = gt; i < m * 16; i += 128) {
+                        const int t = i >> 4, k = i & 15;
+                        const float gv = res_g[gi][t][0][k], uv = res_g[gi][t][1][k];
+                        const float a = p.activation == UMSX_ACT_SWIGLU_OAI ? swiglu_oai(gv, uv, p.alpha, p.limit) : silu_mul(gv, uv);
+                        __stcg(p.act + (size_t)job_j[jf + c0 + t] * I + g * 16 + k, a);
+                    }
+                    // The two units of a 32-value block: whichever finishes second quantizes
+                    // it into the down records.  Neither waits for the other.
+                    __threadfence();
+                    group_bar(1 + gi, 128);
+                    if (gt < m) {
+                        const unsigned prev = atomicAdd(p.act_done + (size_t)job_j[jf + c0 + gt] * nbI + (g >> 1), 1u);
+                        last_g[gi][gt] = prev == 1u;
+                    }
+                    group_bar(1 + gi, 128);
+                    for (int t = wg; t < m; t += 4) {
+                        if (!last_g[gi][t]) continue;
+                        __threadfence();
+                        const size_t job = (size_t)job_j[jf + c0 + t], blk = g >> 1;
+                        const float v = __ldcg(p.act + job * I + blk * 32 + lane);
+                        quantize_record(v, p.act_rec + (job * nbI + blk) * 64, p.act_sc + job * pad4(nbI) + blk, lane);
+                        if (lane == 0) p.act_done[job * nbI + blk] = 0;
+                    }
+                    group_bar(1 + gi, 128);
+                }
+            }
+        }
+        target += nC;
+        if (!grid_sync(p.bar, target, p.err, &ok_s)) return;
+
+        // ---- D: down units -----------------------------------------------------------
+        if (tid == 0 && my_e > 0 && l + 1 < p.n_layers)
+            load_router_rows(p.layer[l + 1].router_w, c, nC, my_e, H, sm.wrow, &wbar);
+        int jb = 0;
+        if (v_lo < v_hi) {
+            const int s_lo = v_lo / G2, s_hi = (v_hi - 1) / G2;
+            jb = slot_first[s_lo];
+            const int nar = slot_first[s_hi] + slot_cnt[s_hi] - jb;  // <= 2T: a CTA spans at most two slots
+            const int rq = nbI * 4, rs = pad4(nbI);
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.act_rec);
+            for (int i = tid; i < nar * rq; i += kDecThreads) {
+                const int a = i / rq;
+                reinterpret_cast<uint4 *>(sm.arec)[i] = __ldcg(src + (size_t)job_j[jb + a] * rq + (i - a * rq));
+            }
+            for (int i = tid; i < nar * rs; i += kDecThreads) {
+                const int a = i / rs;
+                sm.asc[i] = __ldcg(p.act_sc + (size_t)job_j[jb + a] * rs + (i - a * rs));
+            }
+        }
+        __syncthreads();
+        {
+            const int di = warp >> 1, lh = warp & 1, r = lane & 15;
+            Staged as;
+            as.q = reinterpret_cast<const uint4 *>(sm.arec);
+            as.sc = sm.asc;
+            as.flag = nullptr;
+            as.scs = pad4(nbI);
+            for (int v = v_lo + di; v < v_hi; v += kDnGroups) {
+                const int s = v / G2, g = v - s * G2;
+                const int e = slot_e[s], cnt = slot_cnt[s], jf = slot_first[s];
+                MxRing ws;
+                ws.init(Ld.dn_codes + code_offset(UMSX_QUANT_MXFP4, e, G2, g, nbI),
+                        Ld.dn_scales + scale_offset(UMSX_QUANT_MXFP4, e, G2, g, nbI), nbI, lh, my_ring);
+                const float bias = Ld.dn_bias ? __ldg(Ld.dn_bias + (size_t)e * H + g * 16 + r) : 0.0f;
+                for (int c0 = 0; c0 < cnt; c0 += MT) {
+                    const int m = min(MT, cnt - c0);
+                    int trow[MT];
+#pragma unroll
+                    for (int t = 0; t < MT; ++t) trow[t] = t < m ? jf + c0 + t - jb : 0;
+                    float acc[MT][4];
+                    mx_warp_dot_ring<MT, S>(ws, lh, as, nbI, m, lane, acc, trow);
+                    mx_chain_combine<MT>(acc);
+                    if (lh == 1 && lane < 16)
+#pragma unroll
+                        for (int t = 0; t < MT; ++t)
+                            if (t < m)
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) xch_d[di][t][r][q] = acc[t][q];
+                    group_bar(1 + di, 64);
+                    if (lh == 0 && lane < 16)
+#pragma unroll
+                        for (int t = 0; t < MT; ++t)
+                            if (t < m) {
+                                float y = mx_row_total(acc[t], xch_d[di][t][r]);
+                                if (Ld.dn_bias) y = __fadd_rn(y, bias);
+                                __stcg(p.y + (size_t)job_j[jf + c0 + t] * H + g * 16 + r, y);
+                            }
+                    group_bar(1 + di, 64);
+                }
+            }
+        }
+        target += nC;
+        if (!grid_sync(p.bar, target, p.err, &ok_s)) return;
+    }
+    // final fold: each CTA writes its share of the output rows
+    const int total4 = T * H4;
+    const int lo = (int)((long long)c * total4 / nC), hi = (int)((long long)(c + 1) * total4 / nC);
+    const float4 *y4 = reinterpret_cast<const float4 *>(p.y);
+    for (int i = lo + tid; i < hi; i += kDecThreads) {
+        const int t = i / H4;
+        reinterpret_cast<float4 *>(p.out)[i] =
+            fold4(y4, sel_w, t, K, H4, i - t * H4, reinterpret_cast<const float4 *>(sm.hs)[i], p.residual);
+    }
+}
+
+template <int MT>
+int launch_decode_mt(const DecodeParams &p, cudaStream_t s) {
+    size_t off[7];
+    const size_t dyn = decode_smem_layout(p.tokens, p.hidden, p.inter, off);
+    auto kern = k_decode<MT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) return -1;
+    // shared memory as small as the kernel needs: the rest of the 256 KB stays L1
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxL1) != cudaSuccess) return -1;
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, dyn) != cudaSuccess || per_sm < 1)
+        return -1;
+    // a CTA's down units then span at most two slots, whose jobs fit the 2T staged rows
+    if (min(p.experts, p.tokens * p.top_k) > sms || p.experts > kDecRouterRows * sms) return -1;
+    if (cudaMemsetAsync(p.bar, 0, sizeof(unsigned), s) != cudaSuccess) return -1;
+    if (cudaMemsetAsync(p.act_done, 0, (size_t)p.tokens * p.top_k * (p.inter / 32) * 4, s) != cudaSuccess) return -1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(sms);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = dyn;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return -1;
+    return 1;
+}
+
+}  // namespace
+
+bool decode_supported(int tokens, int hidden, int inter, int experts, int top_k, int n_layers) {
+    return tokens >= 1 && tokens <= kDecodeMaxTokens && top_k >= 1 && top_k <= kDecodeMaxTopK && experts >= top_k &&
+           experts <= kDecodeMaxExperts && n_layers >= 1 && n_layers <= kDecodeMaxLayers && hidden % 64 == 0 && inter % 64 == 0;
+}
+
+int launch_decode(const DecodeParams &p, cudaStream_t s) {
+    return p.tokens == 1 ? launch_decode_mt<1>(p, s) : launch_decode_mt<kDecodeMaxTokens>(p, s);
+}
+
+}  // namespace umsx

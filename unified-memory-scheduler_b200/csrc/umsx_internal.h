@@ -111,6 +111,52 @@ struct GemvParams {
     int prefetch_early;     // the slot records were written two kernels back: prefetch weights before waiting
 };
 
+// Persistent decode kernel (umsx_decode.cu): every layer of a stack, or one layer,
+// for at most kDecodeMaxTokens tokens in one cooperative launch.  MXFP4 weights with
+// fused gate_up only; all experts local.
+constexpr int kDecodeMaxLayers = 48;
+constexpr int kDecodeMaxTokens = 4;
+constexpr int kDecodeMaxTopK = 8;
+
+struct DecodeLayer {
+    const float *router_w;    // [E][H]
+    const float *router_b;    // [E] or null
+    const uint8_t *gu_codes;  // fused gate_up planes [E][2I][H]
+    const uint8_t *gu_scales;
+    const float *gu_bias;     // [E][2I] or null
+    const uint8_t *dn_codes;  // down planes [E][H][I]
+    const uint8_t *dn_scales;
+    const float *dn_bias;     // [E][H] or null
+};
+
+struct DecodeParams {
+    DecodeLayer layer[kDecodeMaxLayers];
+    int n_layers;
+    int tokens, hidden, inter, experts, top_k, routing, activation;
+    float routed_scale, alpha, limit, eps;
+    int rmsnorm;       // RMSNorm (unit weight) of h before each router
+    int residual;      // h <- h + MoE(h) per layer; else out = MoE(x)
+    const void *x;     // [T][H] F32 or BF16
+    int x_dtype;
+    float *out;        // [T][H]
+    int32_t *ids_out;  // [T][K] routing of the last layer, or null
+    float *w_out;      // [T][K]
+    float *logits;     // [T][E] scratch
+    float *act;        // [T*K][I] scratch
+    float *y;          // [T*K][H] scratch
+    uint8_t *xr;       // [T][H/32][64] Q8_0 records of the normalised rows
+    float *xr_sc;      // [T][pad4(H/32)]
+    uint8_t *act_rec;  // [T*K][I/32][64] Q8_0 records of the activations
+    float *act_sc;     // [T*K][pad4(I/32)]
+    uint32_t *act_done;  // [T*K][I/32] arrival counters (zeroed by the launcher)
+    unsigned *bar;     // grid barrier counter (zeroed by the launcher)
+    uint32_t *err;     // set when a grid barrier wait ran out
+};
+
+bool decode_supported(int tokens, int hidden, int inter, int experts, int top_k, int n_layers);
+// Returns 1 (kernels launched) or -1 if this device cannot hold the kernel resident on every SM.
+int launch_decode(const DecodeParams &p, cudaStream_t s);
+
 // Thread-local status channel shared by every translation unit (umsx_api.cu).
 void record_error(const char *msg);      // the message umsx_last_error() returns
 void record_launches(uint64_t kernels);  // adds to umsx_kernel_launches()

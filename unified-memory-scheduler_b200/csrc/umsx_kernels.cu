@@ -14,6 +14,7 @@
 
 #include "umsx_device.cuh"
 #include "umsx_internal.h"
+#include "umsx_mx.cuh"
 
 namespace umsx {
 
@@ -23,7 +24,6 @@ namespace umsx {
 // ============================================================================
 
 constexpr int kRouterWarps = 4;
-constexpr int kMaxExperts = 1024;
 constexpr int kFusedDispatchMax = 512;
 constexpr int kRouterRegs = 96;  // router-weight chain values a lane holds in registers (H <= 3072)
 
@@ -34,77 +34,17 @@ constexpr int kRouterRegs = 96;  // router-weight chain values a lane holds in r
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-__device__ __forceinline__ bool better(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
-
 // Warp-wide selection for one token (all 32 lanes participate).
 __device__ int select_token(const RouterParams &p, const Dispatch &d, int t, int lane) {
-    const int E = p.experts, K = p.top_k;
-    float v[kMaxExperts / 32];
-    const float *lg = d.logits + (size_t)t * E;
-#pragma unroll
-    for (int j = 0; j < kMaxExperts / 32; ++j) {
-        const int e = lane + 32 * j;
-        v[j] = e < E ? __ldcg(lg + e) : 0.0f;
-    }
-    if (p.routing != UMSX_ROUTE_TOPK_SOFTMAX) {
-        float m = -__uint_as_float(0x7f800000u);
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j)
-            if (lane + 32 * j < E) m = fmaxf(m, v[j]);
-        m = warp_max(m);
-        float s = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j) {
-            if (lane + 32 * j < E) {
-                v[j] = exp_shared(__fadd_rn(v[j], -m));
-                s = __fadd_rn(s, v[j]);
-            }
-        }
-        const float total = warp_tree_sum(s);
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j)
-            if (lane + 32 * j < E) v[j] = __fdiv_rn(v[j], total);
-    }
-    uint32_t taken = 0;
-    int my_sel = -1;
-    float my_val = 0.0f;
-    for (int r = 0; r < K; ++r) {
-        float bv = -__uint_as_float(0x7f800000u);
-        int be = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < kMaxExperts / 32; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E && !((taken >> j) & 1u) && better(v[j], e, bv, be)) { bv = v[j]; be = e; }
-        }
-#pragma unroll
-        for (int s = 16; s >= 1; s >>= 1) {
-            const float ov = __shfl_xor_sync(kFull, bv, s);
-            const int oe = __shfl_xor_sync(kFull, be, s);
-            if (better(ov, oe, bv, be)) { bv = ov; be = oe; }
-        }
-        if ((be & 31) == lane) taken |= 1u << (be >> 5);
-        if (lane == r) { my_sel = be; my_val = bv; }
-    }
-    // weights: lane r < K holds rank r
-    float w = 0.0f;
-    if (p.routing == UMSX_ROUTE_TOPK_SOFTMAX) {
-        const float m = __shfl_sync(kFull, my_val, 0);
-        const float ex = lane < K ? exp_shared(__fadd_rn(my_val, -m)) : 0.0f;
-        float sum = 0.0f;
-        for (int r = 0; r < K; ++r) sum = __fadd_rn(sum, __shfl_sync(kFull, ex, r));
-        w = __fdiv_rn(ex, sum);
-    } else if (p.routing == UMSX_ROUTE_SOFTMAX_TOPK_NORM) {
-        float sum = 0.0f;
-        for (int r = 0; r < K; ++r) sum = __fadd_rn(sum, __shfl_sync(kFull, my_val, r));
-        w = __fdiv_rn(my_val, sum);
-    } else {
-        w = __fmul_rn(my_val, p.routed_scale);
-    }
+    const int K = p.top_k;
+    int sel;
+    float w;
+    select_topk(d.logits + (size_t)t * p.experts, p.experts, K, p.routing, p.routed_scale, lane, sel, w);
     if (lane < K) {
-        d.ids[(size_t)t * K + lane] = my_sel;
+        d.ids[(size_t)t * K + lane] = sel;
         d.weights[(size_t)t * K + lane] = w;
     }
-    return my_sel;  // lane r < K: the expert of rank r
+    return sel;  // lane r < K: the expert of rank r
 }
 
 // One CTA builds counts / offsets / active list / slot records / job lists for
@@ -159,22 +99,6 @@ __device__ void build_dispatch_cta(const Dispatch &d, int entries, int K, int e_
         const int pos = off[e] + before;
         d.job_token[pos] = j / K;
         d.job_rank[pos] = j % K;
-    }
-}
-
-constexpr long long kWaitLimitCycles = 4000000;  // ~2 ms: bounded waits on mbarriers
-__host__ __device__ constexpr int pad4(int n) { return (n + 3) & ~3; }
-
-// One warp holds the 32 Q8_0 codes of a block (code of element `lane`); writes the
-// block's MXFP4 staging record: for lane half lh and lane p, at
-// ((lh*2 + p/2)*16 + (p%2)*8) the code word a(lh, p) and its byte negation.
-__device__ __forceinline__ void write_mx_record(int code, uint8_t *rec, int lane) {
-    const uint32_t c = (uint32_t)code & 0xffu;
-    const uint32_t w = c | (__shfl_down_sync(kFull, c, 1) << 8) | (__shfl_down_sync(kFull, c, 2) << 16) |
-                       (__shfl_down_sync(kFull, c, 3) << 24);
-    if ((lane & 3) == 0) {
-        const int lh = lane >> 4, p = (lane & 15) >> 2;
-        *reinterpret_cast<uint2 *>(rec + (lh * 2 + (p >> 1)) * 16 + (p & 1) * 8) = make_uint2(w, neg8x4(w));
     }
 }
 
@@ -397,10 +321,6 @@ __global__ void __launch_bounds__(256) k_dispatch(Dispatch d, int entries, int K
 // (1.5*2^23) and subtracting 1.5*2^23: |sum| < 2^22 keeps it in one binade.
 // ============================================================================
 
-constexpr uint32_t kMagicI = 0x4B400000u;
-constexpr float kMagicF = 12582912.0f;
-__device__ __forceinline__ float lane_sum(int biased) { return __fsub_rn(__int_as_float(biased), kMagicF); }
-
 template <int QUANT>
 struct Geo;
 template <>
@@ -414,16 +334,6 @@ struct Geo<UMSX_QUANT_Q8_0> {
     static constexpr int kRowsPerWarp = 32;
     static constexpr int kChains = 1;
     static constexpr int kBatch = 4;  // blocks per load batch
-};
-
-// Staged activations of up to MT jobs: per (job, block) 4 x uint4 =
-// {a(4p..4p+3), a(16+4p..), -a(4p..), -a(16+4p..)} for p = 0..3, one fp32 scale
-// (the fp16 value widened) and, for Q8_0 weights, a "holds -128" flag.
-struct Staged {
-    const uint4 *q;
-    const float *sc;
-    const int *flag;
-    int scs;  // scale stride per job
 };
 
 template <int MT>
@@ -573,15 +483,6 @@ __device__ __forceinline__ float finish_row(const float (&a)[8]) {
     const float t0 = __fadd_rn(l[4], l[0]), t1 = __fadd_rn(l[5], l[1]);
     const float t2 = __fadd_rn(l[6], l[2]), t3 = __fadd_rn(l[7], l[3]);
     return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
-}
-
-// Byte offsets of the planes of row group `rg` of local expert `e`.
-__device__ __forceinline__ size_t code_offset(int quant, int e, int nrg, int rg, int nb) {
-    return ((size_t)e * nrg + rg) * (size_t)nb * (quant == UMSX_QUANT_MXFP4 ? 256 : 1024);
-}
-__device__ __forceinline__ size_t scale_offset(int quant, int e, int nrg, int rg, int nb) {
-    const int chunks = quant == UMSX_QUANT_MXFP4 ? ((nb / 2) + 3) / 4 : nb / 2;
-    return ((size_t)e * nrg + rg) * (size_t)chunks * 128;
 }
 
 // Shared-memory bytes for MT staged jobs of nb blocks.
@@ -855,126 +756,6 @@ __global__ void __launch_bounds__(W * 32) k_gemv(GemvParams p, GemvSrc src, Disp
 // {a(lh, 2q), -a(lh, 2q), a(lh, 2q+1), -a(lh, 2q+1)}, a(lh, p) = its 4 code bytes.
 // ============================================================================
 
-constexpr int kMxBatch = 8;  // block pairs per load batch
-
-struct MxBatch {
-    uint2 w[kMxBatch];
-    uint32_t e[kMxBatch / 4];
-};
-
-struct MxStream {
-    const uint2 *cp;
-    const uint32_t *ep;
-    int steps;
-    __device__ __forceinline__ void init(const uint8_t *codes, const uint8_t *scales, int nb, int lane, int lh) {
-        cp = reinterpret_cast<const uint2 *>(codes + lh * 256) + lane;
-        ep = reinterpret_cast<const uint32_t *>(scales) + lane;
-        steps = nb / 2;
-    }
-    template <bool GUARD>
-    __device__ __forceinline__ void load(int s0, MxBatch &b) const {
-#pragma unroll
-        for (int i = 0; i < kMxBatch; ++i)
-            if (!GUARD || s0 + i < steps) b.w[i] = __ldg(cp + (size_t)(s0 + i) * 64);
-#pragma unroll
-        for (int i = 0; i < kMxBatch / 4; ++i)
-            if (!GUARD || s0 + 4 * i < steps) b.e[i] = __ldg(ep + (size_t)((s0 >> 2) + i) * 32);
-    }
-};
-
-template <int MT>
-__device__ __forceinline__ void mx_half(uint2 wq, uint32_t e8, const uint4 *aq, const float *sc, int nb, int scs,
-                                        int m, float (&acc)[MT][4]) {
-    uint32_t pos[4], neg[4];
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-        const uint32_t w = q ? wq.y : wq.x, n = w ^ 0x88888888u;
-        pos[2 * q] = prmt(kMagLo, kMagHi, w);
-        neg[2 * q] = prmt(kMagLo, kMagHi, n);
-        pos[2 * q + 1] = prmt(kMagLo, kMagHi, w >> 16);
-        neg[2 * q + 1] = prmt(kMagLo, kMagHi, n >> 16);
-    }
-    const float eh = e8m0_half(e8);
-#pragma unroll
-    for (int t = 0; t < MT; ++t) {
-        if (t < m) {
-            const float d = __fmul_rn(sc[t * scs], eh);
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const uint4 av = aq[(size_t)t * nb * 4 + q];
-                const int l0 = dp4a_ss(neg[2 * q], av.y, dp4a_ss(pos[2 * q], av.x, (int)kMagicI));
-                const int l1 = dp4a_ss(neg[2 * q + 1], av.w, dp4a_ss(pos[2 * q + 1], av.z, (int)kMagicI));
-                acc[t][2 * q] = __fmaf_rn(d, lane_sum(l0), acc[t][2 * q]);
-                acc[t][2 * q + 1] = __fmaf_rn(d, lane_sum(l1), acc[t][2 * q + 1]);
-            }
-        }
-    }
-}
-
-// acc[t][p] = lane lh*4+p of this thread's chain, over all blocks of the chain.
-template <int MT>
-__device__ __forceinline__ void mx_warp_dot(const MxStream &ws, MxBatch cur, int lh, const Staged &a, int nb, int m,
-                                            int lane, float (&acc)[MT][4]) {
-#pragma unroll
-    for (int t = 0; t < MT; ++t)
-#pragma unroll
-        for (int l = 0; l < 4; ++l) acc[t][l] = 0.0f;
-    const int half = lane >> 4;
-    const uint4 *aq = a.q + half * 4 + lh * 2;  // block b = 2*pair + half: record (t*nb + b)*4
-    const float *sc = a.sc + half;
-    int s0 = 0;
-    for (; s0 + kMxBatch < ws.steps; s0 += kMxBatch) {  // full batches, next one in flight
-        MxBatch nxt;
-        if (s0 + 2 * kMxBatch <= ws.steps) ws.load<false>(s0 + kMxBatch, nxt);
-        else ws.load<true>(s0 + kMxBatch, nxt);
-#pragma unroll
-        for (int i = 0; i < kMxBatch; ++i)
-            mx_half<MT>(cur.w[i], (cur.e[i >> 2] >> (8 * (i & 3))) & 0xffu, aq + (size_t)(s0 + i) * 8,
-                        sc + 2 * (s0 + i), nb, a.scs, m, acc);
-        cur = nxt;
-    }
-#pragma unroll
-    for (int i = 0; i < kMxBatch; ++i)  // last (possibly partial) batch
-        if (s0 + i < ws.steps)
-            mx_half<MT>(cur.w[i], (cur.e[i >> 2] >> (8 * (i & 3))) & 0xffu, aq + (size_t)(s0 + i) * 8,
-                        sc + 2 * (s0 + i), nb, a.scs, m, acc);
-}
-
-// Staging by bulk copy of precomputed records: job t's records (nb * 64 bytes) and
-// scales (pad4(nb) floats) land at smem + t*nb*64 and at the scale area + t*pad4(nb).
-// Returns false (after flagging `err`) if the copies did not complete in time.
-__device__ __forceinline__ bool stage_mx_bulk(const uint8_t *rec, const float *rsc, const int *rows_s, int m, int nb,
-                                              uint8_t *smem, int mt, uint64_t *bar, uint32_t &phase, uint32_t *err) {
-    const int nbp = pad4(nb);
-    if (threadIdx.x == 0) {
-        mbar_expect_tx(bar, (uint32_t)m * (uint32_t)(nb * 64 + nbp * 4));
-        for (int t = 0; t < m; ++t) {
-            bulk_g2s(smem + (size_t)t * nb * 64, rec + (size_t)rows_s[t] * nb * 64, nb * 64, bar);
-            bulk_g2s(smem + (size_t)mt * nb * 64 + (size_t)t * nbp * 4, rsc + (size_t)rows_s[t] * nbp, nbp * 4, bar);
-        }
-    }
-    const bool ok = mbar_wait_bounded(bar, phase, kWaitLimitCycles);
-    // one decision for the whole CTA, so that no thread leaves while others wait at a barrier
-    const bool failed = __syncthreads_or(!ok) != 0;
-    if (failed) {
-        if (threadIdx.x == 0) atomicOr(err, 1u);
-        mbar_wait_bounded(bar, phase, kWaitLimitCycles);  // let copies in flight land before leaving
-    }
-    phase ^= 1u;
-    return !failed;
-}
-
-__device__ __forceinline__ Staged staged_bulk_view(uint8_t *smem, int mt, int nb) {
-    Staged s;
-    s.q = reinterpret_cast<const uint4 *>(smem);
-    s.sc = reinterpret_cast<const float *>(smem + (size_t)mt * nb * 64);
-    s.flag = nullptr;
-    s.scs = pad4(nb);
-    return s;
-}
-
-__host__ __device__ constexpr size_t bulk_staged_bytes(int mt, int nb) { return (size_t)mt * nb * 64 + (size_t)mt * pad4(nb) * 4; }
-
 // Staging into the MXFP4 record layout from internal Q8 rows (lane-pair order).
 __device__ __forceinline__ void stage_mx_internal(const uint8_t *codes, const float *scales, const int *rows_s, int m,
                                                   int nb, uint8_t *smem, int mt) {
@@ -1055,22 +836,6 @@ __device__ __forceinline__ void stage_mx_f32(const float *f32, int cols, const i
     }
 }
 
-// Completes rows from the four partial lane sets: v = chain-combined lanes of this
-// thread's half.  Returns the row dot on lanes < 16 of the lh = 0 warp.
-template <int MT>
-__device__ __forceinline__ void mx_chain_combine(float (&acc)[MT][4]) {
-#pragma unroll
-    for (int t = 0; t < MT; ++t)
-#pragma unroll
-        for (int p = 0; p < 4; ++p) acc[t][p] = __fadd_rn(acc[t][p], __shfl_xor_sync(kFull, acc[t][p], 16));
-}
-
-__device__ __forceinline__ float mx_row_total(const float (&lo)[4], const float *hi) {
-    const float t0 = __fadd_rn(hi[0], lo[0]), t1 = __fadd_rn(hi[1], lo[1]);
-    const float t2 = __fadd_rn(hi[2], lo[2]), t3 = __fadd_rn(hi[3], lo[3]);
-    return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
-}
-
 // gate_up for MXFP4: a CTA computes 16 intermediate values (warps: gate lh0, gate
 // lh1, up lh0, up lh1) for every job of one expert and writes the activated fp32
 // values; the down kernel quantizes them.  grid = (I/16, slots).
@@ -1096,7 +861,7 @@ __global__ void __launch_bounds__(128) k_gate_up_mx(GateUpParams p, Dispatch d) 
     MxStream ws;
     ws.init(mat.codes + code_offset(UMSX_QUANT_MXFP4, e, nrg, rg, nb),
             mat.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, rg, nb), nb, lane, lh);
-    MxBatch first;
+    MxBatch<> first;
     ws.load<true>(0, first);  // weights stream while the activations are copied in
     if (threadIdx.x == 0) mbar_init(&bar, 1);
     uint32_t phase = 0;
@@ -1111,7 +876,7 @@ __global__ void __launch_bounds__(128) k_gate_up_mx(GateUpParams p, Dispatch d) 
         __syncthreads();
         if (!stage_mx_bulk(d.xr, d.xr_sc, rows_s, m, nb, smem, MT, &bar, phase, d.err)) return;
         float acc[MT][4];
-        mx_warp_dot<MT>(ws, first, lh, st, nb, m, lane, acc);
+        mx_warp_dot<MT, kMxBatch>(ws, first, lh, st, nb, m, lane, acc);
         mx_chain_combine<MT>(acc);
         if (lh == 1 && lane < 16)
 #pragma unroll
@@ -1182,7 +947,7 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
     MxStream ws;
     ws.init(p.m.codes + code_offset(UMSX_QUANT_MXFP4, e, nrg, active_rg ? rg : 0, nb),
             p.m.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, active_rg ? rg : 0, nb), nb, lane, lh);
-    MxBatch first;
+    MxBatch<> first;
     if (active_rg) ws.load<true>(0, first);
     if (p.prefetch_early) {  // the weights were chosen two kernels back; the activations come from the last one
         pdl_wait();
@@ -1210,7 +975,7 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
         __syncthreads();
         float acc[MT][4];
         if (active_rg) {
-            mx_warp_dot<MT>(ws, first, lh, st, nb, m, lane, acc);
+            mx_warp_dot<MT, kMxBatch>(ws, first, lh, st, nb, m, lane, acc);
             mx_chain_combine<MT>(acc);
             if (lh == 1 && lane < 16)
 #pragma unroll
