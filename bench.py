@@ -250,19 +250,23 @@ def gpu_arm(a):
     barrier()
     torch.cuda.synchronize()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
-    # per-stage durations: the same steps again with CUDA events between the stages (the
-    # combine then runs as a kernel of its own so that every stage has a boundary)
-    stack.set_timing(True)
-    for i in range(a.warmup):
-        stack.forward(xs_dev[i % pool], out)
-    stage_sum = dict.fromkeys(stack.STAGES, 0.0)
-    for i in range(a.steps):
-        stack.forward(xs_dev[i % pool], out)
-        for k, v in stack.stage_times().items():
-            stage_sum[k] += v
-    stages = {k: v / a.steps for k, v in stage_sum.items()}
-    stack.set_timing(False)
     ms_step = ms / a.steps
+    per_step_launches = launches / a.steps
+    persistent = per_step_launches == 1  # the whole stack ran as one persistent decode kernel per step
+    stages = None
+    if not persistent:
+        # per-stage durations: the same steps again with CUDA events between the stages (the
+        # combine then runs as a kernel of its own so that every stage has a boundary)
+        stack.set_timing(True)
+        for i in range(a.warmup):
+            stack.forward(xs_dev[i % pool], out)
+        stage_sum = dict.fromkeys(stack.STAGES, 0.0)
+        for i in range(a.steps):
+            stack.forward(xs_dev[i % pool], out)
+            for k, v in stack.stage_times().items():
+                stage_sum[k] += v
+        stages = {k: v / a.steps for k, v in stage_sum.items()}
+        stack.set_timing(False)
     value = world * T * a.steps / (ms / 1e3)
     clocks = clk.summary()
 
@@ -289,12 +293,21 @@ def gpu_arm(a):
 
     peak, peak_kind = peaks()
     gu_bytes, dn_bytes, distinct = algorithmic_bytes(cfg, T)
-    gu_ms = stages["gate_up"] / a.layers
-    roof = {"kernel": "k_gate_up (MXFP4 x Q8_0 exact GEMV, fused SwiGLU-OAI + Q8_0)", "bound": "hbm",
-            "achieved": gu_bytes / (gu_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
-            "frac": gu_bytes / (gu_ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
-            "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms, "traffic": traffic_for(a, "k_gate_up")}
     stack_bytes = a.layers * (gu_bytes + dn_bytes + cfg.router_bytes())
+    if persistent:
+        # one launch per step: its duration is the device-timed step (events on the launching stream)
+        roof = {"kernel": "k_decode (persistent: RMSNorm, router, top-k, exact MXFP4 x Q8_0 gate_up + SwiGLU-OAI, "
+                          "down, rank-order combine; all layers in one launch)", "bound": "hbm",
+                "achieved": stack_bytes / (ms_step / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                "frac": stack_bytes / (ms_step / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "algorithmic_bytes_per_launch": stack_bytes, "avg_launch_ms": ms_step,
+                "traffic": traffic_for(a, "k_decode")}
+    else:
+        gu_ms = stages["gate_up"] / a.layers
+        roof = {"kernel": "k_gate_up (MXFP4 x Q8_0 exact GEMV, fused SwiGLU-OAI + Q8_0)", "bound": "hbm",
+                "achieved": gu_bytes / (gu_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                "frac": gu_bytes / (gu_ms / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms, "traffic": None}
     res = {"metric": metric_name(a), "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
@@ -323,11 +336,12 @@ def gpu_arm(a):
 
 
 def traffic_for(a, kernel: str):
-    """Per-launch DRAM bytes of the kernel from the committed ncu summary, when one exists."""
+    """Per-launch DRAM bytes of the kernel, from the committed ncu capture (profiles/traffic.json):
+    bytes per layer measured on a small stack, times this run's layer count."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            t = json.load(f)
-        return t[f"{a.mode}_T{a.tokens}"][kernel]
+            t = json.load(f)[f"{a.mode}_T{a.tokens}"][kernel]
+        return t["dram_bytes_per_layer"] * a.layers
     except Exception:
         return None
 

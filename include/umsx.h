@@ -151,8 +151,11 @@ umsx_status umsx_moe_export_expert(umsx_moe *moe, int proj, int expert, void *ho
  * omitted: h <- h + MoE_l(RMSNorm(h)) for every layer l in order (RMSNorm with unit
  * weight, eps rms_eps; the norm is fused into each layer's router and the residual add
  * into its combine).  The layers must share device and shape; the stack owns one
- * workspace for up to max_tokens tokens and replays the whole stack as one CUDA graph
+ * workspace for up to max_tokens tokens.  With T <= 4 tokens and MXFP4 fused gate_up
+ * layers (all experts resident) a forward is ONE persistent cooperative kernel on the
+ * caller's stream; otherwise the stack replays the per-stage kernels as one CUDA graph
  * per token count, on a stream of its own ordered after / before the caller's stream.
+ * Both give identical bits.
  * Replaces the per-layer ffn_norm -> build_moe_ffn -> residual sequence of the
  * llama.cpp graph the hybrid patch modifies (llama-b11669-hybrid-experts.patch:1355-1930). */
 typedef struct umsx_stack umsx_stack;

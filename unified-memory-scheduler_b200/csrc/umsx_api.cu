@@ -792,28 +792,33 @@ umsx_status stack_run(umsx_stack *st, const void *x, int dtype, int tokens, void
                       cudaMemcpyKind out_kind, cudaStream_t caller) {
     const size_t in_bytes = (size_t)tokens * st->hidden * (dtype == UMSX_DTYPE_BF16 ? 2 : 4);
     const size_t out_bytes = (size_t)tokens * st->hidden * 4;
-    UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
-    UMSX_CUDA(cudaStreamWaitEvent(st->stream, st->ev_in, 0));
-    UMSX_CUDA(cudaMemcpyAsync(st->ws.x_dev, x, in_bytes, in_kind, st->stream));
     const int L = (int)st->layers.size();
-    bool done = false;
     bool eligible = !st->timing;
     for (int l = 0; l < L && eligible; ++l) eligible = decode_eligible(st->layers[l], tokens, L);
     if (eligible) {
-        DecodeParams p = decode_params(st->layers[0], st->ws, st->ws.x_dev, dtype, tokens, st->h);
+        // one persistent launch on the caller's stream, reading x and writing out in place when they are device memory
+        const bool dev_in = in_kind == cudaMemcpyDeviceToDevice;
+        const bool dev_out = out_kind == cudaMemcpyDeviceToDevice && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+        if (!dev_in) UMSX_CUDA(cudaMemcpyAsync(st->ws.x_dev, x, in_bytes, in_kind, caller));
+        DecodeParams p = decode_params(st->layers[0], st->ws, dev_in ? x : st->ws.x_dev, dtype, tokens,
+                                       dev_out ? static_cast<float *>(out) : st->h);
         p.n_layers = L;
         for (int l = 0; l < L; ++l) p.layer[l] = decode_layer(st->layers[l]);
         p.rmsnorm = 1;
         p.residual = 1;
         p.eps = st->eps;
-        done = try_decode(p, st->stream);
+        if (try_decode(p, caller)) {
+            if (!dev_out) UMSX_CUDA(cudaMemcpyAsync(out, st->h, out_bytes, out_kind, caller));
+            return UMSX_OK;
+        }
     }
-    if (!done) {
-        umsx_stack::Graph *g = nullptr;
-        if (umsx_status r = stack_graph(st, tokens, dtype, &g)) return r;
-        UMSX_CUDA(cudaGraphLaunch(g->exec, st->stream));
-        g_launches += g->kernels;
-    }
+    UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
+    UMSX_CUDA(cudaStreamWaitEvent(st->stream, st->ev_in, 0));
+    UMSX_CUDA(cudaMemcpyAsync(st->ws.x_dev, x, in_bytes, in_kind, st->stream));
+    umsx_stack::Graph *g = nullptr;
+    if (umsx_status r = stack_graph(st, tokens, dtype, &g)) return r;
+    UMSX_CUDA(cudaGraphLaunch(g->exec, st->stream));
+    g_launches += g->kernels;
     UMSX_CUDA(cudaMemcpyAsync(out, st->h, out_bytes, out_kind, st->stream));
     UMSX_CUDA(cudaEventRecord(st->ev_out, st->stream));
     UMSX_CUDA(cudaStreamWaitEvent(caller, st->ev_out, 0));
