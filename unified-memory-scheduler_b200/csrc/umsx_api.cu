@@ -81,6 +81,9 @@ struct Workspace {
     void *x_dev = nullptr;
     float *out_dev = nullptr;
     unsigned *bar = nullptr;  // grid barrier counter of the persistent decode kernel
+    uint16_t *a16 = nullptr;    // prefill: x rows in job order as f16 Q8_0 values, hi then lo [2][T*K][H]
+    uint16_t *act16 = nullptr;  // prefill: activations as f16 Q8_0 values, hi then lo [2][T*K][I]
+    int32_t *inv = nullptr;   // prefill: (token, rank) -> job row
     uint8_t *mem = nullptr;
     int max_tokens = 0;
 };
@@ -127,6 +130,7 @@ size_t weight_bytes(const umsx_moe *m, Arena &a) {
         mm.quant = d.quant;
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
+        mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
     };
     Matrix tmp;
     if (d.fused_gate_up) mat(tmp, 2 * I, H);
@@ -147,6 +151,7 @@ void carve_weights(umsx_moe *m, Arena &a) {
         mm.quant = d.quant;
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
+        mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
     };
     if (d.fused_gate_up) mat(m->gate_up, 2 * I, H);
     else { mat(m->gate, I, H); mat(m->up, I, H); }
@@ -190,6 +195,11 @@ void carve_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_
     w.x_dev = a.take<float>(T * H);
     w.out_dev = a.take<float>(T * H);
     w.bar = a.take<unsigned>(1);
+    if (mx && max_tokens >= kPrefillMinTokens) {  // tensor-core prefill operands
+        w.a16 = a.take<uint16_t>(2 * T * K * H);
+        w.act16 = a.take<uint16_t>(2 * T * K * I);
+        w.inv = a.take<int32_t>(T * K);
+    }
     w.max_tokens = max_tokens;
 }
 
@@ -265,6 +275,14 @@ umsx_status generate_matrix(Matrix &mm, uint64_t seed, uint64_t stream, int e_gl
     return UMSX_OK;
 }
 
+// Row exponent maxima of the MXFP4 matrices (the prefill path's f16 rebase).
+umsx_status compute_row_emax(umsx_moe *m) {
+    if (m->d.quant != UMSX_QUANT_MXFP4) return UMSX_OK;
+    for (Matrix *mm : {&m->gate_up, &m->gate, &m->up, &m->down})
+        if (mm->codes) UMSX_LAUNCHED(launch_row_emax(*mm, m->e_local, mm->emax, 0));
+    return UMSX_OK;
+}
+
 size_t max_expert_bytes(const umsx_moe *m) {
     const auto &d = m->d;
     const size_t bb = block_bytes(d.quant);
@@ -321,6 +339,7 @@ umsx_status umsx_moe_create(const umsx_moe_desc *desc, const umsx_moe_weights *w
             UMSX_CUDA(cudaMemcpy(m->gu_bias, gb.data(), gb.size() * 4, cudaMemcpyHostToDevice));
             UMSX_CUDA(cudaMemcpy(m->down_bias, db.data(), db.size() * 4, cudaMemcpyHostToDevice));
         }
+        if (umsx_status s = compute_row_emax(m)) return s;
         UMSX_CUDA(cudaDeviceSynchronize());
         return UMSX_OK;
     };
@@ -357,6 +376,7 @@ umsx_status umsx_moe_create_synthetic(const umsx_moe_desc *desc, uint64_t seed, 
             UMSX_LAUNCHED(launch_gen_normal_bf16_to_f32(seed, stream_id(layer, 6), (uint64_t)m->e_lo * H,
                                                         (uint64_t)m->e_local * H, normal_scale(bias_sigma), m->down_bias, 0));
         }
+        if (umsx_status s = compute_row_emax(m)) return s;
         UMSX_CUDA(cudaDeviceSynchronize());
         return UMSX_OK;
     };
@@ -390,7 +410,7 @@ umsx_status check_call(umsx_moe *m, const void *x, int x_dtype, int tokens, int 
 }
 
 umsx_status run_router(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, int rmsnorm, float eps,
-                       cudaStream_t s, int skip_counts = 0) {
+                       cudaStream_t s, int skip_counts = 0, int records = -1) {
     RouterParams p{};
     p.x = x;
     p.x_dtype = x_dtype;
@@ -407,7 +427,7 @@ umsx_status run_router(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, i
     p.rmsnorm = rmsnorm;
     p.eps = eps;
     p.skip_counts = skip_counts;
-    p.mx_records = m->d.quant == UMSX_QUANT_MXFP4;
+    p.mx_records = records >= 0 ? records : m->d.quant == UMSX_QUANT_MXFP4;
     UMSX_LAUNCHED(launch_router(p, ws.disp, s));
     return UMSX_OK;
 }
@@ -502,9 +522,87 @@ umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, f
 
 // router -> gate_up (+act, +Q8_0) -> down -> combine (+ optional residual).
 // ev: null or 5 events bracketing the four stages.
+// Many tokens, MXFP4 fused gate_up: router + dispatch, then the tensor-core grouped GEMMs.
+bool prefill_eligible(const umsx_moe *m, const Workspace &ws, int tokens) {
+    return m->d.quant == UMSX_QUANT_MXFP4 && m->d.fused_gate_up && tokens >= kPrefillMinTokens && ws.a16 &&
+           m->e_local <= 1024;
+}
+
+umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
+                        const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev) {
+    const auto &d = m->d;
+    const int K = d.top_k, H = d.hidden, I = d.intermediate, jobs = tokens * K;
+    if (ev) if (umsx_status st = mark(ev[0], s)) return st;
+    {
+        RouterParams rp{};
+        rp.x = x;
+        rp.x_dtype = x_dtype;
+        rp.tokens = tokens;
+        rp.hidden = H;
+        rp.experts = d.experts;
+        rp.top_k = K;
+        rp.routing = d.routing;
+        rp.routed_scale = d.routed_scale;
+        rp.w = m->router_w;
+        rp.b = m->router_b;
+        rp.e_lo = m->e_lo;
+        rp.e_local = m->e_local;
+        rp.rmsnorm = rmsnorm;
+        rp.eps = eps;
+        UMSX_LAUNCHED(launch_router_tiled(rp, ws.disp, s));
+    }
+    UMSX_LAUNCHED(launch_prefill_pack(ws.disp, jobs, K, H, ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));
+    if (ev) if (umsx_status st = mark(ev[1], s)) return st;
+    MoeGemmParams g{};
+    g.codes = m->gate_up.codes;
+    g.scales = m->gate_up.scales;
+    g.emax = m->gate_up.emax;
+    g.rows = 2 * I;
+    g.cols = H;
+    g.fused = 1;
+    g.inter = I;
+    g.bias = m->gu_bias;
+    g.offsets = ws.disp.offsets;
+    g.experts = m->e_local;
+    g.m_tiles = I / 64;
+    g.mode = 0;
+    g.activation = d.activation;
+    g.alpha = d.swiglu_alpha;
+    g.limit = d.swiglu_limit;
+    g.act_hi = ws.act16;
+    g.act_lo = ws.act16 + (size_t)jobs * I;
+    g.err = ws.disp.err;
+    int n = launch_moe_gemm(g, ws.a16, ws.a16 + (size_t)jobs * H, jobs, s);
+    if (n < 0) return fail(UMSX_EDEVICE, "prefill gate_up: tensor map or launch setup failed");
+    UMSX_LAUNCHED(n);
+    if (ev) if (umsx_status st = mark(ev[2], s)) return st;
+    MoeGemmParams dn{};
+    dn.codes = m->down.codes;
+    dn.scales = m->down.scales;
+    dn.emax = m->down.emax;
+    dn.rows = H;
+    dn.cols = I;
+    dn.fused = 0;
+    dn.bias = m->down_bias;
+    dn.offsets = ws.disp.offsets;
+    dn.experts = m->e_local;
+    dn.m_tiles = (H + 127) / 128;
+    dn.mode = 1;
+    dn.y_out = ws.y;
+    dn.err = ws.disp.err;
+    n = launch_moe_gemm(dn, ws.act16, ws.act16 + (size_t)jobs * I, jobs, s);
+    if (n < 0) return fail(UMSX_EDEVICE, "prefill down: tensor map or launch setup failed");
+    UMSX_LAUNCHED(n);
+    if (ev) if (umsx_status st = mark(ev[3], s)) return st;
+    UMSX_LAUNCHED(launch_prefill_combine(ws.y, ws.disp.weights, ws.inv, tokens, K, H, residual, out, s));
+    if (ev) if (umsx_status st = mark(ev[4], s)) return st;
+    return UMSX_OK;
+}
+
 umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
                       const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev) {
     const auto &d = m->d;
+    if (prefill_eligible(m, ws, tokens)) return run_prefill(m, ws, x, x_dtype, tokens, out, residual, rmsnorm, eps, s, ev);
     if (ev) if (umsx_status st = mark(ev[0], s)) return st;
     if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s, 1)) return st;
     if (ev) if (umsx_status st = mark(ev[1], s)) return st;

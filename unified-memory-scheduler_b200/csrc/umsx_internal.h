@@ -26,6 +26,7 @@ namespace umsx {
 struct Matrix {
     uint8_t *codes = nullptr;   // code plane, all local experts
     uint8_t *scales = nullptr;  // exponent / fp16-scale plane
+    uint8_t *emax = nullptr;    // MXFP4: largest block exponent of every row [experts][rows] (prefill rebase)
     int rows = 0;               // N per expert
     int cols = 0;               // K
     int quant = 0;
@@ -156,6 +157,34 @@ struct DecodeParams {
 bool decode_supported(int tokens, int hidden, int inter, int experts, int top_k, int n_layers);
 // Returns 1 (kernels launched) or -1 if this device cannot hold the kernel resident on every SM.
 int launch_decode(const DecodeParams &p, cudaStream_t s);
+
+// Prefill grouped GEMM (umsx_prefill.cu): tcgen05 kind::f16 over the experts' job segments.
+constexpr int kPrefillMinTokens = 65;  // from this many tokens an MXFP4 layer takes the tensor-core path
+
+struct MoeGemmParams {
+    const uint8_t *codes, *scales, *emax;  // the projection's MXFP4 planes and row exponents
+    int rows, cols;       // per expert: output rows N, reduction K
+    int fused, inter;     // fused gate_up: tile rows 0-63 gate rows, 64-127 the matching up rows (offset inter)
+    const float *bias;    // [E][rows] or null
+    const int32_t *offsets;  // [E + 1] job segments (jobs in expert order)
+    int experts, m_tiles;
+    int mode;             // 0: gate_up -> act_hi + act_lo = f16 Q8_0 values [jobs][inter]; 1: down -> y_out [jobs][rows]
+    int activation;
+    float alpha, limit;
+    uint16_t *act_hi, *act_lo;
+    float *y_out;
+    uint32_t *err;
+};
+
+// Router for many tokens: tiled logits (same arithmetic as launch_router), per-token selection and
+// x -> Q8_0 (lane-pair order), then the dispatch build.
+int launch_router_tiled(const RouterParams &p, const Dispatch &d, cudaStream_t s);
+int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, cudaStream_t s);
+int launch_prefill_pack(const Dispatch &d, int jobs, int K, int hidden, void *a_hi, void *a_lo, int32_t *inv,
+                        cudaStream_t s);
+int launch_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
+                           const float *residual, float *out, cudaStream_t s);
+int launch_moe_gemm(const MoeGemmParams &p, const void *act_hi, const void *act_lo, int rows_total, cudaStream_t s);
 
 // Thread-local status channel shared by every translation unit (umsx_api.cu).
 void record_error(const char *msg);      // the message umsx_last_error() returns

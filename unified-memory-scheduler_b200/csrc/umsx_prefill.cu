@@ -1,0 +1,562 @@
+// Prefill path (many tokens per expert): grouped GEMMs on the 5th-generation tensor
+// cores for MXFP4 layers.
+//
+// The exact per-int-lane FMA chains of the decode path cannot run at tensor speed,
+// so this path computes the same layer within a tolerance instead (the north-star bar
+// is rel-L2 <= 5e-3, max-abs <= 2e-2 against the reference's exact packed path):
+//  - activations are the reference's Q8_0 codes times their fp16 scale (the same quantizer
+//    as the exact path, parity patch :41-44, :96), held exactly as two f16 operands hi + lo
+//    (q * d has 18 significant bits) that the tensor cores multiply separately;
+//  - MXFP4 weights are decoded exactly to f16 in shared memory (e2m1 value times the
+//    block's power of two, rebased per row so that the largest block of the row sits
+//    at 2^13 and no block overflows f16);
+//  - tcgen05.mma kind::f16 accumulates in fp32 in tensor memory; the epilogue undoes the
+//    row rebase, adds the bias and either applies SwiGLU-OAI / SiLU and re-quantizes the
+//    activation to Q8_0 (gate_up, the reference's pack_down step, native_cpu.cpp:168-179)
+//    or writes the expert output rows (down); a last kernel combines in rank order.
+//
+// Kernel roles per CTA (320 threads, one CTA per SM, persistent over work items
+// (expert, 128-row tile of the weights, 128-token tile of the expert's jobs)):
+//   warp 0    TMA producer of the activation tiles (128 tokens x 64 K, 128-byte swizzle)
+//   warp 1    MMA issuer (one thread) and owner of the tensor memory (two accumulators)
+//   warps 2-5 weight producers (MXFP4 -> f16 tiles), raw bytes prefetched by cp.async
+//   warps 6-9 epilogue, draining one accumulator while the MMA fills the other
+// Rings of 4 weight tiles and 3 (hi + lo) activation tiles decouple them.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "umsx_device.cuh"
+#include "umsx_internal.h"
+#include "umsx_mx.cuh"
+#include "umsx_tc.cuh"
+
+namespace umsx {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64, kStagesA = 4, kStagesB = 3, kRaw = 6;
+constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB: one f16 operand tile
+constexpr int kGemmThreads = 320;
+constexpr long long kTcWaitCycles = 40000000;  // ~20 ms
+constexpr int kMaxGemmExperts = 256;
+
+// Raw MXFP4 bytes of one tile row for one K stage (block pair): the four 8-byte code words
+// [block h][lane half lh] and the exponent words of the two blocks.
+struct RawRow {
+    uint2 w[4];
+    uint32_t e[2];
+};
+constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + kStagesA * kTileBytes /*weights*/ +
+                             kStagesB * 2 * kTileBytes /*activations hi, lo*/ + kRaw * kBM * sizeof(RawRow) +
+                             2 * 8 * 64 * sizeof(float) /*epilogue exchange*/;
+
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, uint32_t *err) {
+    if (mbar_wait_bounded(bar, parity, kTcWaitCycles)) return true;
+    atomicOr(err, 32u);
+    return false;
+}
+
+// Item -> (expert, m tile, n tile) by the per-expert prefix of item counts.
+__device__ __forceinline__ void decode_item(int it, const int *prefix, int experts, int m_tiles, int &e, int &mt,
+                                            int &nt) {
+    int lo = 0, hi = experts;  // prefix[lo] <= it < prefix[hi]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (prefix[mid] <= it) lo = mid;
+        else hi = mid;
+    }
+    e = lo;
+    const int local = it - prefix[lo];
+    mt = local % m_tiles;
+    nt = local / m_tiles;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_constant__ CUtensorMap tmap_hi,
+                                                              const __grid_constant__ CUtensorMap tmap_lo,
+                                                              const MoeGemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;                                 // [kStagesA] weight tiles
+    uint8_t *sB = sA + kStagesA * kTileBytes;           // [kStagesB][hi, lo] activation tiles
+    RawRow *sRaw = reinterpret_cast<RawRow *>(sB + kStagesB * 2 * kTileBytes);  // [kRaw][row]
+    float *xch = reinterpret_cast<float *>(sRaw + kRaw * kBM);                  // [2][8 cols][64 rows]
+    __shared__ __align__(8) uint64_t full_a[kStagesA], empty_a[kStagesA], full_b[kStagesB], empty_b[kStagesB];
+    __shared__ __align__(8) uint64_t d_full[2], d_empty[2];
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int prefix[kMaxGemmExperts + 1];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int E = p.experts, m_tiles = p.m_tiles, nk = p.cols / kBK;
+    if (tid == 0) {
+        for (int s = 0; s < kStagesA; ++s) {
+            mbar_init(&full_a[s], 128);
+            mbar_init(&empty_a[s], 1);
+        }
+        for (int s = 0; s < kStagesB; ++s) {
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty_b[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&d_full[b], 1);
+            mbar_init(&d_empty[b], 128);
+        }
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&tmem_base_s, 2 * kBN);  // two accumulators: the epilogue drains one while the MMA fills the other
+        tc::tmem_relinquish();
+    }
+    if (warp == 0) {
+        // prefix of work items per expert: m tiles x ceil(jobs / 128)
+        int carry = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            int items = 0;
+            if (e < E) {
+                const int cnt = __ldg(p.offsets + e + 1) - __ldg(p.offsets + e);
+                items = m_tiles * ((cnt + kBN - 1) / kBN);
+            }
+            int incl = items;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(kFull, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (e < E) prefix[e] = carry + incl - items;
+            carry += __shfl_sync(kFull, incl, 31);
+        }
+        if (lane == 0) prefix[E] = carry;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_base_s;
+    const int total = prefix[E];
+
+    if (warp == 0) {
+        // ---- activation tiles by TMA --------------------------------------------------
+        if (lane == 0) {
+            uint32_t g = 0;
+            for (int it = blockIdx.x; it < total; it += gridDim.x) {
+                int e, mt, nt;
+                decode_item(it, prefix, E, m_tiles, e, mt, nt);
+                const int row0 = __ldg(p.offsets + e) + nt * kBN;
+                for (int kk = 0; kk < nk; ++kk, ++g) {
+                    const int s = g % kStagesB;
+                    wait_bar(&empty_b[s], ((g / kStagesB) & 1u) ^ 1u, p.err);
+                    mbar_expect_tx(&full_b[s], 2 * kTileBytes);
+                    tc::tma_load_2d(sB + s * 2 * kTileBytes, &tmap_hi, kk * kBK, row0, &full_b[s]);
+                    tc::tma_load_2d(sB + s * 2 * kTileBytes + kTileBytes, &tmap_lo, kk * kBK, row0, &full_b[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue ------------------------------------------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_f16_f32(kBM, kBN);
+            uint32_t g = 0, n_item = 0;
+            for (int it = blockIdx.x; it < total; it += gridDim.x, ++n_item) {
+                const uint32_t buf = n_item & 1u, d_tm = tmem + buf * kBN;
+                wait_bar(&d_empty[buf], ((n_item >> 1) & 1u) ^ 1u, p.err);  // its last tile has been read out
+                tc::fence_after_sync();
+                for (int kk = 0; kk < nk; ++kk, ++g) {
+                    const int sa = g % kStagesA, sb = g % kStagesB;
+                    wait_bar(&full_a[sa], (g / kStagesA) & 1u, p.err);
+                    wait_bar(&full_b[sb], (g / kStagesB) & 1u, p.err);
+                    tc::fence_after_sync();
+                    const uint64_t da = tc::smem_desc_sw128(sA + sa * kTileBytes);
+                    const uint64_t dh = tc::smem_desc_sw128(sB + sb * 2 * kTileBytes);
+                    const uint64_t dl = tc::smem_desc_sw128(sB + sb * 2 * kTileBytes + kTileBytes);
+#pragma unroll
+                    for (int k16 = 0; k16 < kBK / 16; ++k16) {  // 32 bytes of K per step, inside the swizzle atom
+                        // activation = hi + lo exactly, so the sum of both products is the product with it
+                        tc::mma_f16(d_tm, da + 2 * k16, dh + 2 * k16, idesc, (kk | k16) != 0);
+                        tc::mma_f16(d_tm, da + 2 * k16, dl + 2 * k16, idesc, 1u);
+                    }
+                    tc::mma_commit(&empty_a[sa]);
+                    tc::mma_commit(&empty_b[sb]);
+                }
+                tc::mma_commit(&d_full[buf]);
+            }
+        }
+    } else if (warp < 6) {
+        // ---- weight tiles: MXFP4 -> f16 ---------------------------------------------------
+        const int r = 32 * (warp & 3) + lane;  // tile row
+        const int nbK = p.cols / 32, nrg = p.rows / 16, quads = ((nbK / 2) + 3) / 4;
+        uint32_t g = 0;
+        for (int it = blockIdx.x; it < total; it += gridDim.x) {
+            int e, mt, nt;
+            decode_item(it, prefix, E, m_tiles, e, mt, nt);
+            int mrow;
+            if (p.fused) mrow = r < 64 ? mt * 64 + r : p.inter + mt * 64 + (r - 64);
+            else mrow = mt * kBM + r;
+            const bool valid = mrow < p.rows;
+            const int grp = valid ? mrow >> 4 : 0, rr = mrow & 15;
+            const int emax = valid ? __ldg(p.emax + (size_t)e * p.rows + mrow) : 0;
+            const uint8_t *codes = p.codes + ((size_t)e * nrg + grp) * (size_t)nbK * 256;
+            const uint8_t *scl = p.scales + ((size_t)e * nrg + grp) * (size_t)quads * 128;
+            uint8_t *rowA = sA + r * 128;
+            // this row's raw bytes, kRaw - 1 stages ahead (each thread copies and reads only its own row)
+            auto fetch = [&](int kk) {
+                if (kk < nk && valid) {
+                    RawRow *d = sRaw + (kk % kRaw) * kBM + r;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int lh = 0; lh < 2; ++lh)
+                            tc::cp_async8(&d->w[2 * h + lh], codes + (size_t)kk * 512 + lh * 256 + (16 * h + rr) * 8);
+                    tc::cp_async4(&d->e[0], scl + (size_t)(kk >> 2) * 128 + rr * 4);
+                    tc::cp_async4(&d->e[1], scl + (size_t)(kk >> 2) * 128 + (16 + rr) * 4);
+                }
+                cp_async_commit();
+            };
+#pragma unroll
+            for (int j = 0; j < kRaw - 1; ++j) fetch(j);
+            for (int kk = 0; kk < nk; ++kk, ++g) {
+                const int s = g % kStagesA;
+                cp_async_wait<kRaw - 2>();
+                fetch(kk + kRaw - 1);
+                uint2 w[2][2];
+                uint32_t ew = 0;
+                if (valid) {
+                    const RawRow *sr = sRaw + (kk % kRaw) * kBM + r;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int lh = 0; lh < 2; ++lh) w[h][lh] = sr->w[2 * h + lh];
+                    ew = ((sr->e[0] >> (8 * (kk & 3))) & 0xffu) | (((sr->e[1] >> (8 * (kk & 3))) & 0xffu) << 8);
+                }
+                wait_bar(&empty_a[s], ((g / kStagesA) & 1u) ^ 1u, p.err);
+                uint8_t *dst = rowA + s * kTileBytes;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    // block 2*kk + h: elements 32h..32h+31 of the stage; f16 scale 2^(e - emax + 13)
+                    const int sh = (int)((ew >> (8 * h)) & 0xffu) - emax + 13;
+                    const uint32_t sbits = sh >= -14 ? (uint32_t)(sh + 15) << 10 : 0u;
+                    const __half2 sc2 = __halves2half2(__ushort_as_half((unsigned short)sbits),
+                                                       __ushort_as_half((unsigned short)sbits));
+#pragma unroll
+                    for (int lh = 0; lh < 2; ++lh) {
+                        const uint32_t wv[2] = {valid ? w[h][lh].x : 0u, valid ? w[h][lh].y : 0u};
+                        uint32_t o[8];
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+#pragma unroll
+                            for (int b = 0; b < 4; ++b) {
+                                const uint32_t f = tc::e2m1x2_to_f16x2((wv[q] >> (8 * b)) & 0xffu);
+                                const __half2 v = __hmul2(*reinterpret_cast<const __half2 *>(&f), sc2);
+                                o[q * 4 + b] = *reinterpret_cast<const uint32_t *>(&v);
+                            }
+                        // 16 elements = chunks c and c+1 of the 128-byte row, c = 4h + 2lh
+                        const int c = 4 * h + 2 * lh;
+                        *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                        *reinterpret_cast<uint4 *>(dst + (((c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+                    }
+                }
+                tc::fence_proxy_async();
+                tc::mbar_arrive(&full_a[s]);
+            }
+        }
+    } else {
+        // ---- epilogue: drains one accumulator while the MMA fills the other -------------
+        const int r = 32 * (warp & 3) + lane;  // TMEM lane == tile row
+        const uint32_t lane_field = (uint32_t)(32 * (warp & 3)) << 16;
+        uint32_t n_item = 0;
+        for (int it = blockIdx.x; it < total; it += gridDim.x, ++n_item) {
+            int e, mt, nt;
+            decode_item(it, prefix, E, m_tiles, e, mt, nt);
+            int mrow;
+            if (p.fused) mrow = r < 64 ? mt * 64 + r : p.inter + mt * 64 + (r - 64);
+            else mrow = mt * kBM + r;
+            const bool valid = mrow < p.rows;
+            const int emax = valid ? __ldg(p.emax + (size_t)e * p.rows + mrow) : 0;
+            const int seg = __ldg(p.offsets + e), cnt = __ldg(p.offsets + e + 1) - seg;
+            // 2^(emax - 140): the f16 weights carried 2^(e - emax + 13), the block scale is 2^(e - 127)
+            const float rs = valid ? __uint_as_float((uint32_t)(emax > 13 ? emax - 13 : 1) << 23) : 0.0f;
+            const float bias = (valid && p.bias) ? __ldg(p.bias + (size_t)e * p.rows + mrow) : 0.0f;
+            const uint32_t buf = n_item & 1u;
+            const uint32_t taddr = tmem + buf * kBN + lane_field;
+            wait_bar(&d_full[buf], (n_item >> 1) & 1u, p.err);
+            tc::fence_after_sync();
+            if (p.mode == 0) {
+                // gate rows 0-63 live in warps 8, 9 and up rows 64-127 in warps 6, 7.  Per 16 columns
+                // the gate warps take columns 0-7 and the up warps columns 8-15: each hands the other
+                // pair the values it lacks through xch.  Warp (row half) = one Q8_0 block of 32 values.
+                const bool up = r >= 64;
+                const int ar = up ? r - 64 : r;  // activation row of this thread
+                for (int c0 = 0; c0 < kBN; c0 += 16) {
+                    float v[16];
+                    tc::tmem_ld16(taddr + c0, v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = __fadd_rn(__fmul_rn(v[i], rs), bias);
+                    float *xo = xch + (up ? 0 : 8 * 64);  // up values of cols 0-7 / gate values of cols 8-15
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) xo[i * 64 + ar] = v[up ? i : 8 + i];
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    const float *xi = xch + (up ? 8 * 64 : 0);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int col = c0 + (up ? 8 : 0) + i;
+                        const float gv = up ? xi[i * 64 + ar] : v[i];
+                        const float uv = up ? v[8 + i] : xi[i * 64 + ar];
+                        const float a = p.activation == UMSX_ACT_SWIGLU_OAI ? swiglu_oai(gv, uv, p.alpha, p.limit)
+                                                                            : silu_mul(gv, uv);
+                        const float amax = warp_max(fabsf(a));
+                        const float qinv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                        const float qd = __fmul_rn((float)q8_code(a, qinv),
+                                                   f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f))));
+                        const int n = nt * kBN + col;
+                        if (n < cnt) {  // q * d exactly, as f16 hi + lo
+                            const __half hi = __float2half_rn(qd);
+                            const size_t o = (size_t)(seg + n) * p.inter + mt * 64 + ar;
+                            reinterpret_cast<__half *>(p.act_hi)[o] = hi;
+                            reinterpret_cast<__half *>(p.act_lo)[o] = __float2half_rn(__fsub_rn(qd, __half2float(hi)));
+                        }
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                }
+            } else {
+                for (int c0 = 0; c0 < kBN; c0 += 16) {
+                    float v[16];
+                    tc::tmem_ld16(taddr + c0, v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int n = nt * kBN + c0 + i;
+                        if (n < cnt && valid) p.y_out[(size_t)(seg + n) * p.rows + mrow] = __fadd_rn(__fmul_rn(v[i], rs), bias);
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            tc::mbar_arrive(&d_empty[buf]);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 2 * kBN);
+    }
+}
+
+// ---- router for many tokens -------------------------------------------------
+// Same arithmetic as k_router (32 strided FMA chains per (token, expert) -> xor tree ->
+// + bias; RMSNorm with the strided sum of squares), tiled so that router rows and
+// normalised token rows are read from shared memory and reused: a CTA owns 16 tokens x
+// 16 experts, warp w the 4 x 4 block (w / 4, w % 4), lane l chain l of all 16 pairs.
+
+constexpr int kLgTile = 16, kLgKc = 256;
+
+__device__ __forceinline__ float load_x(const void *x, int x_dtype, size_t i) {
+    return x_dtype == UMSX_DTYPE_BF16 ? bf16_bits_to_f32(static_cast<const uint16_t *>(x)[i])
+                                      : static_cast<const float *>(x)[i];
+}
+
+// inv RMS of row t (warp-wide; every lane ends with it), or 1 without RMSNorm.
+__device__ __forceinline__ float row_inv_rms(const void *x, int x_dtype, int t, int H, int rmsnorm, float eps,
+                                             int lane) {
+    if (!rmsnorm) return 1.0f;
+    float a = 0.0f;
+    for (int k = lane; k < H; k += 32) {
+        const float v = load_x(x, x_dtype, (size_t)t * H + k);
+        a = __fmaf_rn(v, v, a);
+    }
+    const float ss = warp_tree_sum(a);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+}
+
+__global__ void __launch_bounds__(512) k_logits_tiled(const void *x, int x_dtype, int tokens, int H, int E,
+                                                      const float *w, const float *b, int rmsnorm, float eps,
+                                                      float *logits) {
+    __shared__ float xs[kLgTile][kLgKc];
+    __shared__ float wsm[kLgTile][kLgKc];
+    __shared__ float inv_s[kLgTile];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.y * kLgTile, e0 = blockIdx.x * kLgTile;
+    if (t0 + warp < tokens) {
+        const float inv = row_inv_rms(x, x_dtype, t0 + warp, H, rmsnorm, eps, lane);
+        if (lane == 0) inv_s[warp] = inv;
+    }
+    __syncthreads();
+    const int ti = (warp >> 2) * 4, ei = (warp & 3) * 4;
+    float acc[4][4] = {};
+    for (int kc = 0; kc < H; kc += kLgKc) {
+        for (int i = threadIdx.x; i < kLgTile * kLgKc; i += blockDim.x) {
+            const int r = i / kLgKc, k = i - r * kLgKc;
+            const bool kin = kc + k < H;
+            xs[r][k] = (kin && t0 + r < tokens) ? __fmul_rn(load_x(x, x_dtype, (size_t)(t0 + r) * H + kc + k), inv_s[r]) : 0.0f;
+            wsm[r][k] = (kin && e0 + r < E) ? __ldg(w + (size_t)(e0 + r) * H + kc + k) : 0.0f;
+        }
+        __syncthreads();
+        const int steps = min(kLgKc, H - kc) / 32;
+        for (int i = 0; i < steps; ++i) {
+            const int k = 32 * i + lane;
+            float xv[4], wv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) xv[a] = xs[ti + a][k];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) wv[c] = wsm[ei + c][k];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[a][c] = __fmaf_rn(wv[c], xv[a], acc[a][c]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int t = t0 + ti + a, e = e0 + ei + c;
+            float l = warp_tree_sum(acc[a][c]);
+            if (t < tokens && e < E) {
+                if (b) l = __fadd_rn(l, __ldg(b + e));
+                if (lane == 0) logits[(size_t)t * E + e] = l;
+            }
+        }
+}
+
+// Per token (one warp): top-k + weights from the logits, and x -> Q8_0 (lane-pair order).
+__global__ void k_select_quant(const void *x, int x_dtype, int tokens, int H, int E, int K, int routing,
+                               float routed_scale, int rmsnorm, float eps, Dispatch d) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= tokens) return;
+    int sel;
+    float wgt;
+    select_topk(d.logits + (size_t)t * E, E, K, routing, routed_scale, lane, sel, wgt);
+    if (lane < K) {
+        d.ids[(size_t)t * K + lane] = sel;
+        d.weights[(size_t)t * K + lane] = wgt;
+    }
+    const float inv = row_inv_rms(x, x_dtype, t, H, rmsnorm, eps, lane);
+    const int nb = H / 32;
+    for (int blk = 0; blk < nb; ++blk) {
+        const float v = __fmul_rn(load_x(x, x_dtype, (size_t)t * H + blk * 32 + lane), inv);
+        const float amax = warp_max(fabsf(v));
+        const float qinv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        d.xq_codes[((size_t)t * nb + blk) * 32 + lane_pair_offset(lane)] = (uint8_t)(int8_t)q8_code(v, qinv);
+        if (lane == 0) d.xq_scales[(size_t)t * nb + blk] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
+    }
+}
+
+// Job rows in expert order as f16 Q8_0 values (codes from the router's quantizer) and the
+// inverse map (token, rank) -> job row.
+__global__ void k_prefill_pack(const uint8_t *xq_codes, const float *xq_scales, const int32_t *job_token,
+                               const int32_t *job_rank, int jobs, int K, int hidden, __half *a_hi, __half *a_lo,
+                               int32_t *inv) {
+    const int nb = hidden / 32;
+    const size_t total = (size_t)jobs * hidden;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int pos = (int)(i / hidden), k = (int)(i - (size_t)pos * hidden);
+        const int t = __ldg(job_token + pos), b = k >> 5, el = k & 31;
+        const int8_t q = (int8_t)__ldg(xq_codes + ((size_t)t * nb + b) * 32 + lane_pair_offset(el));
+        const float qd = __fmul_rn((float)q, __ldg(xq_scales + (size_t)t * nb + b));  // exact (18 bits)
+        const __half hi = __float2half_rn(qd);
+        a_hi[i] = hi;
+        a_lo[i] = __float2half_rn(__fsub_rn(qd, __half2float(hi)));
+        if (k == 0) inv[(size_t)t * K + __ldg(job_rank + pos)] = pos;
+    }
+}
+
+// out[t][n] = (residual[t][n] +) sum_r w[t][r] * y[inv[t][r]][n], rank order from 0.
+__global__ void k_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
+                                  const float *residual, float *out) {
+    const size_t total = (size_t)tokens * width;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / width), n = (int)(i - (size_t)t * width);
+        float acc = 0.0f;
+        for (int r = 0; r < K; ++r)
+            acc = __fadd_rn(acc, __fmul_rn(__ldg(w + (size_t)t * K + r),
+                                           __ldcg(y + (size_t)__ldg(inv + (size_t)t * K + r) * width + n)));
+        out[i] = residual ? __fadd_rn(residual[i], acc) : acc;
+    }
+}
+
+// Largest block exponent of every row of an MXFP4 matrix (for the f16 rebase).
+__global__ void k_row_emax(Matrix m, int experts, uint8_t *emax) {
+    const int nbK = m.cols / 32, nrg = m.rows / 16, quads = ((nbK / 2) + 3) / 4;
+    const size_t total = (size_t)experts * m.rows;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int e = (int)(i / m.rows), row = (int)(i - (size_t)e * m.rows);
+        const uint8_t *sc = m.scales + ((size_t)e * nrg + (row >> 4)) * (size_t)quads * 128;
+        uint32_t mx = 0;
+        for (int pr = 0; pr < nbK / 2; ++pr)
+            for (int h = 0; h < 2; ++h) mx = max(mx, (uint32_t)sc[(size_t)(pr >> 2) * 128 + (16 * h + (row & 15)) * 4 + (pr & 3)]);
+        emax[i] = (uint8_t)mx;
+    }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+int launch_router_tiled(const RouterParams &p, const Dispatch &d, cudaStream_t s) {
+    dim3 grid((p.experts + kLgTile - 1) / kLgTile, (p.tokens + kLgTile - 1) / kLgTile);
+    k_logits_tiled<<<grid, 512, 0, s>>>(p.x, p.x_dtype, p.tokens, p.hidden, p.experts, p.w, p.b, p.rmsnorm, p.eps,
+                                        d.logits);
+    k_select_quant<<<(p.tokens + 7) / 8, 256, 0, s>>>(p.x, p.x_dtype, p.tokens, p.hidden, p.experts, p.top_k,
+                                                      p.routing, p.routed_scale, p.rmsnorm, p.eps, d);
+    return 2 + launch_dispatch(d, p.tokens * p.top_k, p.top_k, p.e_lo, p.e_local, s);
+}
+
+int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, cudaStream_t s) {
+    k_row_emax<<<592, 256, 0, s>>>(m, experts, emax);
+    return 1;
+}
+
+int launch_prefill_pack(const Dispatch &d, int jobs, int K, int hidden, void *a_hi, void *a_lo, int32_t *inv,
+                        cudaStream_t s) {
+    k_prefill_pack<<<148 * 8, 256, 0, s>>>(d.xq_codes, d.xq_scales, d.job_token, d.job_rank, jobs, K, hidden,
+                                           static_cast<__half *>(a_hi), static_cast<__half *>(a_lo), inv);
+    return 1;
+}
+
+int launch_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
+                           const float *residual, float *out, cudaStream_t s) {
+    k_prefill_combine<<<148 * 8, 256, 0, s>>>(y, w, inv, tokens, K, width, residual, out);
+    return 1;
+}
+
+// Grouped GEMM over the experts' job segments.  `act` is the activation operand
+// [rows_total][p.cols] f16 (job rows in expert order).  Returns -1 when the tensor map
+// cannot be encoded.
+int launch_moe_gemm(const MoeGemmParams &p, const void *act_hi, const void *act_lo, int rows_total, cudaStream_t s) {
+    EncodeTiled enc = encoder();
+    if (!enc || p.experts > kMaxGemmExperts) return -1;
+    CUtensorMap tmap[2];
+    const cuuint64_t dims[2] = {(cuuint64_t)p.cols, (cuuint64_t)rows_total};
+    const cuuint64_t strides[1] = {(cuuint64_t)p.cols * 2};
+    const cuuint32_t box[2] = {kBK, kBN};
+    const cuuint32_t estr[2] = {1, 1};
+    const void *src[2] = {act_hi, act_lo};
+    for (int i = 0; i < 2; ++i)
+        if (enc(&tmap[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(src[i]), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return -1;
+    if (cudaFuncSetAttribute(k_moe_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
+        return -1;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    k_moe_gemm<<<sms, kGemmThreads, kGemmSmem, s>>>(tmap[0], tmap[1], p);
+    return 1;
+}
+
+}  // namespace umsx

@@ -1,0 +1,119 @@
+// tcgen05 / TMA building blocks for sm_100a (inline PTX).
+//
+// Conventions used by the grouped GEMM (umsx_prefill.cu):
+// - operands are K-major tiles in shared memory with the 128-byte swizzle: a row of
+//   64 f16 values is 128 bytes, 16-byte chunk c of row r sits at chunk c ^ (r & 7),
+//   eight rows form a 1024-byte atom, atoms are 1024 bytes apart;
+// - accumulators are fp32 in tensor memory, one row per TMEM lane;
+// - every wait on an mbarrier is bounded and reports through the caller.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "umsx_device.cuh"
+
+namespace umsx {
+namespace tc {
+
+// ---- tensor memory ---------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes (lane = thread's lane).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- descriptors -----------------------------------------------------------
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 1024-byte atoms.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void *p) {
+    const uint64_t addr = smem_u32(p);
+    return ((addr & 0x3FFFFull) >> 4)   // start address
+           | (1ull << 16)               // leading byte offset (unused for swizzled K-major)
+           | (64ull << 32)              // stride byte offset: 1024 bytes between 8-row atoms
+           | (1ull << 46)               // descriptor version for sm_100
+           | (2ull << 61);              // SWIZZLE_128B
+}
+
+// Instruction descriptor, kind::f16: f16 x f16 -> f32, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+    return (1u << 4)                      // D format F32
+           | (0u << 7) | (0u << 10)       // A, B format F16
+           | ((uint32_t)(N >> 3) << 17)   // N
+           | ((uint32_t)(M >> 4) << 24);  // M
+}
+
+// D (+)= A * B^T for one K=16 slice; issued by one thread.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// ---- mbarriers / TMA ----------------------------------------------------------
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 2D tiled TMA load (no multicast) of box {x, y} at coordinates (x, y), completing on bar.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 8- and 4-byte asynchronous copies global -> shared (L1-allocating), completed by cp.async groups.
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+
+// Generic-proxy writes to shared memory become visible to the tensor cores / TMA.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Two e2m1 codes (low nibble = first element) -> f16x2, exact.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+    uint32_t d;
+    asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(d) : "r"(byte));
+    return d;
+}
+
+}  // namespace tc
+}  // namespace umsx
