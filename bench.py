@@ -33,6 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 HBM_FALLBACK_GBS = 6650.0
+PREFILL_MIN_TOKENS = 65  # from this many tokens the MXFP4 layers run the tensor-core prefill path
 
 
 def parse():
@@ -56,13 +57,17 @@ def parse():
     return a
 
 
-def peaks():
+TENSOR_FALLBACK_TFLOPS = 1590.0
+
+
+def peaks(kind: str = "hbm_gbs"):
+    """A measured peak from MEASURED_PEAKS.json (hbm_gbs, bf16_tflops, bf16_tflops_sustained), else the fallback."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return float(p[kind]), "measured"
     except Exception:
-        return HBM_FALLBACK_GBS, "fallback"
+        return (HBM_FALLBACK_GBS if kind == "hbm_gbs" else TENSOR_FALLBACK_TFLOPS), "fallback"
 
 
 def metric_name(a):
@@ -302,6 +307,18 @@ def gpu_arm(a):
                 "frac": stack_bytes / (ms_step / 1e3) / 1e9 / peak, "peak_source": f"{peak_kind} hbm_gbs",
                 "algorithmic_bytes_per_launch": stack_bytes, "avg_launch_ms": ms_step,
                 "traffic": traffic_for(a, "k_decode")}
+    elif T >= PREFILL_MIN_TOKENS:
+        # tensor-core prefill: the gate_up grouped GEMM (k_moe_gemm) dominates; useful FLOPs =
+        # 2 x jobs x 2I x H per launch (the kernel issues twice that: activation hi + lo)
+        gu_ms = stages["gate_up"] / a.layers
+        gu_flops = 2.0 * T * cfg.top_k * 2 * cfg.intermediate * cfg.hidden
+        tpeak, tkind = peaks("bf16_tflops_sustained")
+        roof = {"kernel": "k_moe_gemm gate_up (tcgen05 kind::f16, exact f16 MXFP4 weights x hi+lo f16 Q8_0 "
+                          "activations, fp32 TMEM accumulators, fused bias + SwiGLU-OAI + Q8_0)", "bound": "tensor",
+                "achieved": gu_flops / (gu_ms / 1e3) / 1e12, "peak": tpeak, "unit": "TFLOP/s",
+                "frac": gu_flops / (gu_ms / 1e3) / 1e12 / tpeak, "peak_source": f"{tkind} bf16_tflops_sustained",
+                "algorithmic_flops_per_launch": gu_flops, "mma_flops_issued_per_launch": 2 * gu_flops,
+                "avg_launch_ms": gu_ms, "traffic": traffic_for(a, "k_moe_gemm")}
     else:
         gu_ms = stages["gate_up"] / a.layers
         roof = {"kernel": "k_gate_up (MXFP4 x Q8_0 exact GEMV, fused SwiGLU-OAI + Q8_0)", "bound": "hbm",
@@ -310,7 +327,10 @@ def gpu_arm(a):
                 "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms, "traffic": None}
     res = {"metric": metric_name(a), "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
+           "vs_baseline": None,
+           "dtype": ("f16 tensor-core MMA (exact f16 MXFP4 weights x hi+lo f16 Q8_0 activations), fp32 accumulate"
+                     if T >= PREFILL_MIN_TOKENS else "int8 dot (MXFP4 x Q8_0), fp32 accumulate"),
+           "data": "synthetic",
            "config": {"workload": f"gpt-oss-120b-stack {a.mode}", "layers": a.layers, "experts": cfg.experts,
                       "top_k": cfg.top_k, "hidden": cfg.hidden, "ffn": cfg.intermediate, "quant": "mxfp4",
                       "tokens_per_step_per_gpu": T, "global_batch": T * world,
