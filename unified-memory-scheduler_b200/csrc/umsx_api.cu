@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -131,6 +132,7 @@ size_t weight_bytes(const umsx_moe *m, Arena &a) {
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
         mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
+        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
     };
     Matrix tmp;
     if (d.fused_gate_up) mat(tmp, 2 * I, H);
@@ -152,6 +154,7 @@ void carve_weights(umsx_moe *m, Arena &a) {
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
         mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
+        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
     };
     if (d.fused_gate_up) mat(m->gate_up, 2 * I, H);
     else { mat(m->gate, I, H); mat(m->up, I, H); }
@@ -461,14 +464,22 @@ DecodeLayer decode_layer(const umsx_moe *m) {
     L.dn_codes = m->down.codes;
     L.dn_scales = m->down.scales;
     L.dn_bias = m->down_bias;
+    L.gu_tc = m->gate_up.tc_codes;
+    L.dn_tc = m->down.tc_codes;
     return L;
+}
+
+// Layer l of the persistent kernel's stack.
+void set_decode_layer(DecodeParams &p, int l, const umsx_moe *m) {
+    p.layer[l] = decode_layer(m);
+    p.tc_ready = (l == 0 || p.tc_ready) && p.layer[l].gu_tc && p.layer[l].dn_tc;
 }
 
 DecodeParams decode_params(const umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out) {
     const auto &d = m->d;
     DecodeParams p{};
     p.n_layers = 1;
-    p.layer[0] = decode_layer(m);
+    set_decode_layer(p, 0, m);
     p.tokens = tokens;
     p.hidden = d.hidden;
     p.inter = d.intermediate;
@@ -490,20 +501,40 @@ DecodeParams decode_params(const umsx_moe *m, Workspace &ws, const void *x, int 
     p.act_rec = ws.act_rec;
     p.act_sc = ws.act_sc;
     p.act_done = ws.act_done;
+    p.act_q8 = reinterpret_cast<int8_t *>(ws.act_codes);
+    p.act_q8_sc = ws.act_scales;
     p.bar = ws.bar;
     p.err = ws.disp.err;
     return p;
 }
 
-// Launches the persistent kernel; false if this device cannot hold it resident
-// (the caller then takes the per-stage path).
-bool try_decode(const DecodeParams &p, cudaStream_t s) {
+// UMSX_DECODE_PATH picks the persistent kernel of one-token calls: "tc" requires the
+// tensor-core kernel (a call it cannot serve fails with UMSX_EUNSUPPORTED), "tc-auto" prefers
+// it and falls back; unset or anything else keeps the SIMT kernel.  Both give the same bits.
+int decode_path() {
+    const char *v = std::getenv("UMSX_DECODE_PATH");
+    if (!v) return 1;
+    if (!std::strcmp(v, "tc")) return 2;
+    if (!std::strcmp(v, "tc-auto")) return 0;
+    return 1;
+}
+
+// Launches a persistent kernel: 1 launched; 0 this device cannot hold it resident (the caller
+// then takes the per-stage path); -1 the required tensor-core kernel could not be launched.
+int try_decode(const DecodeParams &p, cudaStream_t s) {
+    const int path = decode_path();
+    if (path != 1 && p.tc_ready && launch_decode_tc(p, s) > 0) {
+        g_launches += 1;
+        return 1;
+    }
+    (void)cudaGetLastError();
+    if (path == 2) return -1;
     if (launch_decode(p, s) < 0) {
         (void)cudaGetLastError();
-        return false;
+        return 0;
     }
     g_launches += 1;
-    return true;
+    return 1;
 }
 
 // Reads and clears the device error flag after a synchronised call.
@@ -658,7 +689,9 @@ umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, f
         DecodeParams p = decode_params(m, m->ws, x, x_dtype, tokens, out);
         p.ids_out = m->ws.disp.ids;
         p.w_out = m->ws.disp.weights;
-        if (try_decode(p, s)) return UMSX_OK;
+        const int r = try_decode(p, s);
+        if (r > 0) return UMSX_OK;
+        if (r < 0) return fail(UMSX_EUNSUPPORTED, "UMSX_DECODE_PATH=tc: the tensor-core decode kernel cannot serve this call");
     }
     return run_layer(m, m->ws, x, x_dtype, tokens, out, nullptr, 0, 0.0f, s, nullptr);
 }
@@ -901,14 +934,16 @@ umsx_status stack_run(umsx_stack *st, const void *x, int dtype, int tokens, void
         DecodeParams p = decode_params(st->layers[0], st->ws, dev_in ? x : st->ws.x_dev, dtype, tokens,
                                        dev_out ? static_cast<float *>(out) : st->h);
         p.n_layers = L;
-        for (int l = 0; l < L; ++l) p.layer[l] = decode_layer(st->layers[l]);
+        for (int l = 0; l < L; ++l) set_decode_layer(p, l, st->layers[l]);
         p.rmsnorm = 1;
         p.residual = 1;
         p.eps = st->eps;
-        if (try_decode(p, caller)) {
+        const int r = try_decode(p, caller);
+        if (r > 0) {
             if (!dev_out) UMSX_CUDA(cudaMemcpyAsync(out, st->h, out_bytes, out_kind, caller));
             return UMSX_OK;
         }
+        if (r < 0) return fail(UMSX_EUNSUPPORTED, "UMSX_DECODE_PATH=tc: the tensor-core decode kernel cannot serve this call");
     }
     UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
     UMSX_CUDA(cudaStreamWaitEvent(st->stream, st->ev_in, 0));

@@ -110,14 +110,6 @@ __device__ __forceinline__ void quantize_record(float v, uint8_t *rec, float *sc
     if (lane == 0) *scale = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
 }
 
-// Thread 0: bulk-copies the router rows of experts c, c + nC, ... (n_rows of them) into smem.
-__device__ __forceinline__ void load_router_rows(const float *router_w, int c, int nC, int n_rows, int H, float *wrow,
-                                                 uint64_t *bar) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier generic reads of wrow come first
-    mbar_expect_tx(bar, (uint32_t)(n_rows * H * 4));
-    for (int j = 0; j < n_rows; ++j) bulk_g2s(wrow + (size_t)j * H, router_w + (size_t)(c + j * nC) * H, H * 4, bar);
-}
-
 // out4[i] = (residual ? h4[i] : 0) + sum_r w[t][r] * y[t*K + r] over float4 columns, rank order;
 // the loads of four ranks are in flight together.
 __device__ __forceinline__ float4 fold4(const float4 *y4, const float *w, int t, int K, int H4, int n4, float4 h,
@@ -158,6 +150,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
     __shared__ int ok_s, late_s;
     __shared__ int last_g[kGuGroups][MT];
     __shared__ __align__(8) uint64_t wbar;
+    __shared__ __align__(16) float wbias[kDecRouterRows][4];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nC = gridDim.x, c = blockIdx.x;
@@ -179,7 +172,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
     if (tid == 0) {
         mbar_init(&wbar, 1);
         late_s = 0;
-        if (my_e > 0) load_router_rows(p.layer[0].router_w, c, nC, my_e, H, sm.wrow, &wbar);
+        if (my_e > 0) load_router_rows(p.layer[0].router_w, p.layer[0].router_b, c, nC, my_e, H, sm.wrow, wbias, &wbar);
     }
     // h <- x
     if (p.x_dtype == UMSX_DTYPE_BF16) {
@@ -223,7 +216,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
         __syncthreads();
         if (warp < n_lw) {
             // logits of (expert, token) pairs: 32 strided FMA chains, then the xor tree
-            const float rb = Ld.router_b ? __ldg(Ld.router_b + c + nC * (warp / T)) : 0.0f;  // in flight meanwhile
             if (!mbar_wait_bounded(&wbar, wphase, kWaitLimitCycles) && lane == 0) late_s = 1;
             for (int q = warp; q < n_lw; q += kDecWarps) {
                 const int j = q / T, t = q - j * T, e = c + nC * j;
@@ -243,16 +235,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                         if (k0 + 32 * i < H) acc = __fmaf_rn(w[i], __fmul_rn(x[i], inv), acc);
                 }
                 float lg = warp_tree_sum(acc);
-                if (Ld.router_b) lg = __fadd_rn(lg, q == warp ? rb : __ldg(Ld.router_b + e));
+                if (Ld.router_b) lg = __fadd_rn(lg, wbias[j][e & 3]);
                 if (lane == 0) __stcg(p.logits + (size_t)t * E + e, lg);
             }
         } else {
-            // Q8_0 records of the normalised rows (the gate_up activations): blocks c, c + #CTAs, ...
-            // here, all of them copied back by every CTA after the barrier
-            for (int it = c + nC * (warp - n_lw); it < T * nb; it += nC * (kDecWarps - n_lw)) {
+            // Q8_0 records of the normalised rows (the gate_up activations), every CTA its own copy,
+            // made by the warps that have no logit to compute
+            for (int it = warp - n_lw; it < T * nb; it += kDecWarps - n_lw) {
                 const int t = it / nb, b = it - t * nb;
                 const float v = __fmul_rn(sm.hs[(size_t)t * H + b * 32 + lane], inv_s[t]);
-                quantize_record(v, p.xr + ((size_t)t * nb + b) * 64, p.xr_sc + (size_t)t * pad4(nb) + b, lane);
+                quantize_record(v, sm.xrec + ((size_t)t * nb + b) * 64, sm.xsc + (size_t)t * pad4(nb) + b, lane);
             }
         }
         wphase ^= 1u;
@@ -271,11 +263,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             float w;
             select_topk<kDecodeMaxExperts / 32>(p.logits + (size_t)warp * E, E, K, p.routing, p.routed_scale, lane, sel, w);
             if (lane < K) { sel_e[warp * K + lane] = sel; sel_w[warp * K + lane] = w; }
-        } else {
-            const int tt = tid - T * 32, nt = kDecThreads - T * 32;
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.xr);
-            for (int i = tt; i < T * nb * 4; i += nt) reinterpret_cast<uint4 *>(sm.xrec)[i] = __ldcg(src + i);
-            for (int i = tt; i < T * pad4(nb); i += nt) sm.xsc[i] = __ldcg(p.xr_sc + i);
         }
         __syncthreads();
         if (warp == 0) {
@@ -381,7 +368,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
 
         // ---- D: down units -----------------------------------------------------------
         if (tid == 0 && my_e > 0 && l + 1 < p.n_layers)
-            load_router_rows(p.layer[l + 1].router_w, c, nC, my_e, H, sm.wrow, &wbar);
+            load_router_rows(p.layer[l + 1].router_w, p.layer[l + 1].router_b, c, nC, my_e, H, sm.wrow, wbias, &wbar);
         int jb = 0;
         if (v_lo < v_hi) {
             const int s_lo = v_lo / G2, s_hi = (v_hi - 1) / G2;

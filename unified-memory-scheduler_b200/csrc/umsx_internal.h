@@ -27,6 +27,11 @@ struct Matrix {
     uint8_t *codes = nullptr;   // code plane, all local experts
     uint8_t *scales = nullptr;  // exponent / fp16-scale plane
     uint8_t *emax = nullptr;    // MXFP4: largest block exponent of every row [experts][rows] (prefill rebase)
+    // MXFP4 tensor-core copy, pre-swizzled operand tiles: [experts][K stage][row group of 16][8-row half]
+    // [block pair q][8 rows][32 B]; a K stage = 4 block pairs (256 values, e2m1, element 2i in the low
+    // nibble); 16-byte chunk c of row r8 at c ^ ((r8 >> 2) & 1) (the 32-byte swizzle); the last stage
+    // is zero-padded
+    uint8_t *tc_codes = nullptr;
     int rows = 0;               // N per expert
     int cols = 0;               // K
     int quant = 0;
@@ -35,6 +40,8 @@ struct Matrix {
         if (quant == UMSX_QUANT_MXFP4) return (size_t)(rows / 16) * (((cols / 64) + 3) / 4) * 128;
         return (size_t)rows * (cols / 32) * 2;
     }
+    __host__ __device__ int tc_stages() const { return (cols + 255) / 256; }
+    __host__ __device__ size_t tc_bytes_per_expert() const { return (size_t)rows * tc_stages() * 128; }
 };
 
 // Routing/dispatch state that the router writes and the expert kernels read.
@@ -128,6 +135,8 @@ struct DecodeLayer {
     const uint8_t *dn_codes;  // down planes [E][H][I]
     const uint8_t *dn_scales;
     const float *dn_bias;     // [E][H] or null
+    const uint8_t *gu_tc;     // tensor-core copies (Matrix::tc_codes) or null
+    const uint8_t *dn_tc;
 };
 
 struct DecodeParams {
@@ -152,11 +161,18 @@ struct DecodeParams {
     uint32_t *act_done;  // [T*K][I/32] arrival counters (zeroed by the launcher)
     unsigned *bar;     // grid barrier counter (zeroed by the launcher)
     uint32_t *err;     // set when a grid barrier wait ran out
+    // tensor-core variant (one token): plain Q8_0 activation codes and scales
+    int8_t *act_q8;    // [T*K][I]
+    float *act_q8_sc;  // [T*K][I/32]
+    int tc_ready;      // every layer has its tensor-core copies
 };
 
 bool decode_supported(int tokens, int hidden, int inter, int experts, int top_k, int n_layers);
 // Returns 1 (kernels launched) or -1 if this device cannot hold the kernel resident on every SM.
 int launch_decode(const DecodeParams &p, cudaStream_t s);
+// The tensor-core variant for one token (gu_tc / dn_tc / act_q8 set); same contract and bits.
+bool decode_tc_supported(int tokens, int hidden, int inter, int experts, int top_k);
+int launch_decode_tc(const DecodeParams &p, cudaStream_t s);
 
 // Prefill grouped GEMM (umsx_prefill.cu): tcgen05 kind::f16 over the experts' job segments.
 constexpr int kPrefillMinTokens = 65;  // from this many tokens an MXFP4 layer takes the tensor-core path

@@ -352,4 +352,17 @@ __device__ __forceinline__ float mx_row_total(const float (&lo)[4], const float 
     return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
 }
 
+// Thread 0: bulk-copies the router rows of experts c, c + nC, ... (n_rows of them) into smem, and
+// for each the 16-byte aligned group of four router biases that holds its bias.
+__device__ __forceinline__ void load_router_rows(const float *router_w, const float *router_b, int c, int nC,
+                                                 int n_rows, int H, float *wrow, float (*wbias)[4], uint64_t *bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier generic reads of wrow come first
+    mbar_expect_tx(bar, (uint32_t)(n_rows * (H * 4 + (router_b ? 16 : 0))));
+    for (int j = 0; j < n_rows; ++j) {
+        const int e = c + j * nC;
+        bulk_g2s(wrow + (size_t)j * H, router_w + (size_t)e * H, H * 4, bar);
+        if (router_b) bulk_g2s(wbias[j], router_b + (e & ~3), 16, bar);
+    }
+}
+
 }  // namespace umsx
