@@ -106,8 +106,9 @@ _TC_SHAPES = [dict(), dict(hidden=320, intermediate=128, experts=16, top_k=8), d
 @pytest.mark.parametrize("path", ["tc", "simt"])
 @pytest.mark.parametrize("shape", range(len(_TC_SHAPES)))
 def test_one_token_layer_bit_exact(oracle, monkeypatch, path, shape):
-    """UMSX_DECODE_PATH=tc requires the tensor-core kernel (the call fails if it cannot run),
-    =simt the SIMT kernel; both must reproduce the oracle's bits.  The shapes cover a
+    """UMSX_DECODE_PATH=tc (set before the layer is created, which then keeps the tensor-core
+    weight copy) requires the tensor-core kernel (the call fails if it cannot run), =simt the SIMT
+    kernel; both must reproduce the oracle's bits.  The shapes cover a
     partial last K stage (5 block pairs), top-8, and more experts than a CTA's router rows
     hold at once."""
     monkeypatch.setenv("UMSX_DECODE_PATH", path)
@@ -162,6 +163,7 @@ def test_tensor_core_decode_matches_simt_gpt_oss_120b_shape(monkeypatch):
     per-stage kernels give identical bits for one token."""
     from tests.helpers import C
     cfg = C.GPT_OSS_120B
+    monkeypatch.setenv("UMSX_DECODE_PATH", "tc")  # at creation: the layers keep the tensor-core weight copy
     layers = [U.MoeLayer(cfg.desc(max_tokens=1), synthetic=cfg.synthetic(layer=l)) for l in range(3)]
     stack = umsx.MoeStack(layers, max_tokens=1)
     rng = np.random.default_rng(11)

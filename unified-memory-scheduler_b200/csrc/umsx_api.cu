@@ -103,6 +103,14 @@ struct umsx_moe {
 
 namespace {
 
+// The tensor-core decode kernel reads a second copy of the MXFP4 codes (Matrix::tc_codes, as
+// large as the codes themselves); it is made only when UMSX_DECODE_PATH asks for that kernel
+// ("tc" or "tc-auto") at the time the layer is created.
+bool tc_copy_wanted() {
+    const char *v = std::getenv("UMSX_DECODE_PATH");
+    return v && (!std::strcmp(v, "tc") || !std::strcmp(v, "tc-auto"));
+}
+
 umsx_status validate_desc(const umsx_moe_desc *d) {
     if (!d) return fail(UMSX_EINVAL, "null descriptor");
     if (d->hidden <= 0 || d->hidden % 64 || d->intermediate <= 0 || d->intermediate % 64)
@@ -132,7 +140,7 @@ size_t weight_bytes(const umsx_moe *m, Arena &a) {
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
         mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
-        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
+        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 && tc_copy_wanted() ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
     };
     Matrix tmp;
     if (d.fused_gate_up) mat(tmp, 2 * I, H);
@@ -154,7 +162,7 @@ void carve_weights(umsx_moe *m, Arena &a) {
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
         mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
-        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
+        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 && tc_copy_wanted() ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
     };
     if (d.fused_gate_up) mat(m->gate_up, 2 * I, H);
     else { mat(m->gate, I, H); mat(m->up, I, H); }

@@ -162,8 +162,9 @@ __device__ __forceinline__ uint32_t digit_codes(int q) {
 // Writes the digit planes of `codes` (npairs block pairs) into B: row n = 24h + 8j + l of pair p
 // holds digit plane j of the four values of int lane l of block 2p + h; all other bytes stay
 // zero.  Layout per stage (6 KB): [atom n / 8][pair in stage][8 rows][32 B], 32-byte swizzle.
-__device__ void build_planes(const int8_t *codes, int npairs, uint8_t *sB) {
-    for (int item = threadIdx.x; item < npairs * 16; item += blockDim.x) {
+// Threads t0 .. t0 + nt - 1 of the caller share the work.
+__device__ void build_planes(const int8_t *codes, int npairs, uint8_t *sB, int t0, int nt) {
+    for (int item = t0; item < npairs * 16; item += nt) {
         const int pr = item >> 4, h = (item >> 3) & 1, l = item & 7;
         const int e0 = 64 * pr + 32 * h + 4 * l;  // first element of the lane
         const uint32_t c4 = *reinterpret_cast<const uint32_t *>(codes + e0);
@@ -208,6 +209,8 @@ __device__ __forceinline__ TileSpan tile_at(int u, int u_hi, int per_slot, int m
 
 // The 24 result columns of this warp's chain for two block pairs (pair 0 at taddr, pair 1 at
 // taddr + kDPair), loaded and waited for in one block so that no use can move above the wait.
+// Volatile asm keeps its place among the barrier waits and tcgen05 fences; no memory clobber, so
+// that shared-memory loads may overlap it.
 __device__ __forceinline__ void tmem_ld_two_pairs(uint32_t taddr, uint32_t (&a)[24], uint32_t (&b)[24]) {
     asm volatile(
         "{\n\t"
@@ -218,59 +221,63 @@ __device__ __forceinline__ void tmem_ld_two_pairs(uint32_t taddr, uint32_t (&a)[
         "tcgen05.wait::ld.sync.aligned;\n\t}"
         : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15]), "=r"(a[16]), "=r"(a[17]), "=r"(a[18]), "=r"(a[19]), "=r"(a[20]), "=r"(a[21]), "=r"(a[22]), "=r"(a[23]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15]), "=r"(b[16]), "=r"(b[17]), "=r"(b[18]), "=r"(b[19]), "=r"(b[20]), "=r"(b[21]), "=r"(b[22]), "=r"(b[23])
         : "r"(taddr), "r"(taddr + 16), "r"(taddr + kDPair), "r"(taddr + kDPair + 16)
-        : "memory");
+        );
 }
 
 // One fp32 chain (block parity h) of one row over `npairs` block pairs, read stage by stage
 // (4 pairs) from the TMEM ring: acc[l] = fma(d_b, L_l, acc[l]) over the blocks b = 2p + h.
 // tcol: this warp's lanes and chain columns; ex: the row's exponent words of parity h in the
-// tiled scale plane (quad qd at ex[32 qd], byte = pair in the quad), prefetched four quads
-// ahead; sc: the activation's block scales.  A warp with no row in the tile (live = false)
-// still waits for and releases every ring stage, which keeps the ring's phases in step.
+// tiled scale plane (quad qd at ex[32 qd], byte = pair in the quad), all loaded at the start so
+// that one memory latency covers the tile; sc: the activation's block scales.  A warp with no
+// row in the tile (live = false) still waits for and releases every ring stage, which keeps the
+// ring's phases in step.
 __device__ __forceinline__ void chain8(uint32_t tcol, uint64_t *dfull, uint64_t *dfree, uint32_t &gd, int npairs,
                                        const uint32_t *ex, const float *sc, int h, bool live, uint32_t *err,
                                        float (&acc)[8]) {
 #pragma unroll
     for (int l = 0; l < 8; ++l) acc[l] = 0.0f;
     const int nq = (npairs + 3) / 4;
-    uint32_t w[4];
+    uint32_t w[kBStages];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) w[k] = live && k < nq ? __ldg(ex + 32 * k) : 0u;
-    for (int q0 = 0; q0 < nq; q0 += 4) {
+    for (int k = 0; k < kBStages; ++k) w[k] = live && k < nq ? __ldg(ex + 32 * k) : 0u;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int qd = q0 + k;
-            if (qd < nq) {
-                const uint32_t we = w[k];
-                if (live && qd + 4 < nq) w[k] = __ldg(ex + 32 * (qd + 4));
-                const int ds = (int)(gd % kDStages);
-                wait_tc(&dfull[ds], (gd / kDStages) & 1u, err);
-                tc::fence_after_sync();
-                if (live) {
+    for (int qd = 0; qd < kBStages; ++qd) {
+        if (qd < nq) {
+            const uint32_t we = w[qd];
+            const int ds = (int)(gd % kDStages);
+            if ((threadIdx.x & 31) == 0) wait_tc(&dfull[ds], (gd / kDStages) & 1u, err);  // one poller per warp
+            __syncwarp();
+            tc::fence_after_sync();
+            if (live) {
+                float dq[4];  // block factors of the stage's pairs, ready before the loads land
 #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        uint32_t v[2][24];
-                        tmem_ld_two_pairs(tcol + ds * 4 * kDPair + 2 * hf * kDPair, v[0], v[1]);
+                for (int i = 0; i < 4; ++i) {
+                    const int pr = min(4 * qd + i, npairs - 1);
+                    dq[i] = __fmul_rn(sc[2 * pr + h], e8m0_half((we >> (8 * i)) & 0xffu));
+                }
 #pragma unroll
-                        for (int i2 = 0; i2 < 2; ++i2) {
-                            const int i = 2 * hf + i2, pr = 4 * qd + i;
-                            if (pr < npairs) {
-                                const float d = __fmul_rn(sc[2 * pr + h], e8m0_half((we >> (8 * i)) & 0xffu));
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t v[2][24];
+                    tmem_ld_two_pairs(tcol + ds * 4 * kDPair + 2 * hf * kDPair, v[0], v[1]);
 #pragma unroll
-                                for (int l = 0; l < 8; ++l) {
-                                    const float L = __fadd_rn(__fadd_rn(__uint_as_float(v[i2][l]), __uint_as_float(v[i2][8 + l])),
-                                                              __uint_as_float(v[i2][16 + l]));
-                                    acc[l] = __fmaf_rn(d, L, acc[l]);
-                                }
+                    for (int i2 = 0; i2 < 2; ++i2) {
+                        const int i = 2 * hf + i2, pr = 4 * qd + i;
+                        if (pr < npairs) {
+                            const float d = dq[i];
+#pragma unroll
+                            for (int l = 0; l < 8; ++l) {
+                                const float L = __fadd_rn(__fadd_rn(__uint_as_float(v[i2][l]), __uint_as_float(v[i2][8 + l])),
+                                                          __uint_as_float(v[i2][16 + l]));
+                                acc[l] = __fmaf_rn(d, L, acc[l]);
                             }
                         }
                     }
                 }
-                tc::fence_before_sync();
-                __syncwarp();
-                if ((threadIdx.x & 31) == 0) tc::mbar_arrive(&dfree[ds]);
-                ++gd;
             }
+            tc::fence_before_sync();
+            __syncwarp();
+            if ((threadIdx.x & 31) == 0) tc::mbar_arrive(&dfree[ds]);
+            ++gd;
         }
     }
 }
@@ -465,10 +472,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_decode_tc(const __grid_consta
                 p.ids_out[lane] = sel;
                 p.w_out[lane] = w;
             }
+        } else {
+            // meanwhile the gate_up digit planes of x (B is idle: the previous layer's MMAs all
+            // completed before the last grid barrier)
+            build_planes(xq, H / 64, sB, tid - 32, kTcThreads - 32);
+            tc::fence_proxy_async();
         }
-        // the gate_up digit planes of x (every gate_up tile reads them)
-        build_planes(xq, H / 64, sB);
-        tc::fence_proxy_async();
         __syncthreads();
         const int n_slots = n_slots_s;
 
@@ -495,7 +504,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_decode_tc(const __grid_consta
                             __ldcg(reinterpret_cast<const uint4 *>(p.act_q8 + (size_t)job * I) + i);
                     for (int i = tid; i < nbI; i += kTcThreads) xqs[i] = __ldcg(p.act_q8_sc + (size_t)job * nbI + i);
                     __syncthreads();
-                    build_planes(xq, npairs, sB);
+                    build_planes(xq, npairs, sB, tid, kTcThreads);
                     tc::fence_proxy_async();
                     __syncthreads();
                     built = job;
