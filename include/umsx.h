@@ -72,7 +72,7 @@ typedef struct umsx_moe_desc {
     float routed_scale;      /* weight multiplier for UMSX_ROUTE_SOFTMAX_TOPK (1.0 for DeepSeek-V2-Lite) */
     int32_t max_tokens;      /* largest T a forward call passes; sizes the handle's workspace */
     int32_t ep_rank;         /* expert-parallel rank: experts [ep_rank*E/ep_world, ...) are resident */
-    int32_t ep_world;        /* 1 for a single GPU */
+    int32_t ep_world;        /* 1 for a single GPU; > 1: see umsx_moe_forward_jobs */
 } umsx_moe_desc;
 
 /* HOST pointers in ggml layouts (what a GGUF holds); create() copies the
@@ -114,6 +114,18 @@ umsx_status umsx_moe_forward(umsx_moe *moe, const void *x, int x_dtype, int toke
  * synchronous host-vector contract, quantized_cuda.cu:413-453). */
 umsx_status umsx_moe_forward_host(umsx_moe *moe, const void *x, int x_dtype, int tokens, float *out,
                                   umsx_stream stream);
+
+/* Expert parallelism, one rank's share of a layer (no counterpart in the reference, which runs
+ * on one GPU): routes all `tokens` rows (the router is replicated on every rank), runs the
+ * experts this handle holds (desc.ep_rank of desc.ep_world: experts [ep_rank*E/ep_world, ...))
+ * for the (token, rank) jobs that chose them, and writes their outputs to y[t][r][:] (fp32
+ * [T][k][H], expert bias included, 16-byte aligned device buffer); rows of jobs whose expert
+ * lives on another rank are left untouched.  ids/weights [T][k] (may be NULL) as umsx_route.
+ * The caller moves every row to the token's rank and combines there in rank order with
+ * umsx_combine, which gives the single-GPU layer's bits (each row is computed by the same
+ * kernels from the same inputs).  umsx_moe_forward and stacks refuse expert-parallel handles. */
+umsx_status umsx_moe_forward_jobs(umsx_moe *moe, const void *x, int x_dtype, int tokens, int32_t *ids,
+                                  float *weights, float *y, umsx_stream stream);
 
 /* Router only: logits (fixed fp32 reduction order), softmax/top-k/renormalise per
  * desc.routing, ties to the lowest expert index (topk-tie-probe.cpp:111-113),

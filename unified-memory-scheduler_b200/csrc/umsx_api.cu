@@ -124,7 +124,6 @@ umsx_status validate_desc(const umsx_moe_desc *d) {
     const int world = d->ep_world <= 0 ? 1 : d->ep_world;
     if (d->experts % world || d->ep_rank < 0 || d->ep_rank >= world)
         return fail(UMSX_EINVAL, "experts must split evenly over ep_world and 0 <= ep_rank < ep_world");
-    if (world != 1) return fail(UMSX_EUNSUPPORTED, "expert-parallel handles are created per rank with ep_world == 1 in this build");
     return UMSX_OK;
 }
 
@@ -567,8 +566,11 @@ bool prefill_eligible(const umsx_moe *m, const Workspace &ws, int tokens) {
            m->e_local <= 1024;
 }
 
+// y_jobs (expert parallelism): instead of combining, write each resident job's output to
+// y_jobs[t][r][:] and leave the other rows alone.
 umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
-                        const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev) {
+                        const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
+                        float *y_jobs = nullptr) {
     const auto &d = m->d;
     const int K = d.top_k, H = d.hidden, I = d.intermediate, jobs = tokens * K;
     if (ev) if (umsx_status st = mark(ev[0], s)) return st;
@@ -590,7 +592,8 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
         rp.eps = eps;
         UMSX_LAUNCHED(launch_router_tiled(rp, ws.disp, s));
     }
-    UMSX_LAUNCHED(launch_prefill_pack(ws.disp, jobs, K, H, ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));
+    UMSX_LAUNCHED(launch_prefill_pack(ws.disp, jobs, m->e_local == d.experts ? nullptr : ws.disp.offsets + m->e_local, K, H,
+                                      ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));
     if (ev) if (umsx_status st = mark(ev[1], s)) return st;
     MoeGemmParams g{};
     g.codes = m->gate_up.codes;
@@ -633,15 +636,22 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
     if (n < 0) return fail(UMSX_EDEVICE, "prefill down: tensor map or launch setup failed");
     UMSX_LAUNCHED(n);
     if (ev) if (umsx_status st = mark(ev[3], s)) return st;
+    if (y_jobs) {
+        UMSX_LAUNCHED(launch_prefill_scatter(ws.y, ws.inv, ws.disp.ids, m->e_lo, m->e_local, tokens, K, H, y_jobs, s));
+        return UMSX_OK;
+    }
     UMSX_LAUNCHED(launch_prefill_combine(ws.y, ws.disp.weights, ws.inv, tokens, K, H, residual, out, s));
     if (ev) if (umsx_status st = mark(ev[4], s)) return st;
     return UMSX_OK;
 }
 
+// y_jobs: as run_prefill.
 umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
-                      const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev) {
+                      const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
+                      float *y_jobs = nullptr) {
     const auto &d = m->d;
-    if (prefill_eligible(m, ws, tokens)) return run_prefill(m, ws, x, x_dtype, tokens, out, residual, rmsnorm, eps, s, ev);
+    if (prefill_eligible(m, ws, tokens))
+        return run_prefill(m, ws, x, x_dtype, tokens, out, residual, rmsnorm, eps, s, ev, y_jobs);
     if (ev) if (umsx_status st = mark(ev[0], s)) return st;
     if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s, 1)) return st;
     if (ev) if (umsx_status st = mark(ev[1], s)) return st;
@@ -669,9 +679,9 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     p.m = m->down;
     p.bias = m->down_bias;
     p.a_by_job = 1;
-    p.out = ws.y;
+    p.out = y_jobs ? y_jobs : ws.y;
     p.o_ts = d.top_k;
-    if (!ev) {
+    if (!ev && !y_jobs) {
         // down + fused rank-order combine (+ residual); the down weights follow from the
         // router's slot records, so their loads start before gate_up has finished
         p.tile_done = ws.disp.tile_done;
@@ -684,6 +694,7 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     if (d.quant == UMSX_QUANT_MXFP4) { p.a_rec = ws.act_rec; p.a_rsc = ws.act_sc; }  // bulk-copied records
     else { p.a_codes = ws.act_codes; p.a_scales = ws.act_scales; }
     UMSX_LAUNCHED(launch_gemv(p, ws.disp, slots, tokens, s));
+    if (y_jobs) return UMSX_OK;
     if (ev) {  // timed stages keep the combine a kernel of its own so that every stage has a boundary
         if (umsx_status st = mark(ev[3], s)) return st;
         UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, s));
@@ -712,6 +723,8 @@ umsx_status umsx_moe_forward(umsx_moe *m, const void *x, int x_dtype, int tokens
                              float *weights, umsx_stream stream) {
     if (umsx_status st = check_call(m, x, x_dtype, tokens, m ? m->d.max_tokens : 0)) return st;
     if (!out) return fail(UMSX_EINVAL, "null output");
+    if (m->e_local != m->d.experts)
+        return fail(UMSX_EUNSUPPORTED, "expert-parallel handle: use umsx_moe_forward_jobs and combine on the token's rank");
     std::lock_guard<std::mutex> lock(m->mu);
     UMSX_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -722,9 +735,25 @@ umsx_status umsx_moe_forward(umsx_moe *m, const void *x, int x_dtype, int tokens
     return UMSX_OK;
 }
 
+umsx_status umsx_moe_forward_jobs(umsx_moe *m, const void *x, int x_dtype, int tokens, int32_t *ids, float *weights,
+                                  float *y, umsx_stream stream) {
+    if (umsx_status st = check_call(m, x, x_dtype, tokens, m ? m->d.max_tokens : 0)) return st;
+    if (!y || reinterpret_cast<uintptr_t>(y) % 16) return fail(UMSX_EINVAL, "y must be a 16-byte aligned device buffer");
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (umsx_status st = run_layer(m, m->ws, x, x_dtype, tokens, nullptr, nullptr, 0, 0.0f, s, nullptr, y)) return st;
+    const size_t n = (size_t)tokens * m->d.top_k;
+    if (ids) UMSX_CUDA(cudaMemcpyAsync(ids, m->ws.disp.ids, n * 4, cudaMemcpyDeviceToDevice, s));
+    if (weights) UMSX_CUDA(cudaMemcpyAsync(weights, m->ws.disp.weights, n * 4, cudaMemcpyDeviceToDevice, s));
+    return UMSX_OK;
+}
+
 umsx_status umsx_moe_forward_host(umsx_moe *m, const void *x, int x_dtype, int tokens, float *out, umsx_stream stream) {
     if (umsx_status st = check_call(m, x, x_dtype, tokens, m ? m->d.max_tokens : 0)) return st;
     if (!out) return fail(UMSX_EINVAL, "null output");
+    if (m->e_local != m->d.experts)
+        return fail(UMSX_EUNSUPPORTED, "expert-parallel handle: use umsx_moe_forward_jobs and combine on the token's rank");
     std::lock_guard<std::mutex> lock(m->mu);
     UMSX_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -980,6 +1009,8 @@ umsx_status umsx_stack_create(umsx_moe *const *layers, int n_layers, int max_tok
         if (!m || m->device != l0->device || m->d.hidden != l0->d.hidden || m->d.top_k != l0->d.top_k ||
             m->d.experts != l0->d.experts || m->d.intermediate != l0->d.intermediate || m->e_local != l0->e_local)
             return fail(UMSX_EINVAL, "stack layers must share device and shape");
+        if (m->e_local != m->d.experts)
+            return fail(UMSX_EUNSUPPORTED, "a stack runs whole layers; expert-parallel handles use umsx_moe_forward_jobs");
     }
     if (max_tokens <= 0 || max_tokens > 65535) return fail(UMSX_EINVAL, "max_tokens must be in [1, 65535]");
     UMSX_CUDA(cudaSetDevice(l0->device));

@@ -196,8 +196,12 @@ struct MoeGemmParams {
 // x -> Q8_0 (lane-pair order), then the dispatch build.
 int launch_router_tiled(const RouterParams &p, const Dispatch &d, cudaStream_t s);
 int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, cudaStream_t s);
-int launch_prefill_pack(const Dispatch &d, int jobs, int K, int hidden, void *a_hi, void *a_lo, int32_t *inv,
-                        cudaStream_t s);
+// n_jobs: device count of the resident experts' jobs (offsets[e_local]) bounding `jobs`, or null.
+int launch_prefill_pack(const Dispatch &d, int jobs, const int32_t *n_jobs, int K, int hidden, void *a_hi, void *a_lo,
+                        int32_t *inv, cudaStream_t s);
+// y[t][r] = yj[inv[t][r]] for the (t, r) whose expert id lies in [e_lo, e_lo + e_local).
+int launch_prefill_scatter(const float *yj, const int32_t *inv, const int32_t *ids, int e_lo, int e_local, int tokens,
+                           int K, int width, float *y, cudaStream_t s);
 int launch_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
                            const float *residual, float *out, cudaStream_t s);
 int launch_moe_gemm(const MoeGemmParams &p, const void *act_hi, const void *act_lo, int rows_total, cudaStream_t s);

@@ -443,9 +443,10 @@ __global__ void k_select_quant(const void *x, int x_dtype, int tokens, int H, in
 // Job rows in expert order as f16 Q8_0 values (codes from the router's quantizer) and the
 // inverse map (token, rank) -> job row.
 __global__ void k_prefill_pack(const uint8_t *xq_codes, const float *xq_scales, const int32_t *job_token,
-                               const int32_t *job_rank, int jobs, int K, int hidden, __half *a_hi, __half *a_lo,
-                               int32_t *inv) {
+                               const int32_t *job_rank, int jobs, const int32_t *n_jobs, int K, int hidden,
+                               __half *a_hi, __half *a_lo, int32_t *inv) {
     const int nb = hidden / 32;
+    if (n_jobs) jobs = min(jobs, __ldg(n_jobs));  // the jobs of the resident experts (expert parallelism)
     const size_t total = (size_t)jobs * hidden;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int pos = (int)(i / hidden), k = (int)(i - (size_t)pos * hidden);
@@ -470,6 +471,21 @@ __global__ void k_prefill_combine(const float *y, const float *w, const int32_t 
             acc = __fadd_rn(acc, __fmul_rn(__ldg(w + (size_t)t * K + r),
                                            __ldcg(y + (size_t)__ldg(inv + (size_t)t * K + r) * width + n)));
         out[i] = residual ? __fadd_rn(residual[i], acc) : acc;
+    }
+}
+
+// y[t][r][:] = yj[inv[t][r]][:] for the jobs whose expert is resident (e_lo <= id < e_lo + e_local);
+// the other rows of y are left as they are.
+__global__ void k_prefill_scatter(const float *yj, const int32_t *inv, const int32_t *ids, int e_lo, int e_local,
+                                  int tokens, int K, int width, float *y) {
+    const int w4 = width / 4;
+    const size_t total = (size_t)tokens * K * w4;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t job = i / w4;
+        const int n = (int)(i - job * w4), e = __ldg(ids + job) - e_lo;
+        if (e < 0 || e >= e_local) continue;
+        reinterpret_cast<float4 *>(y)[job * w4 + n] =
+            __ldcg(reinterpret_cast<const float4 *>(yj) + (size_t)__ldg(inv + job) * w4 + n);
     }
 }
 
@@ -520,10 +536,16 @@ int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, cudaStream_t s)
     return 1;
 }
 
-int launch_prefill_pack(const Dispatch &d, int jobs, int K, int hidden, void *a_hi, void *a_lo, int32_t *inv,
-                        cudaStream_t s) {
-    k_prefill_pack<<<148 * 8, 256, 0, s>>>(d.xq_codes, d.xq_scales, d.job_token, d.job_rank, jobs, K, hidden,
+int launch_prefill_pack(const Dispatch &d, int jobs, const int32_t *n_jobs, int K, int hidden, void *a_hi, void *a_lo,
+                        int32_t *inv, cudaStream_t s) {
+    k_prefill_pack<<<148 * 8, 256, 0, s>>>(d.xq_codes, d.xq_scales, d.job_token, d.job_rank, jobs, n_jobs, K, hidden,
                                            static_cast<__half *>(a_hi), static_cast<__half *>(a_lo), inv);
+    return 1;
+}
+
+int launch_prefill_scatter(const float *yj, const int32_t *inv, const int32_t *ids, int e_lo, int e_local, int tokens,
+                           int K, int width, float *y, cudaStream_t s) {
+    k_prefill_scatter<<<148 * 8, 256, 0, s>>>(yj, inv, ids, e_lo, e_local, tokens, K, width, y);
     return 1;
 }
 

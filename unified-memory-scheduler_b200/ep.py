@@ -1,0 +1,93 @@
+"""Expert parallelism over torch.distributed, one process per GPU.
+
+Rank g of G holds experts [g*E/G, (g+1)*E/G) of every layer (a MoeLayer created with
+ep_rank=g, ep_world=G).  The input rows are on every rank (the router is replicated, so every
+rank knows every job's expert); each rank runs the jobs of its own experts
+(umsx_moe_forward_jobs), then one all-to-all moves every job's output row to the rank that owns
+the token (contiguous token blocks), and that rank combines its tokens in rank order
+(umsx_combine).  Every output row is computed by the same kernels from the same inputs as on one
+GPU, so the result has the single-GPU layer's bits.  The exchange plan needs no count exchange:
+it follows from the routing, which all ranks share.
+
+The reference (appatalks/unified-memory-scheduler) runs a layer on one GPU (plus the host); this
+module is the multi-GPU extension of its layer call (`ExpertPlan::execute`,
+tools/engine/expert_dispatch.cpp:22-89, whose combine loop :77-87 is the per-token rank-order sum
+done here on the token's rank).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def token_range(tokens: int, world: int, rank: int) -> tuple[int, int]:
+    """Tokens [t0, t1) that `rank` combines: contiguous blocks, the first tokens % world ranks one longer."""
+    base, extra = divmod(tokens, world)
+    t0 = rank * base + min(rank, extra)
+    return t0, t0 + base + (1 if rank < extra else 0)
+
+
+def token_ranks(tokens: int, world: int) -> torch.Tensor:
+    """Rank that combines each token (the inverse of token_range)."""
+    owner = torch.empty(tokens, dtype=torch.int64)
+    for r in range(world):
+        t0, t1 = token_range(tokens, world, r)
+        owner[t0:t1] = r
+    return owner
+
+
+def plan_exchange(ids: torch.Tensor, experts: int, world: int, rank: int):
+    """The all-to-all of one layer for `rank`, from the routing ids [T, k] shared by all ranks.
+
+    Returns (send_jobs, send_sizes, recv_jobs, recv_sizes): send_jobs are the job indices t*k + r
+    whose expert is on this rank, grouped by destination rank (the token's rank), ascending within
+    a group; recv_jobs are the job indices of this rank's tokens grouped by source rank (the
+    expert's rank), ascending within a group, which is the order the rows arrive in."""
+    T, K = ids.shape
+    per = experts // world
+    owner = ids.to("cpu", torch.int64).reshape(-1) // per
+    dest = token_ranks(T, world).repeat_interleave(K)
+    jobs = torch.arange(T * K)
+    mine = owner == rank
+    send = [jobs[mine & (dest == d)] for d in range(world)]
+    recv = [jobs[(dest == rank) & (owner == s)] for s in range(world)]
+    return (torch.cat(send), [int(a.numel()) for a in send], torch.cat(recv), [int(a.numel()) for a in recv])
+
+
+def exchange(y: torch.Tensor, ids: torch.Tensor, experts: int, group=None) -> tuple[torch.Tensor, tuple[int, int]]:
+    """y [T, k, H]: this rank's job outputs (rows of its experts' jobs valid).  Returns the
+    complete job outputs of this rank's tokens, [t1 - t0, k, H], and (t0, t1)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    T, K, H = y.shape
+    send_jobs, send_sizes, recv_jobs, recv_sizes = plan_exchange(ids, experts, world, rank)
+    dev = y.device
+    send = y.reshape(T * K, H).index_select(0, send_jobs.to(dev))
+    recv = torch.empty((sum(recv_sizes), H), dtype=y.dtype, device=dev)
+    dist.all_to_all_single(recv, send, recv_sizes, send_sizes, group=group)
+    t0, t1 = token_range(T, world, rank)
+    mine = torch.empty(((t1 - t0) * K, H), dtype=y.dtype, device=dev)
+    mine.index_copy_(0, (recv_jobs - t0 * K).to(dev), recv)
+    return mine.reshape(t1 - t0, K, H), (t0, t1)
+
+
+class ExpertParallelLayer:
+    """One MoE layer split over the ranks of `group` by expert (see the module docstring)."""
+
+    def __init__(self, layer, group=None):
+        self.layer = layer
+        self.group = group
+        d = layer.desc
+        if d.ep_world != dist.get_world_size(group) or d.ep_rank != dist.get_rank(group):
+            raise ValueError("the layer's ep_rank / ep_world must match the process group")
+
+    def forward(self, x: torch.Tensor, stream=None):
+        """x [T, H] on this rank's GPU, the same rows on every rank.  Returns (out [t1 - t0, H] f32
+        for this rank's tokens, (t0, t1))."""
+        from .umsx import combine
+        y, ids, w = self.layer.forward_jobs(x, stream=stream)
+        mine, (t0, t1) = exchange(y, ids, self.layer.desc.experts, self.group)
+        if t1 == t0:  # fewer tokens than ranks: nothing to combine here
+            return torch.empty((0, self.layer.desc.hidden), dtype=torch.float32, device=x.device), (t0, t1)
+        out = combine(mine, w[t0:t1].contiguous(), stream=stream)
+        return out, (t0, t1)

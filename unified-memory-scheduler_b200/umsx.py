@@ -31,7 +31,8 @@ BLOCK_BYTES = {QUANT_Q8_0: 34, QUANT_MXFP4: 17}
 
 # exported symbols of include/umsx.h (the tests check each one is present)
 EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "umsx_moe_forward",
-           "umsx_moe_forward_host", "umsx_route", "umsx_expert_down_q8", "umsx_mul_mat_id", "umsx_combine",
+           "umsx_moe_forward_host", "umsx_moe_forward_jobs", "umsx_route", "umsx_expert_down_q8", "umsx_mul_mat_id",
+           "umsx_combine",
            "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_destroy", "umsx_stack_forward",
            "umsx_stack_forward_host", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_route_static",
            "umsx_kernel_launches", "umsx_last_error", "umsx_version"]
@@ -75,6 +76,7 @@ def lib():
         "umsx_moe_destroy": (None, [vp]),
         "umsx_moe_forward": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "umsx_moe_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
+        "umsx_moe_forward_jobs": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "umsx_route": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "umsx_expert_down_q8": (i32, [vp, vp, vp, i32, vp, vp]),
         "umsx_mul_mat_id": (i32, [vp, i32, vp, i32, vp, i32, i32, vp, vp]),
@@ -198,6 +200,19 @@ class MoeLayer:
         check(lib().umsx_moe_forward(self._h, _ptr(x), _dtype_code(x), T, _ptr(out), _ptr(ids), _ptr(weights),
                                      _stream(stream)))
         return out
+
+    def forward_jobs(self, x, y=None, ids=None, weights=None, stream=None):
+        """Expert-parallel share of the layer (umsx_moe_forward_jobs): routes all T rows, writes the
+        outputs of the jobs whose expert this handle holds into y [T, k, H] f32 (other rows untouched).
+        Returns (y, ids [T, k] int32, weights [T, k] f32)."""
+        import torch
+        T, K, H = x.shape[0], self.desc.top_k, self.desc.hidden
+        y = y if y is not None else torch.zeros((T, K, H), dtype=torch.float32, device=x.device)
+        ids = ids if ids is not None else torch.empty((T, K), dtype=torch.int32, device=x.device)
+        weights = weights if weights is not None else torch.empty((T, K), dtype=torch.float32, device=x.device)
+        check(lib().umsx_moe_forward_jobs(self._h, _ptr(x), _dtype_code(x), T, _ptr(ids), _ptr(weights), _ptr(y),
+                                          _stream(stream)))
+        return y, ids, weights
 
     def forward_host(self, x_host, out_host, stream=None):
         """x_host / out_host: pinned (or pageable) CPU torch tensors; synchronous."""
