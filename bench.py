@@ -8,7 +8,7 @@ generated on the device from seed 0 (~61 GB); inputs are seeded bf16 N(0,1)
 tokens drawn from a pool of 16 batches so that routing changes every step.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--mode decode|prefill]
-                  [--tokens T] [--layers L] [--impl umsx|reference]
+                  [--tokens T] [--layers L] [--impl umsx|reference] [--ep]
 
 With N > 1 (torchrun, one rank per GPU) every rank holds the whole stack and
 runs its own tokens (data-parallel replicas, weak scaling); the value is all
@@ -16,6 +16,12 @@ ranks' tokens over the slowest rank's time.  `--impl reference` times the
 reference's own CPU implementation of the path (tools/trace/exact_packed_cpu.h
 packed MXFP4 GEMV compiled from the reference sources into oracle/_ref/) on
 this host's cores, on rank 0 only.
+
+`--ep` (prefill) splits every layer's experts over the N ranks instead (expert parallelism,
+unified-memory-scheduler_b200/ep.py): all ranks see the same T tokens, each runs its experts'
+jobs, one NCCL all-to-all per layer brings the job outputs to the token's rank, which combines
+them; an all-gather then gives every rank the next layer's input (RMSNorm in torch between
+layers).  Total work is fixed as N grows (strong scaling).
 """
 from __future__ import annotations
 
@@ -50,6 +56,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the bounded CPU sample")
+    ap.add_argument("--ep", action="store_true", help="expert parallelism over the ranks (prefill)")
     a = ap.parse_args()
     if a.tokens is None:
         a.tokens = 1 if a.mode == "decode" else 4096
@@ -355,6 +362,112 @@ def gpu_arm(a):
         print(json.dumps(res))
 
 
+def ep_arm(a):
+    """Expert-parallel prefill: every layer's experts split over the ranks (see the module docstring)."""
+    import datetime
+    import importlib
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    for k, v in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29511"), ("RANK", "0"), ("WORLD_SIZE", "1")):
+        os.environ.setdefault(k, v)  # a single-GPU run without torchrun
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    pkg = load_pkg()
+    ep = importlib.import_module(pkg.__name__ + ".ep")
+    cfg = pkg.configs.GPT_OSS_120B
+    if a.experts:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, experts=a.experts)
+    T, H = a.tokens, cfg.hidden
+    if T % world:
+        raise SystemExit("--ep needs tokens divisible by the number of GPUs")
+    layers = [pkg.MoeLayer(cfg.desc(max_tokens=T, ep_rank=rank, ep_world=world), synthetic=cfg.synthetic(layer=l),
+                           device=dev.index, reserve_bytes=2 << 30) for l in range(a.layers)]
+    epl = [ep.ExpertParallelLayer(l) for l in layers]
+    pool = 4
+    rng = np.random.default_rng(1000)  # the same tokens on every rank
+    xs = torch.from_numpy(rng.standard_normal((pool, T, H)).astype(np.float32))
+    xs_dev = xs.to(dev)
+    full = torch.empty((T, H), dtype=torch.float32, device=dev)
+    yjobs = torch.zeros((T, cfg.top_k, H), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(x):
+        h = x
+        for layer in epl:
+            xn = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5)
+            mine, _ = layer.forward(xn, y=yjobs)
+            dist.all_gather_into_tensor(full, mine)
+            h = h + full
+        return h
+
+    for i in range(a.warmup):
+        step(xs_dev[i % pool])
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = pkg.kernel_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index) as clk:
+        ev0.record(stream)
+        for i in range(a.steps):
+            step(xs_dev[i % pool])
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = pkg.kernel_launches() - launches0
+    dist.barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_step = ms / a.steps
+    # end to end: the tokens come from pinned host memory each step, the rank's rows go back
+    xh = xs.pin_memory()
+    oh = torch.empty((T // world, H), dtype=torch.float32).pin_memory()
+    t0 = rank * (T // world)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(a.steps):
+        h = step(xh[i % pool].to(dev, non_blocking=True))
+        oh.copy_(h[t0:t0 + T // world], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    ems = float(te.item())
+    flops = a.layers * 2.0 * T * cfg.top_k * 3 * cfg.intermediate * H  # gate_up (2I x H) + down (H x I) per job
+    tpeak, tkind = peaks("bf16_tflops_sustained")
+    achieved = flops / world / (ms_step / 1e3) / 1e12
+    res = {"metric": metric_name(a) + f", expert-parallel over {world} GPU(s)", "value": T * a.steps / (ms / 1e3),
+           "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "f16 tensor-core MMA (exact f16 MXFP4 weights x hi+lo f16 Q8_0 activations), fp32 accumulate",
+           "data": "synthetic",
+           "config": {"workload": f"gpt-oss-120b-stack {a.mode}, expert parallel", "layers": a.layers,
+                      "experts": cfg.experts, "experts_per_gpu": cfg.experts // world, "top_k": cfg.top_k,
+                      "hidden": H, "ffn": cfg.intermediate, "quant": "mxfp4", "global_batch": T,
+                      "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single of job rows + all_gather",
+                      "l2": "inputs larger than L2"},
+           "roofline": {"kernel": "whole step, expert FLOPs per GPU (useful, not the hi+lo MMAs issued)",
+                        "bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
+                        "frac": achieved / tpeak, "peak_source": f"{tkind} bf16_tflops_sustained", "traffic": None},
+           "gpu_launches": launches, "clocks": clk.summary(),
+           "e2e": {"value": T * a.steps / (ems / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(T * H * 4),
+                   "d2h_bytes_per_step": int(T // world * H * 4), "ms_per_step": ems / a.steps,
+                   "api": "MoeLayer.forward_jobs (umsx_moe_forward_jobs) + ep.exchange + umsx_combine"}}
+    for l in layers:
+        l.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res))
+
+
 def traffic_for(a, kernel: str):
     """Per-launch DRAM bytes of the kernel, from the committed ncu capture (profiles/traffic.json):
     bytes per layer measured on a small stack, times this run's layer count."""
@@ -387,6 +500,8 @@ def main():
     a = parse()
     if a.impl == "reference":
         reference_arm(a)
+    elif a.ep:
+        ep_arm(a)
     else:
         gpu_arm(a)
 

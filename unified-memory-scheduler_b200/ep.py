@@ -81,11 +81,12 @@ class ExpertParallelLayer:
         if d.ep_world != dist.get_world_size(group) or d.ep_rank != dist.get_rank(group):
             raise ValueError("the layer's ep_rank / ep_world must match the process group")
 
-    def forward(self, x: torch.Tensor, stream=None):
-        """x [T, H] on this rank's GPU, the same rows on every rank.  Returns (out [t1 - t0, H] f32
-        for this rank's tokens, (t0, t1))."""
+    def forward(self, x: torch.Tensor, y: torch.Tensor | None = None, stream=None):
+        """x [T, H] on this rank's GPU, the same rows on every rank; y: optional [T, k, H] f32
+        scratch for the job outputs (reused across calls: only this rank's rows are read).
+        Returns (out [t1 - t0, H] f32 for this rank's tokens, (t0, t1))."""
         from .umsx import combine
-        y, ids, w = self.layer.forward_jobs(x, stream=stream)
+        y, ids, w = self.layer.forward_jobs(x, y=y, stream=stream)
         mine, (t0, t1) = exchange(y, ids, self.layer.desc.experts, self.group)
         if t1 == t0:  # fewer tokens than ranks: nothing to combine here
             return torch.empty((0, self.layer.desc.hidden), dtype=torch.float32, device=x.device), (t0, t1)
