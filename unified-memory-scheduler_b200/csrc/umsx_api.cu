@@ -590,7 +590,9 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
         rp.e_local = m->e_local;
         rp.rmsnorm = rmsnorm;
         rp.eps = eps;
-        UMSX_LAUNCHED(launch_router_tiled(rp, ws.disp, s));
+        const int n = launch_router_tiled(rp, ws.disp, s);
+        if (n < 0) return fail(UMSX_EDEVICE, "prefill router: shared-memory attribute refused");
+        UMSX_LAUNCHED(n);
     }
     UMSX_LAUNCHED(launch_prefill_pack(ws.disp, jobs, m->e_local == d.experts ? nullptr : ws.disp.offsets + m->e_local, K, H,
                                       ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));

@@ -345,7 +345,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
 // normalised token rows are read from shared memory and reused: a CTA owns 16 tokens x
 // 16 experts, warp w the 4 x 4 block (w / 4, w % 4), lane l chain l of all 16 pairs.
 
-constexpr int kLgTile = 16, kLgKc = 256;
+constexpr int kLgT = 32, kLgE = 32, kLgKc = 128;  // router logits: CTA tile tokens x experts, K chunk
+constexpr size_t kLgSmem = (size_t)2 * (kLgT + kLgE) * kLgKc * 4;
 
 __device__ __forceinline__ float load_x(const void *x, int x_dtype, size_t i) {
     return x_dtype == UMSX_DTYPE_BF16 ? bf16_bits_to_f32(static_cast<const uint16_t *>(x)[i])
@@ -365,48 +366,100 @@ __device__ __forceinline__ float row_inv_rms(const void *x, int x_dtype, int t, 
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
 }
 
-__global__ void __launch_bounds__(512) k_logits_tiled(const void *x, int x_dtype, int tokens, int H, int E,
-                                                      const float *w, const float *b, int rmsnorm, float eps,
-                                                      float *logits) {
-    __shared__ float xs[kLgTile][kLgKc];
-    __shared__ float wsm[kLgTile][kLgKc];
-    __shared__ float inv_s[kLgTile];
+// Router logits for a tile of kLgT tokens x kLgE experts per CTA: every logit is the decode
+// router's exact sum (lane i accumulates the elements i, i + 32, ... of w[e] * (x[t] * inv[t])
+// in order, then the xor tree, then the bias), each warp holding an 8 x 8 block of (token,
+// expert) chains in registers.  K is staged through shared memory in chunks of kLgKc values,
+// the next chunk's global loads in flight while the current one is consumed.
+__global__ void __launch_bounds__(512, 1) k_logits_tiled(const void *x, int x_dtype, int tokens, int H, int E,
+                                                         const float *w, const float *b, int rmsnorm, float eps,
+                                                         float *logits) {
+    extern __shared__ __align__(16) float lg_smem[];
+    float *xs = lg_smem;                      // [2][kLgT][kLgKc]
+    float *wsm = lg_smem + 2 * kLgT * kLgKc;  // [2][kLgE][kLgKc]
+    __shared__ float inv_s[kLgT];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t0 = blockIdx.y * kLgTile, e0 = blockIdx.x * kLgTile;
-    if (t0 + warp < tokens) {
-        const float inv = row_inv_rms(x, x_dtype, t0 + warp, H, rmsnorm, eps, lane);
-        if (lane == 0) inv_s[warp] = inv;
+    const int t0 = blockIdx.y * kLgT, e0 = blockIdx.x * kLgE;
+    for (int r = warp; r < kLgT; r += 16) {
+        const float inv = t0 + r < tokens ? row_inv_rms(x, x_dtype, t0 + r, H, rmsnorm, eps, lane) : 0.0f;
+        if (lane == 0) inv_s[r] = inv;
     }
-    __syncthreads();
-    const int ti = (warp >> 2) * 4, ei = (warp & 3) * 4;
-    float acc[4][4] = {};
-    for (int kc = 0; kc < H; kc += kLgKc) {
-        for (int i = threadIdx.x; i < kLgTile * kLgKc; i += blockDim.x) {
-            const int r = i / kLgKc, k = i - r * kLgKc;
-            const bool kin = kc + k < H;
-            xs[r][k] = (kin && t0 + r < tokens) ? __fmul_rn(load_x(x, x_dtype, (size_t)(t0 + r) * H + kc + k), inv_s[r]) : 0.0f;
-            wsm[r][k] = (kin && e0 + r < E) ? __ldg(w + (size_t)(e0 + r) * H + kc + k) : 0.0f;
+    // staging: thread -> (row, 8 consecutive values) of x, and two (row, 4 values) pieces of w
+    const int xr = threadIdx.x >> 4, xk = (threadIdx.x & 15) * 8;
+    const int wr0 = threadIdx.x >> 5, wk = (threadIdx.x & 31) * 4;
+    float xv_n[8], wv_n[2][4];
+    auto load = [&](int kc) {
+        const int k = kc + xk;
+        const bool tin = t0 + xr < tokens && k < H;
+        if (x_dtype == UMSX_DTYPE_BF16) {
+            uint4 u = tin ? __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + (size_t)(t0 + xr) * H + k))
+                          : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                xv_n[2 * i] = bf16_bits_to_f32(q[i] & 0xffffu);
+                xv_n[2 * i + 1] = bf16_bits_to_f32(q[i] >> 16);
+            }
+        } else {
+            const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(x) + (size_t)(t0 + xr) * H + k);
+            const float4 a = tin ? __ldg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 c = tin ? __ldg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+            xv_n[0] = a.x; xv_n[1] = a.y; xv_n[2] = a.z; xv_n[3] = a.w;
+            xv_n[4] = c.x; xv_n[5] = c.y; xv_n[6] = c.z; xv_n[7] = c.w;
         }
-        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = wr0 + 16 * h, kw = kc + wk;
+            const float4 v = (e0 + r < E && kw < H) ? __ldg(reinterpret_cast<const float4 *>(w + (size_t)(e0 + r) * H + kw))
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            wv_n[h][0] = v.x; wv_n[h][1] = v.y; wv_n[h][2] = v.z; wv_n[h][3] = v.w;
+        }
+    };
+    auto store = [&](int buf) {
+        const float inv = inv_s[xr];
+        float4 *xd = reinterpret_cast<float4 *>(xs + ((size_t)buf * kLgT + xr) * kLgKc + xk);
+        xd[0] = make_float4(__fmul_rn(xv_n[0], inv), __fmul_rn(xv_n[1], inv), __fmul_rn(xv_n[2], inv), __fmul_rn(xv_n[3], inv));
+        xd[1] = make_float4(__fmul_rn(xv_n[4], inv), __fmul_rn(xv_n[5], inv), __fmul_rn(xv_n[6], inv), __fmul_rn(xv_n[7], inv));
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            *reinterpret_cast<float4 *>(wsm + ((size_t)buf * kLgE + wr0 + 16 * h) * kLgKc + wk) =
+                make_float4(wv_n[h][0], wv_n[h][1], wv_n[h][2], wv_n[h][3]);
+    };
+    const int ti = (warp >> 2) * 8, ei = (warp & 3) * 8;
+    float acc[8][8];
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[a][c] = 0.0f;
+    load(0);
+    __syncthreads();  // inv_s
+    store(0);
+    __syncthreads();
+    const int nchunks = (H + kLgKc - 1) / kLgKc;
+    for (int ch = 0; ch < nchunks; ++ch) {
+        const int buf = ch & 1, kc = ch * kLgKc;
+        if (ch + 1 < nchunks) load(kc + kLgKc);
+        const float *xb = xs + (size_t)buf * kLgT * kLgKc, *wb = wsm + (size_t)buf * kLgE * kLgKc;
         const int steps = min(kLgKc, H - kc) / 32;
         for (int i = 0; i < steps; ++i) {
             const int k = 32 * i + lane;
-            float xv[4], wv[4];
+            float xv[8], wv[8];
 #pragma unroll
-            for (int a = 0; a < 4; ++a) xv[a] = xs[ti + a][k];
+            for (int a = 0; a < 8; ++a) xv[a] = xb[(ti + a) * kLgKc + k];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) wv[c] = wsm[ei + c][k];
+            for (int c = 0; c < 8; ++c) wv[c] = wb[(ei + c) * kLgKc + k];
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+            for (int a = 0; a < 8; ++a)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) acc[a][c] = __fmaf_rn(wv[c], xv[a], acc[a][c]);
+                for (int c = 0; c < 8; ++c) acc[a][c] = __fmaf_rn(wv[c], xv[a], acc[a][c]);
         }
+        if (ch + 1 < nchunks) store(buf ^ 1);
         __syncthreads();
     }
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < 8; ++a)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 8; ++c) {
             const int t = t0 + ti + a, e = e0 + ei + c;
             float l = warp_tree_sum(acc[a][c]);
             if (t < tokens && e < E) {
@@ -445,17 +498,34 @@ __global__ void k_select_quant(const void *x, int x_dtype, int tokens, int H, in
 __global__ void k_prefill_pack(const uint8_t *xq_codes, const float *xq_scales, const int32_t *job_token,
                                const int32_t *job_rank, int jobs, const int32_t *n_jobs, int K, int hidden,
                                __half *a_hi, __half *a_lo, int32_t *inv) {
-    const int nb = hidden / 32;
+    const int nb = hidden / 32, hg = hidden / 8;
     if (n_jobs) jobs = min(jobs, __ldg(n_jobs));  // the jobs of the resident experts (expert parallelism)
-    const size_t total = (size_t)jobs * hidden;
+    const size_t total = (size_t)jobs * hg;
+    // one thread per 8 consecutive values: two code words of the block (lane-pair order), 16-byte stores
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int pos = (int)(i / hidden), k = (int)(i - (size_t)pos * hidden);
-        const int t = __ldg(job_token + pos), b = k >> 5, el = k & 31;
-        const int8_t q = (int8_t)__ldg(xq_codes + ((size_t)t * nb + b) * 32 + lane_pair_offset(el));
-        const float qd = __fmul_rn((float)q, __ldg(xq_scales + (size_t)t * nb + b));  // exact (18 bits)
-        const __half hi = __float2half_rn(qd);
-        a_hi[i] = hi;
-        a_lo[i] = __float2half_rn(__fsub_rn(qd, __half2float(hi)));
+        const int pos = (int)(i / hg), k = (int)(i - (size_t)pos * hg) * 8;
+        const int t = __ldg(job_token + pos), b = k >> 5, g = (k & 31) >> 3;
+        const uint32_t *cw = reinterpret_cast<const uint32_t *>(xq_codes + ((size_t)t * nb + b) * 32);
+        const uint32_t w0 = __ldg(cw + (g & 1) * 4 + (g >> 1)), w1 = __ldg(cw + (g & 1) * 4 + (g >> 1) + 2);
+        const float sc = __ldg(xq_scales + (size_t)t * nb + b);
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            const uint32_t wd = j < 4 ? w0 : w1;
+            __half h2[2], l2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int8_t q = (int8_t)(wd >> (8 * ((j + u) & 3)));
+                const float qd = __fmul_rn((float)q, sc);  // exact (18 bits)
+                h2[u] = __float2half_rn(qd);
+                l2[u] = __float2half_rn(__fsub_rn(qd, __half2float(h2[u])));
+            }
+            hi[j / 2] = (uint32_t)__half_as_ushort(h2[0]) | ((uint32_t)__half_as_ushort(h2[1]) << 16);
+            lo[j / 2] = (uint32_t)__half_as_ushort(l2[0]) | ((uint32_t)__half_as_ushort(l2[1]) << 16);
+        }
+        const size_t o = (size_t)pos * hidden + k;
+        *reinterpret_cast<uint4 *>(a_hi + o) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4 *>(a_lo + o) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         if (k == 0) inv[(size_t)t * K + __ldg(job_rank + pos)] = pos;
     }
 }
@@ -523,8 +593,10 @@ EncodeTiled encoder() {
 }  // namespace
 
 int launch_router_tiled(const RouterParams &p, const Dispatch &d, cudaStream_t s) {
-    dim3 grid((p.experts + kLgTile - 1) / kLgTile, (p.tokens + kLgTile - 1) / kLgTile);
-    k_logits_tiled<<<grid, 512, 0, s>>>(p.x, p.x_dtype, p.tokens, p.hidden, p.experts, p.w, p.b, p.rmsnorm, p.eps,
+    if (cudaFuncSetAttribute(k_logits_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLgSmem) != cudaSuccess)
+        return -1;  // 64 KB of dynamic shared memory
+    dim3 grid((p.experts + kLgE - 1) / kLgE, (p.tokens + kLgT - 1) / kLgT);
+    k_logits_tiled<<<grid, 512, kLgSmem, s>>>(p.x, p.x_dtype, p.tokens, p.hidden, p.experts, p.w, p.b, p.rmsnorm, p.eps,
                                         d.logits);
     k_select_quant<<<(p.tokens + 7) / 8, 256, 0, s>>>(p.x, p.x_dtype, p.tokens, p.hidden, p.experts, p.top_k,
                                                       p.routing, p.routed_scale, p.rmsnorm, p.eps, d);
