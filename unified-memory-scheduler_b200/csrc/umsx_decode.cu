@@ -41,6 +41,7 @@ constexpr int kDecWarps = kDecThreads / 32;
 constexpr long long kGridWaitCycles = 40000000;  // ~20 ms at 2 GHz
 constexpr int kMaxEntries = kDecodeMaxTokens * kDecodeMaxTopK;
 constexpr int kDecodeMaxExperts = 256;
+constexpr int kLogitBar = 11;  // named barrier of the logit warps (1..10 are the unit groups')
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
     unsigned v;
@@ -52,13 +53,16 @@ __device__ __forceinline__ void group_bar(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// All CTAs arrive; returns false (uniformly within the CTA) if the wait ran out
-// or another CTA reported an error.
-__device__ bool grid_sync(unsigned *bar, unsigned target, uint32_t *err, int *ok_s) {
-    __syncthreads();
+// The arrival half of a grid barrier, by thread 0 after a CTA-level barrier that orders the
+// writes other CTAs need: release, so those writes become visible with the arrival.
+__device__ __forceinline__ void grid_arrive(unsigned *bar) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+}
+
+// The waiting half: returns false (uniformly within the CTA) if the wait ran out or another
+// CTA reported an error.
+__device__ bool grid_wait(unsigned *bar, unsigned target, uint32_t *err, int *ok_s) {
     if (threadIdx.x == 0) {
-        // release: this CTA's writes (ordered before by the barrier above) become visible with the arrival
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
         int ok = 1;
         const long long t0 = clock64();
         for (unsigned it = 0; ld_acquire_gpu(bar) < target; ++it) {
@@ -71,6 +75,13 @@ __device__ bool grid_sync(unsigned *bar, unsigned target, uint32_t *err, int *ok
     }
     __syncthreads();
     return *ok_s != 0;
+}
+
+// All CTAs arrive, then wait.
+__device__ bool grid_sync(unsigned *bar, unsigned target, uint32_t *err, int *ok_s) {
+    __syncthreads();
+    if (threadIdx.x == 0) grid_arrive(bar);
+    return grid_wait(bar, target, err, ok_s);
 }
 
 struct DecSmem {
@@ -238,7 +249,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                 if (Ld.router_b) lg = __fadd_rn(lg, wbias[j][e & 3]);
                 if (lane == 0) __stcg(p.logits + (size_t)t * E + e, lg);
             }
+            // this CTA's logits are out: it arrives at the grid barrier now and quantizes x (a
+            // CTA-local job) while the other CTAs finish
+            group_bar(kLogitBar, n_lw * 32);
+            if (tid == 0) grid_arrive(p.bar);
         } else {
+            if (n_lw == 0 && tid == 0) grid_arrive(p.bar);  // no logits here
             // Q8_0 records of the normalised rows (the gate_up activations), every CTA its own copy,
             // made by the warps that have no logit to compute
             for (int it = warp - n_lw; it < T * nb; it += kDecWarps - n_lw) {
@@ -255,7 +271,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             return;
         }
         target += nC;
-        if (!grid_sync(p.bar, target, p.err, &ok_s)) return;
+        if (!grid_wait(p.bar, target, p.err, &ok_s)) return;
 
         // ---- S: selection and slots (every CTA) -----------------------------------
         if (warp < T) {
@@ -363,8 +379,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                 }
             }
         }
+        // arrive, then start each warp's first down weights streaming while the others finish
+        __syncthreads();
+        if (tid == 0) grid_arrive(p.bar);
         target += nC;
-        if (!grid_sync(p.bar, target, p.err, &ok_s)) return;
+        const int di0 = warp >> 1, lh0 = warp & 1;
+        const bool primed = v_lo + di0 < v_hi;
+        if (primed) {
+            const int s = (v_lo + di0) / G2, g = v_lo + di0 - s * G2, e = slot_e[s];
+            MxRing ws;
+            ws.init(Ld.dn_codes + code_offset(UMSX_QUANT_MXFP4, e, G2, g, nbI),
+                    Ld.dn_scales + scale_offset(UMSX_QUANT_MXFP4, e, G2, g, nbI), nbI, lh0, my_ring);
+            mx_ring_prime<S>(ws, lane);
+        }
+        if (!grid_wait(p.bar, target, p.err, &ok_s)) {
+            cp_async_wait<0>();  // the primed copies land before the CTA leaves
+            return;
+        }
 
         // ---- D: down units -----------------------------------------------------------
         if (tid == 0 && my_e > 0 && l + 1 < p.n_layers)
@@ -406,7 +437,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
 #pragma unroll
                     for (int t = 0; t < MT; ++t) trow[t] = t < m ? jf + c0 + t - jb : 0;
                     float acc[MT][4];
-                    mx_warp_dot_ring<MT, S>(ws, lh, as, nbI, m, lane, acc, trow);
+                    mx_warp_dot_ring<MT, S>(ws, lh, as, nbI, m, lane, acc, trow, primed && v == v_lo + di && c0 == 0);
                     mx_chain_combine<MT>(acc);
                     if (lh == 1 && lane < 16)
 #pragma unroll

@@ -259,9 +259,10 @@ struct MxRing {
 };
 
 // mx_warp_dot over a cp.async ring of S stages.
+// primed: the caller has already issued the ring's first S - 1 stages (mx_ring_prime).
 template <int MT, int S>
 __device__ __forceinline__ void mx_warp_dot_ring(const MxRing &ws, int lh, const Staged &a, int nb, int m, int lane,
-                                                 float (&acc)[MT][4], const int (&trow)[MT]) {
+                                                 float (&acc)[MT][4], const int (&trow)[MT], bool primed = false) {
 #pragma unroll
     for (int t = 0; t < MT; ++t)
 #pragma unroll
@@ -270,8 +271,9 @@ __device__ __forceinline__ void mx_warp_dot_ring(const MxRing &ws, int lh, const
     const uint4 *aq = a.q + half * 4 + lh * 2;
     const float *sc = a.sc + half;
     const int nst = (ws.steps + 3) / 4;
+    if (!primed)
 #pragma unroll
-    for (int j = 0; j < S - 1; ++j) ws.issue<S>(j, lane);
+        for (int j = 0; j < S - 1; ++j) ws.issue<S>(j, lane);
     for (int j = 0; j < nst; ++j) {
         cp_async_wait<S - 2>();
         __syncwarp();
@@ -289,6 +291,13 @@ __device__ __forceinline__ void mx_warp_dot_ring(const MxRing &ws, int lh, const
     }
     cp_async_wait<0>();
     __syncwarp();  // the ring is free for the next row group
+}
+
+// Issues the first S - 1 stages of a ring ahead of its mx_warp_dot_ring(..., primed = true).
+template <int S>
+__device__ __forceinline__ void mx_ring_prime(const MxRing &ws, int lane) {
+#pragma unroll
+    for (int j = 0; j < S - 1; ++j) ws.issue<S>(j, lane);
 }
 
 // Staged rows 0..m-1 in order.
