@@ -83,3 +83,12 @@ DEEPSEEK_V2_LITE = LayerConfig("deepseek-v2-lite-layer", 2048, 1408, 64, 6, QUAN
                                False, False, False, seed=4, layers=27, tokens=(1, 2048))
 
 CONFIGS = {c.name: c for c in (GPT_OSS_20B, QWEN3_30B, GPT_OSS_120B, QWEN3_SKEW_Q8, QWEN3_SKEW_MXFP4, DEEPSEEK_V2_LITE)}
+
+# configs[4], the rest of the block: the two always-on shared experts (one FFN of width 2 x 1408,
+# as the GGUF stores them) and the dense FFN of layer 0, each a one-expert top-1 layer (softmax
+# over one logit is exactly 1.0, so its output is the FFN's)
+DEEPSEEK_V2_LITE_SHARED = LayerConfig("deepseek-v2-lite-shared", 2048, 2 * 1408, 1, 1, QUANT_Q8_0, ROUTE_SOFTMAX_TOPK,
+                                      ACT_SILU, False, False, False, seed=4, layers=27, tokens=(1, 2048))
+DEEPSEEK_V2_LITE_DENSE = LayerConfig("deepseek-v2-lite-dense", 2048, 10944, 1, 1, QUANT_Q8_0, ROUTE_SOFTMAX_TOPK,
+                                     ACT_SILU, False, False, False, seed=4, layers=1, tokens=(1, 2048))
+CONFIGS.update({c.name: c for c in (DEEPSEEK_V2_LITE_SHARED, DEEPSEEK_V2_LITE_DENSE)})
