@@ -77,3 +77,27 @@ def test_prefill_stack_within_tolerance(oracle):
     stack.close()
     for l in layers:
         l.close()
+
+
+@pytest.mark.parametrize("tokens", [65, 300])
+def test_prefill_q8_0_separate_gate_up_within_tolerance(oracle, tokens):
+    """configs[1] shapes (Qwen3-30B-A3B: Q8_0, separate gate/up, SiLU, softmax -> top-8 ->
+    renormalise): the tensor-core path with Q8_0 weights decoded to f16 (q * d rounded once).
+    Routing stays bit-exact; the layer output is held to the north-star tolerance."""
+    from tests.helpers import C
+    cfg = C.QWEN3_30B
+    w = host_weights(oracle, cfg)
+    xb = x_bits(oracle, cfg, tokens)
+    want = oracle.moe_layer(oracle_desc(cfg), w, bf16_bits_to_f32(xb), threads=16)
+    layer = U.MoeLayer(cfg.desc(tokens), synthetic=cfg.synthetic())
+    ids = torch.empty((tokens, cfg.top_k), dtype=torch.int32, device="cuda")
+    wt = torch.empty((tokens, cfg.top_k), dtype=torch.float32, device="cuda")
+    launches = U.kernel_launches()
+    out = layer.forward(to_cuda_bf16(xb), ids=ids, weights=wt).cpu().numpy()
+    assert U.kernel_launches() - launches <= 8, "expected the tensor-core prefill path"
+    np.testing.assert_array_equal(ids.cpu().numpy(), want["ids"])
+    np.testing.assert_array_equal(bits(wt.cpu().numpy()), bits(want["weights"]))
+    rel, mab = _close(out, want["out"])
+    scale = float(np.abs(want["out"]).max())
+    assert rel <= REL_L2 and mab <= MAX_ABS * max(1.0, scale), (rel, mab, scale)
+    layer.close()

@@ -205,7 +205,7 @@ void carve_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_
     w.x_dev = a.take<float>(T * H);
     w.out_dev = a.take<float>(T * H);
     w.bar = a.take<unsigned>(1);
-    if (mx && max_tokens >= kPrefillMinTokens) {  // tensor-core prefill operands
+    if (max_tokens >= kPrefillMinTokens && (d.quant == UMSX_QUANT_Q8_0 || d.fused_gate_up)) {  // tensor-core prefill operands
         w.a16 = a.take<uint16_t>(2 * T * K * H);
         w.act16 = a.take<uint16_t>(2 * T * K * I);
         w.inv = a.take<int32_t>(T * K);
@@ -560,10 +560,11 @@ umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, f
 
 // router -> gate_up (+act, +Q8_0) -> down -> combine (+ optional residual).
 // ev: null or 5 events bracketing the four stages.
-// Many tokens, MXFP4 fused gate_up: router + dispatch, then the tensor-core grouped GEMMs.
+// Many tokens, MXFP4 with fused gate_up or Q8_0 (fused or separate gate/up): router + dispatch,
+// then the tensor-core grouped GEMMs.
 bool prefill_eligible(const umsx_moe *m, const Workspace &ws, int tokens) {
-    return m->d.quant == UMSX_QUANT_MXFP4 && m->d.fused_gate_up && tokens >= kPrefillMinTokens && ws.a16 &&
-           m->e_local <= 1024;
+    return (m->d.quant == UMSX_QUANT_Q8_0 || (m->d.quant == UMSX_QUANT_MXFP4 && m->d.fused_gate_up)) &&
+           tokens >= kPrefillMinTokens && ws.a16 && m->e_local <= 256;
 }
 
 // y_jobs (expert parallelism): instead of combining, write each resident job's output to
@@ -598,9 +599,19 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
                                       ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));
     if (ev) if (umsx_status st = mark(ev[1], s)) return st;
     MoeGemmParams g{};
-    g.codes = m->gate_up.codes;
-    g.scales = m->gate_up.scales;
-    g.emax = m->gate_up.emax;
+    g.quant = d.quant;
+    if (d.fused_gate_up) {
+        g.codes = m->gate_up.codes;
+        g.scales = m->gate_up.scales;
+        g.emax = m->gate_up.emax;
+        g.plane_rows = 2 * I;
+    } else {  // Q8_0 only (prefill_eligible)
+        g.codes = m->gate.codes;
+        g.scales = m->gate.scales;
+        g.codes2 = m->up.codes;
+        g.scales2 = m->up.scales;
+        g.plane_rows = I;
+    }
     g.rows = 2 * I;
     g.cols = H;
     g.fused = 1;
@@ -621,9 +632,11 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
     UMSX_LAUNCHED(n);
     if (ev) if (umsx_status st = mark(ev[2], s)) return st;
     MoeGemmParams dn{};
+    dn.quant = d.quant;
     dn.codes = m->down.codes;
     dn.scales = m->down.scales;
-    dn.emax = m->down.emax;
+    dn.emax = d.quant == UMSX_QUANT_MXFP4 ? m->down.emax : nullptr;
+    dn.plane_rows = H;
     dn.rows = H;
     dn.cols = I;
     dn.fused = 0;

@@ -178,7 +178,10 @@ int launch_decode_tc(const DecodeParams &p, cudaStream_t s);
 constexpr int kPrefillMinTokens = 65;  // from this many tokens an MXFP4 layer takes the tensor-core path
 
 struct MoeGemmParams {
-    const uint8_t *codes, *scales, *emax;  // the projection's MXFP4 planes and row exponents
+    int quant;            // UMSX_QUANT_MXFP4 or UMSX_QUANT_Q8_0
+    const uint8_t *codes, *scales, *emax;  // the projection's planes (and, MXFP4, row exponents; null for Q8_0)
+    const uint8_t *codes2, *scales2;       // separate gate/up (Q8_0): the up planes, else null
+    int plane_rows;       // rows per expert of the plane(s) `codes` points to
     int rows, cols;       // per expert: output rows N, reduction K
     int fused, inter;     // fused gate_up: tile rows 0-63 gate rows, 64-127 the matching up rows (offset inter)
     const float *bias;    // [E][rows] or null

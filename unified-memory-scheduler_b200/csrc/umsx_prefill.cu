@@ -48,6 +48,15 @@ struct RawRow {
     uint2 w[4];
     uint32_t e[2];
 };
+// Raw Q8_0 bytes of one tile row for one K stage: the two 32-byte code blocks (lane-pair order)
+// and their two fp16 scales; the same shared-memory ring holds kRawQ8 stages of these.
+struct RawRowQ8 {
+    uint4 c[4];
+    uint32_t s;
+    uint32_t pad[3];
+};
+constexpr int kRawQ8 = (int)(kRaw * sizeof(RawRow) / sizeof(RawRowQ8));
+static_assert(kRawQ8 >= 3, "Q8_0 raw ring depth");
 constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + kStagesA * kTileBytes /*weights*/ +
                              kStagesB * 2 * kTileBytes /*activations hi, lo*/ + kRaw * kBM * sizeof(RawRow) +
                              2 * 8 * 64 * sizeof(float) /*epilogue exchange*/;
@@ -180,6 +189,94 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                 tc::mma_commit(&d_full[buf]);
             }
         }
+    } else if (warp < 6 && p.quant == UMSX_QUANT_Q8_0) {
+        // ---- weight tiles: Q8_0 -> f16, q * d rounded to f16 (the prefill tolerance) -----------
+        const int r = 32 * (warp & 3) + lane;  // tile row
+        const int nbK = p.cols / 32, nrg = p.plane_rows / 32;
+        RawRowQ8 *sRq = reinterpret_cast<RawRowQ8 *>(sRaw);
+        uint32_t g = 0;
+        for (int it = blockIdx.x; it < total; it += gridDim.x) {
+            int e, mt, nt;
+            decode_item(it, prefix, E, m_tiles, e, mt, nt);
+            int prow, brow;  // row in the plane, row of the layer's output (bias / validity)
+            const uint8_t *cb = p.codes, *sb = p.scales;
+            if (p.fused) {
+                const int j = mt * 64 + (r & 63);
+                if (r < 64) {
+                    prow = brow = j;
+                } else if (p.codes2) {
+                    prow = j;
+                    brow = p.inter + j;
+                    cb = p.codes2;
+                    sb = p.scales2;
+                } else {
+                    prow = brow = p.inter + j;
+                }
+            } else {
+                prow = brow = mt * kBM + r;
+            }
+            const bool valid = brow < p.rows;
+            const int rg = valid ? prow >> 5 : 0, r32 = prow & 31;
+            const uint8_t *codes = cb + ((size_t)e * nrg + rg) * (size_t)nbK * 1024 + r32 * 32;
+            const uint8_t *scl = sb + ((size_t)e * nrg + rg) * (size_t)(nbK / 2) * 128 + r32 * 4;
+            uint8_t *rowA = sA + r * 128;
+            auto fetch = [&](int kk) {
+                if (kk < nk && valid) {
+                    RawRowQ8 *d = sRq + (kk % kRawQ8) * kBM + r;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        cp_async16(&d->c[2 * h], codes + (size_t)(2 * kk + h) * 1024);
+                        cp_async16(&d->c[2 * h + 1], codes + (size_t)(2 * kk + h) * 1024 + 16);
+                    }
+                    tc::cp_async4(&d->s, scl + (size_t)kk * 128);
+                }
+                cp_async_commit();
+            };
+#pragma unroll
+            for (int j = 0; j < kRawQ8 - 1; ++j) fetch(j);
+            for (int kk = 0; kk < nk; ++kk, ++g) {
+                const int s = g % kStagesA;
+                cp_async_wait<kRawQ8 - 2>();
+                fetch(kk + kRawQ8 - 1);
+                uint4 c[4] = {};
+                uint32_t sv = 0;
+                if (valid) {
+                    const RawRowQ8 *sr = sRq + (kk % kRawQ8) * kBM + r;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) c[i] = sr->c[i];
+                    sv = sr->s;
+                }
+                wait_bar(&empty_a[s], ((g / kStagesA) & 1u) ^ 1u, p.err);
+                uint8_t *dst = rowA + s * kTileBytes;
+                const __half2 k1152 = __float2half2_rn(1152.0f);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const __half d = __ushort_as_half((unsigned short)(sv >> (16 * h)));
+                    const __half2 d2 = __halves2half2(d, d);
+                    const uint32_t W[8] = {c[2 * h].x, c[2 * h].y, c[2 * h].z, c[2 * h].w,
+                                           c[2 * h + 1].x, c[2 * h + 1].y, c[2 * h + 1].z, c[2 * h + 1].w};
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        // elements 8cc..8cc+7 of the block: two code words of the lane-pair order
+                        const uint32_t wd[2] = {W[(cc & 1) * 4 + (cc >> 1)] ^ 0x80808080u,
+                                                W[(cc & 1) * 4 + (cc >> 1) + 2] ^ 0x80808080u};
+                        uint32_t o[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            // (q + 128) in the low mantissa of 1024: 1024 + q + 128 - 1152 = q, exactly
+                            const uint32_t bits = __byte_perm(wd[q >> 1], 0x64u, (q & 1) ? 0x4342u : 0x4140u);
+                            const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&bits), k1152), d2);
+                            o[q] = *reinterpret_cast<const uint32_t *>(&v);
+                        }
+                        const int ch = 4 * h + cc;
+                        *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) =
+                            valid ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+                tc::fence_proxy_async();
+                tc::mbar_arrive(&full_a[s]);
+            }
+        }
     } else if (warp < 6) {
         // ---- weight tiles: MXFP4 -> f16 ---------------------------------------------------
         const int r = 32 * (warp & 3) + lane;  // tile row
@@ -270,10 +367,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             if (p.fused) mrow = r < 64 ? mt * 64 + r : p.inter + mt * 64 + (r - 64);
             else mrow = mt * kBM + r;
             const bool valid = mrow < p.rows;
-            const int emax = valid ? __ldg(p.emax + (size_t)e * p.rows + mrow) : 0;
+            const int emax = valid && p.emax ? __ldg(p.emax + (size_t)e * p.rows + mrow) : 0;
             const int seg = __ldg(p.offsets + e), cnt = __ldg(p.offsets + e + 1) - seg;
-            // 2^(emax - 140): the f16 weights carried 2^(e - emax + 13), the block scale is 2^(e - 127)
-            const float rs = valid ? __uint_as_float((uint32_t)(emax > 13 ? emax - 13 : 1) << 23) : 0.0f;
+            // MXFP4: 2^(emax - 140), the f16 weights carried 2^(e - emax + 13) and the block scale is
+            // 2^(e - 127); Q8_0: the f16 weights are q * d already
+            const float rs = !valid ? 0.0f
+                           : p.emax ? __uint_as_float((uint32_t)(emax > 13 ? emax - 13 : 1) << 23) : 1.0f;
             const float bias = (valid && p.bias) ? __ldg(p.bias + (size_t)e * p.rows + mrow) : 0.0f;
             const uint32_t buf = n_item & 1u;
             const uint32_t taddr = tmem + buf * kBN + lane_field;
