@@ -101,3 +101,21 @@ def test_prefill_q8_0_separate_gate_up_within_tolerance(oracle, tokens):
     scale = float(np.abs(want["out"]).max())
     assert rel <= REL_L2 and mab <= MAX_ABS * max(1.0, scale), (rel, mab, scale)
     layer.close()
+
+
+def test_prefill_mxfp4_separate_gate_up_within_tolerance(oracle):
+    """MXFP4 with separate gate and up matrices (the configs[3] MXFP4 skew layer's layout, SiLU):
+    the tile's up rows come from the second matrix and its own row exponents."""
+    cfg = small_config(fused_gate_up=False, activation=U.ACT_SILU, has_bias=False, experts=16, top_k=4, seed=21)
+    tokens = 100
+    w = host_weights(oracle, cfg)
+    xb = x_bits(oracle, cfg, tokens)
+    want = oracle.moe_layer(oracle_desc(cfg), w, bf16_bits_to_f32(xb), threads=8)
+    layer = U.MoeLayer(cfg.desc(tokens), synthetic=cfg.synthetic())
+    ids = torch.empty((tokens, cfg.top_k), dtype=torch.int32, device="cuda")
+    out = layer.forward(to_cuda_bf16(xb), ids=ids).cpu().numpy()
+    np.testing.assert_array_equal(ids.cpu().numpy(), want["ids"])
+    rel, mab = _close(out, want["out"])
+    scale = float(np.abs(want["out"]).max())
+    assert rel <= REL_L2 and mab <= MAX_ABS * max(1.0, scale), (rel, mab, scale)
+    layer.close()

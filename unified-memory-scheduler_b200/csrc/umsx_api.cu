@@ -205,7 +205,7 @@ void carve_workspace(Workspace &w, const umsx_moe_desc &d, int e_local, int max_
     w.x_dev = a.take<float>(T * H);
     w.out_dev = a.take<float>(T * H);
     w.bar = a.take<unsigned>(1);
-    if (max_tokens >= kPrefillMinTokens && (d.quant == UMSX_QUANT_Q8_0 || d.fused_gate_up)) {  // tensor-core prefill operands
+    if (max_tokens >= kPrefillMinTokens) {  // tensor-core prefill operands
         w.a16 = a.take<uint16_t>(2 * T * K * H);
         w.act16 = a.take<uint16_t>(2 * T * K * I);
         w.inv = a.take<int32_t>(T * K);
@@ -560,11 +560,10 @@ umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, f
 
 // router -> gate_up (+act, +Q8_0) -> down -> combine (+ optional residual).
 // ev: null or 5 events bracketing the four stages.
-// Many tokens, MXFP4 with fused gate_up or Q8_0 (fused or separate gate/up): router + dispatch,
-// then the tensor-core grouped GEMMs.
+// Many tokens (MXFP4 or Q8_0, fused or separate gate/up): router + dispatch, then the tensor-core
+// grouped GEMMs.
 bool prefill_eligible(const umsx_moe *m, const Workspace &ws, int tokens) {
-    return (m->d.quant == UMSX_QUANT_Q8_0 || (m->d.quant == UMSX_QUANT_MXFP4 && m->d.fused_gate_up)) &&
-           tokens >= kPrefillMinTokens && ws.a16 && m->e_local <= 256;
+    return tokens >= kPrefillMinTokens && ws.a16 && m->e_local <= 256;
 }
 
 // y_jobs (expert parallelism): instead of combining, write each resident job's output to
@@ -605,11 +604,13 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
         g.scales = m->gate_up.scales;
         g.emax = m->gate_up.emax;
         g.plane_rows = 2 * I;
-    } else {  // Q8_0 only (prefill_eligible)
+    } else {
         g.codes = m->gate.codes;
         g.scales = m->gate.scales;
+        g.emax = m->gate.emax;
         g.codes2 = m->up.codes;
         g.scales2 = m->up.scales;
+        g.emax2 = m->up.emax;
         g.plane_rows = I;
     }
     g.rows = 2 * I;

@@ -180,7 +180,7 @@ constexpr int kPrefillMinTokens = 65;  // from this many tokens an MXFP4 layer t
 struct MoeGemmParams {
     int quant;            // UMSX_QUANT_MXFP4 or UMSX_QUANT_Q8_0
     const uint8_t *codes, *scales, *emax;  // the projection's planes (and, MXFP4, row exponents; null for Q8_0)
-    const uint8_t *codes2, *scales2;       // separate gate/up (Q8_0): the up planes, else null
+    const uint8_t *codes2, *scales2, *emax2;  // separate gate/up: the up planes (and MXFP4 row exponents), else null
     int plane_rows;       // rows per expert of the plane(s) `codes` points to
     int rows, cols;       // per expert: output rows N, reduction K
     int fused, inter;     // fused gate_up: tile rows 0-63 gate rows, 64-127 the matching up rows (offset inter)

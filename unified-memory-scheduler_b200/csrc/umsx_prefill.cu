@@ -280,19 +280,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
     } else if (warp < 6) {
         // ---- weight tiles: MXFP4 -> f16 ---------------------------------------------------
         const int r = 32 * (warp & 3) + lane;  // tile row
-        const int nbK = p.cols / 32, nrg = p.rows / 16, quads = ((nbK / 2) + 3) / 4;
+        const int nbK = p.cols / 32, nrg = p.plane_rows / 16, quads = ((nbK / 2) + 3) / 4;
         uint32_t g = 0;
         for (int it = blockIdx.x; it < total; it += gridDim.x) {
             int e, mt, nt;
             decode_item(it, prefix, E, m_tiles, e, mt, nt);
-            int mrow;
-            if (p.fused) mrow = r < 64 ? mt * 64 + r : p.inter + mt * 64 + (r - 64);
-            else mrow = mt * kBM + r;
+            int mrow, prow;  // row of the layer's output, row in the plane
+            const uint8_t *cb = p.codes, *sb = p.scales, *eb = p.emax;
+            if (p.fused) {
+                mrow = prow = r < 64 ? mt * 64 + r : p.inter + mt * 64 + (r - 64);
+                if (r >= 64 && p.codes2) {  // separate gate/up: the up rows come from the second matrix
+                    prow = mt * 64 + (r - 64);
+                    cb = p.codes2;
+                    sb = p.scales2;
+                    eb = p.emax2;
+                }
+            } else {
+                mrow = prow = mt * kBM + r;
+            }
             const bool valid = mrow < p.rows;
-            const int grp = valid ? mrow >> 4 : 0, rr = mrow & 15;
-            const int emax = valid ? __ldg(p.emax + (size_t)e * p.rows + mrow) : 0;
-            const uint8_t *codes = p.codes + ((size_t)e * nrg + grp) * (size_t)nbK * 256;
-            const uint8_t *scl = p.scales + ((size_t)e * nrg + grp) * (size_t)quads * 128;
+            const int grp = valid ? prow >> 4 : 0, rr = prow & 15;
+            const int emax = valid ? __ldg(eb + (size_t)e * p.plane_rows + prow) : 0;
+            const uint8_t *codes = cb + ((size_t)e * nrg + grp) * (size_t)nbK * 256;
+            const uint8_t *scl = sb + ((size_t)e * nrg + grp) * (size_t)quads * 128;
             uint8_t *rowA = sA + r * 128;
             // this row's raw bytes, kRaw - 1 stages ahead (each thread copies and reads only its own row)
             auto fetch = [&](int kk) {
@@ -367,12 +377,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             if (p.fused) mrow = r < 64 ? mt * 64 + r : p.inter + mt * 64 + (r - 64);
             else mrow = mt * kBM + r;
             const bool valid = mrow < p.rows;
-            const int emax = valid && p.emax ? __ldg(p.emax + (size_t)e * p.rows + mrow) : 0;
+            const bool up2 = p.fused && r >= 64 && p.codes2;  // up row of a separate up matrix
+            const int prow = up2 ? mrow - p.inter : mrow;
+            const uint8_t *eb = up2 ? p.emax2 : p.emax;
+            const int emax = valid && eb ? __ldg(eb + (size_t)e * p.plane_rows + prow) : 0;
             const int seg = __ldg(p.offsets + e), cnt = __ldg(p.offsets + e + 1) - seg;
             // MXFP4: 2^(emax - 140), the f16 weights carried 2^(e - emax + 13) and the block scale is
             // 2^(e - 127); Q8_0: the f16 weights are q * d already
             const float rs = !valid ? 0.0f
-                           : p.emax ? __uint_as_float((uint32_t)(emax > 13 ? emax - 13 : 1) << 23) : 1.0f;
+                           : eb ? __uint_as_float((uint32_t)(emax > 13 ? emax - 13 : 1) << 23) : 1.0f;
             const float bias = (valid && p.bias) ? __ldg(p.bias + (size_t)e * p.rows + mrow) : 0.0f;
             const uint32_t buf = n_item & 1u;
             const uint32_t taddr = tmem + buf * kBN + lane_field;
