@@ -662,6 +662,18 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
 }
 
 // y_jobs: as run_prefill.
+// Jobs per pass of the per-stage expert kernels.  A CTA holds one expert's jobs in
+// registers and staging, MT at a time, and loops over the rest (re-reading its weights,
+// mostly from L2).  With lambda = T * k / E jobs per expert on average, MT covers
+// lambda + sqrt(lambda): large enough that few experts need a second pass, small enough
+// that more CTAs fit on an SM and more weight bytes are in flight.
+static int per_stage_chunk(int tokens, int top_k, int experts) {
+    if (tokens <= 1) return 1;
+    const double lam = (double)tokens * top_k / experts;
+    const int want = std::max(2, (int)std::ceil(lam + std::sqrt(lam)));
+    return std::min(tokens, want);
+}
+
 umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
                       const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
                       float *y_jobs = nullptr) {
@@ -689,7 +701,8 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     g.act_rec = ws.act_rec;
     g.act_sc = ws.act_sc;
     g.act_done = ws.act_done;
-    UMSX_LAUNCHED(launch_gate_up(g, ws.disp, slots, tokens, s));
+    const int chunk = per_stage_chunk(tokens, d.top_k, d.experts);
+    UMSX_LAUNCHED(launch_gate_up(g, ws.disp, slots, chunk, s));
     if (ev) if (umsx_status st = mark(ev[2], s)) return st;
     GemvParams p{};
     p.m = m->down;
@@ -709,7 +722,7 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     }
     if (d.quant == UMSX_QUANT_MXFP4) { p.a_rec = ws.act_rec; p.a_rsc = ws.act_sc; }  // bulk-copied records
     else { p.a_codes = ws.act_codes; p.a_scales = ws.act_scales; }
-    UMSX_LAUNCHED(launch_gemv(p, ws.disp, slots, tokens, s));
+    UMSX_LAUNCHED(launch_gemv(p, ws.disp, slots, chunk, s));
     if (y_jobs) return UMSX_OK;
     if (ev) {  // timed stages keep the combine a kernel of its own so that every stage has a boundary
         if (umsx_status st = mark(ev[3], s)) return st;

@@ -216,6 +216,7 @@ void record_launches(uint64_t kernels);  // adds to umsx_kernel_launches()
 // Launchers (umsx_kernels.cu).  Each returns the number of kernels launched.
 int launch_router(const RouterParams &p, const Dispatch &d, cudaStream_t s);
 int launch_dispatch(const Dispatch &d, int entries, int top_k, int e_lo, int e_local, cudaStream_t s);
+// max_per_expert: jobs a CTA takes per pass (the kernels loop over an expert's other jobs).
 int launch_gate_up(const GateUpParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
 int launch_gemv(const GemvParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
 

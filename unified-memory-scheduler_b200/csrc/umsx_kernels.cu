@@ -838,8 +838,10 @@ __device__ __forceinline__ void stage_mx_f32(const float *f32, int cols, const i
 
 // gate_up for MXFP4: a CTA computes 16 intermediate values (warps: gate lh0, gate
 // lh1, up lh0, up lh1) for every job of one expert and writes the activated fp32
-// values; the down kernel quantizes them.  grid = (I/16, slots).
-template <int MT>
+// values; the down kernel quantizes them.  grid = (I/16, slots).  Each warp streams
+// its weights through an S-stage cp.async ring placed after the staged activations;
+// the ring's first S - 1 stages are in flight while the activations are copied in.
+template <int MT, int S>
 __global__ void __launch_bounds__(128) k_gate_up_mx(GateUpParams p, Dispatch d) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float xch[MT][2][16][4];
@@ -858,25 +860,30 @@ __global__ void __launch_bounds__(128) k_gate_up_mx(GateUpParams p, Dispatch d) 
     const Matrix &mat = p.fused ? p.gate_up : (half ? p.up : p.gate);
     const int nrg = mat.rows / 16;
     const int rg = p.fused ? half * (I / 16) + blockIdx.x : blockIdx.x;
-    MxStream ws;
+    MxRing ws;
     ws.init(mat.codes + code_offset(UMSX_QUANT_MXFP4, e, nrg, rg, nb),
-            mat.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, rg, nb), nb, lane, lh);
-    MxBatch<> first;
-    ws.load<true>(0, first);  // weights stream while the activations are copied in
+            mat.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, rg, nb), nb, lh,
+            smem + bulk_staged_bytes(MT, nb) + (size_t)warp * S * kRingStageBytes);
+    mx_ring_prime<S>(ws, lane);  // weights stream while the activations are copied in
     if (threadIdx.x == 0) mbar_init(&bar, 1);
+    int trow[MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) trow[t] = t;
     uint32_t phase = 0;
     const int r = lane & 15;
     const float bias = p.bias ? __ldg(p.bias + (size_t)e * 2 * I + half * I + blockIdx.x * 16 + r) : 0.0f;
     const Staged st = staged_bulk_view(smem, MT, nb);
     for (int c0 = 0; c0 < cnt; c0 += MT) {
         const int m = min(MT, cnt - c0);
-        if (c0 > 0) ws.load<true>(0, first);
         __syncthreads();
         if (threadIdx.x < m) rows_s[threadIdx.x] = __ldcg(d.job_token + seg + c0 + threadIdx.x);
         __syncthreads();
-        if (!stage_mx_bulk(d.xr, d.xr_sc, rows_s, m, nb, smem, MT, &bar, phase, d.err)) return;
+        if (!stage_mx_bulk(d.xr, d.xr_sc, rows_s, m, nb, smem, MT, &bar, phase, d.err)) {
+            cp_async_wait<0>();  // the ring's copies land before the CTA leaves
+            return;
+        }
         float acc[MT][4];
-        mx_warp_dot<MT, kMxBatch>(ws, first, lh, st, nb, m, lane, acc);
+        mx_warp_dot_ring<MT, S>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
         mx_chain_combine<MT>(acc);
         if (lh == 1 && lane < 16)
 #pragma unroll
@@ -922,8 +929,9 @@ __global__ void __launch_bounds__(128) k_gate_up_mx(GateUpParams p, Dispatch d) 
 }
 
 // Generic MXFP4 GEMV: W row groups (2W warps) of one expert; grid = (N/(16W), slots).
-// Sources as k_gemv: 0 internal Q8, 1 ggml block_q8_0, 2 fp32 (quantized here).
-template <int W, int MT, int SRC, int COMBINE>
+// Sources as k_gemv: 0 internal Q8, 1 ggml block_q8_0, 2 fp32 (quantized here), 3 bulk-copied
+// records.  Weights stream through one S-stage cp.async ring per warp, after the staging area.
+template <int W, int MT, int SRC, int COMBINE, int S>
 __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, Dispatch d) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float xch[MT][W][16][4];
@@ -944,11 +952,14 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
     const int rgl = warp >> 1, lh = warp & 1;
     const int rg = blockIdx.x * W + rgl;
     const bool active_rg = rg < nrg;
-    MxStream ws;
+    MxRing ws;
     ws.init(p.m.codes + code_offset(UMSX_QUANT_MXFP4, e, nrg, active_rg ? rg : 0, nb),
-            p.m.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, active_rg ? rg : 0, nb), nb, lane, lh);
-    MxBatch<> first;
-    if (active_rg) ws.load<true>(0, first);
+            p.m.scales + scale_offset(UMSX_QUANT_MXFP4, e, nrg, active_rg ? rg : 0, nb), nb, lh,
+            smem + (SRC == 3 ? bulk_staged_bytes(MT, nb) : staged_bytes(MT, nb)) + (size_t)warp * S * kRingStageBytes);
+    if (active_rg) mx_ring_prime<S>(ws, lane);
+    int trow[MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) trow[t] = t;
     if (p.prefetch_early) {  // the weights were chosen two kernels back; the activations come from the last one
         pdl_wait();
         pdl_launch_dependents();
@@ -959,7 +970,6 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
     const Staged st = SRC == 3 ? staged_bulk_view(smem, MT, nb) : staged_view(smem, MT, nb);
     for (int c0 = 0; c0 < cnt; c0 += MT) {
         const int m = min(MT, cnt - c0);
-        if (c0 > 0 && active_rg) ws.load<true>(0, first);
         __syncthreads();
         if (threadIdx.x < m) {
             const int j = seg + c0 + threadIdx.x;
@@ -971,11 +981,14 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
         if constexpr (SRC == 0) stage_mx_internal(src.q8_codes, src.q8_scales, rows_s, m, nb, smem, MT);
         else if constexpr (SRC == 1) stage_mx_ggml(src.ggml, rows_s, m, nb, smem, MT);
         else if constexpr (SRC == 2) stage_mx_f32(src.f32, p.m.cols, rows_s, m, nb, smem, MT);
-        else if (!stage_mx_bulk(p.a_rec, p.a_rsc, rows_s, m, nb, smem, MT, &bar, phase, d.err)) return;
+        else if (!stage_mx_bulk(p.a_rec, p.a_rsc, rows_s, m, nb, smem, MT, &bar, phase, d.err)) {
+            cp_async_wait<0>();  // the ring's copies land before the CTA leaves
+            return;
+        }
         __syncthreads();
         float acc[MT][4];
         if (active_rg) {
-            mx_warp_dot<MT, kMxBatch>(ws, first, lh, st, nb, m, lane, acc);
+            mx_warp_dot_ring<MT, S>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
             mx_chain_combine<MT>(acc);
             if (lh == 1 && lane < 16)
 #pragma unroll
@@ -1229,11 +1242,15 @@ static void gate_up_mt(const GateUpParams &p, const Dispatch &d, int slots, cuda
     launch_pdl(kern, dim3(p.intermediate / 32, slots), dim3(64 * Geo<QUANT>::kChains), smem, s, p, d);
 }
 
+// cp.async ring depth of the per-stage MXFP4 kernels: S - 1 stages of 4 block pairs
+// (1 KB of codes) in flight per warp.
+constexpr int kPerStageRing = 6;
+
 template <int MT>
 static void gate_up_mx_mt(const GateUpParams &p, const Dispatch &d, int slots, cudaStream_t s) {
     const int nb = p.hidden / 32;
-    const size_t smem = bulk_staged_bytes(MT, nb);
-    auto kern = k_gate_up_mx<MT>;
+    const size_t smem = bulk_staged_bytes(MT, nb) + (size_t)4 * kPerStageRing * kRingStageBytes;
+    auto kern = k_gate_up_mx<MT, kPerStageRing>;
     if (smem + kStaticSmemMargin > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     launch_pdl(kern, dim3(p.intermediate / 16, slots), dim3(128), smem, s, p, d);
 }
@@ -1272,8 +1289,9 @@ template <int MT, int SRC, int COMBINE>
 static void gemv_mx_mt(const GemvParams &p, const GemvSrc &src, const Dispatch &d, int slots, cudaStream_t s) {
     constexpr int W = 2;
     const int nb = p.m.cols / 32;
-    const size_t smem = SRC == 3 ? bulk_staged_bytes(MT, nb) : staged_bytes(MT, nb);
-    auto kern = k_gemv_mx<W, MT, SRC, COMBINE>;
+    const size_t smem = (SRC == 3 ? bulk_staged_bytes(MT, nb) : staged_bytes(MT, nb)) +
+                        (size_t)2 * W * kPerStageRing * kRingStageBytes;
+    auto kern = k_gemv_mx<W, MT, SRC, COMBINE, kPerStageRing>;
     if (smem + kStaticSmemMargin > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int tiles = (p.m.rows / 16 + W - 1) / W;
     launch_pdl(kern, dim3(tiles, slots), dim3(W * 64), smem, s, p, src, d);
