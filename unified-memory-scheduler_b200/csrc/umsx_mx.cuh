@@ -126,35 +126,6 @@ __device__ __forceinline__ size_t scale_offset(int quant, int e, int nrg, int rg
     return ((size_t)e * nrg + rg) * (size_t)chunks * 128;
 }
 
-constexpr int kMxBatch = 8;  // block pairs per load batch (per-stage kernels)
-
-template <int B = kMxBatch>
-struct MxBatch {
-    uint2 w[B];
-    uint32_t e[(B + 3) / 4];
-};
-
-struct MxStream {
-    const uint2 *cp;
-    const uint32_t *ep;
-    int steps;
-    __device__ __forceinline__ void init(const uint8_t *codes, const uint8_t *scales, int nb, int lane, int lh) {
-        cp = reinterpret_cast<const uint2 *>(codes + lh * 256) + lane;
-        ep = reinterpret_cast<const uint32_t *>(scales) + lane;
-        steps = nb / 2;
-    }
-    // Batch of B block pairs starting at s0 (a multiple of B; B a multiple of 4 or 4 / B integral).
-    template <bool GUARD, int B>
-    __device__ __forceinline__ void load(int s0, MxBatch<B> &b) const {
-#pragma unroll
-        for (int i = 0; i < B; ++i)
-            if (!GUARD || s0 + i < steps) b.w[i] = __ldg(cp + (size_t)(s0 + i) * 64);
-#pragma unroll
-        for (int i = 0; i < (B + 3) / 4; ++i)
-            if (!GUARD || s0 + 4 * i < steps) b.e[i] = __ldg(ep + (size_t)((s0 >> 2) + i) * 32);
-    }
-};
-
 template <int MT>
 __device__ __forceinline__ void mx_half(uint2 wq, uint32_t e8, const uint4 *aq, const float *sc, int nb, int scs,
                                         int m, float (&acc)[MT][4], const int (&trow)[MT]) {
@@ -182,38 +153,6 @@ __device__ __forceinline__ void mx_half(uint2 wq, uint32_t e8, const uint4 *aq, 
             }
         }
     }
-}
-
-// acc[t][p] = lane lh*4+p of this thread's chain, over all blocks of the chain, for the
-// activation rows trow[t] (t < m) of the staged set.  Batches of B block pairs, the
-// next one in flight while the current one is consumed.
-template <int MT, int B>
-__device__ __forceinline__ void mx_warp_dot(const MxStream &ws, MxBatch<B> cur, int lh, const Staged &a, int nb, int m,
-                                            int lane, float (&acc)[MT][4], const int (&trow)[MT]) {
-    static_assert(B % 4 == 0, "a batch covers whole exponent words");
-#pragma unroll
-    for (int t = 0; t < MT; ++t)
-#pragma unroll
-        for (int l = 0; l < 4; ++l) acc[t][l] = 0.0f;
-    const int half = lane >> 4;
-    const uint4 *aq = a.q + half * 4 + lh * 2;  // block b = 2*pair + half: record (t*nb + b)*4
-    const float *sc = a.sc + half;
-    int s0 = 0;
-    for (; s0 + B < ws.steps; s0 += B) {  // full batches, next one in flight
-        MxBatch<B> nxt;
-        if (s0 + 2 * B <= ws.steps) ws.load<false>(s0 + B, nxt);
-        else ws.load<true>(s0 + B, nxt);
-#pragma unroll
-        for (int i = 0; i < B; ++i)
-            mx_half<MT>(cur.w[i], (cur.e[i >> 2] >> (8 * (i & 3))) & 0xffu, aq + (size_t)(s0 + i) * 8,
-                        sc + 2 * (s0 + i), nb, a.scs, m, acc, trow);
-        cur = nxt;
-    }
-#pragma unroll
-    for (int i = 0; i < B; ++i)  // last (possibly partial) batch
-        if (s0 + i < ws.steps)
-            mx_half<MT>(cur.w[i], (cur.e[i >> 2] >> (8 * (i & 3))) & 0xffu, aq + (size_t)(s0 + i) * 8,
-                        sc + 2 * (s0 + i), nb, a.scs, m, acc, trow);
 }
 
 // ---- per-warp cp.async ring for the weight stream --------------------------
@@ -298,16 +237,6 @@ template <int S>
 __device__ __forceinline__ void mx_ring_prime(const MxRing &ws, int lane) {
 #pragma unroll
     for (int j = 0; j < S - 1; ++j) ws.issue<S>(j, lane);
-}
-
-// Staged rows 0..m-1 in order.
-template <int MT, int B>
-__device__ __forceinline__ void mx_warp_dot(const MxStream &ws, MxBatch<B> cur, int lh, const Staged &a, int nb, int m,
-                                            int lane, float (&acc)[MT][4]) {
-    int trow[MT];
-#pragma unroll
-    for (int t = 0; t < MT; ++t) trow[t] = t;
-    mx_warp_dot<MT, B>(ws, cur, lh, a, nb, m, lane, acc, trow);
 }
 
 // Staging by bulk copy of precomputed records: job t's records (nb * 64 bytes) and
