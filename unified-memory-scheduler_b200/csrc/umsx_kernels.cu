@@ -1243,8 +1243,12 @@ static void gate_up_mt(const GateUpParams &p, const Dispatch &d, int slots, cuda
 }
 
 // cp.async ring depth of the per-stage MXFP4 kernels: S - 1 stages of 4 block pairs
-// (1 KB of codes) in flight per warp.
-constexpr int kPerStageRing = 6;
+// (1 KB of codes) in flight per warp.  Measured on GPT-OSS-120B-shaped layers at
+// T = 8 / 16 / 64, depths 2, 3, 4, 6, 8 gave 164 / 173 / 167 / 183 / 200 us at T = 8:
+// these short CTAs are bound by their serial phases (slot and job reads, activation
+// copy, epilogue), not by the bytes in flight, and a small ring leaves shared memory
+// to more resident CTAs.
+constexpr int kPerStageRing = 2;
 
 template <int MT>
 static void gate_up_mx_mt(const GateUpParams &p, const Dispatch &d, int slots, cudaStream_t s) {
