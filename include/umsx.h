@@ -200,6 +200,42 @@ umsx_status umsx_route_static(const void *x, int x_dtype, int tokens, const floa
                               int hidden, int experts, int top_k, int routing, float routed_scale, int32_t *ids,
                               float *weights, int32_t *counts, umsx_stream stream);
 
+/* ---- GGUF checkpoints ------------------------------------------------------------------
+ * The selected experts of one layer read from a GGUF file or a set of shards named
+ * <stem>-00001-of-NNNNN.gguf (pass the first).  Replaces load_gguf_experts
+ * (tools/engine/gguf_experts.cpp:45-140; LoadedExperts, gguf_experts.hpp:14-20): tensors
+ * blk.L.ffn_{gate,up,down}_exps.weight (required, separate gate and up) and .bias (optional),
+ * each in one shard; per tensor the byte slice of every selected expert (stride = tensor bytes /
+ * experts) and, with dequantize != 0, its fp32 values; biases always as fp32.  Same limits as
+ * the reference: layer in [0, 4096), 1..16 distinct ids, at most 32 Mi values per tensor
+ * selection, experts per tensor <= 65536; types f32, f16, bf16, q8_0, mxfp4.  Errors:
+ * UMSX_EINVAL with the reason in umsx_last_error().  Index p of each array: 0 gate, 1 up,
+ * 2 down.  Host memory, released by umsx_gguf_experts_free. */
+typedef struct umsx_gguf_experts {
+    int32_t hidden, intermediate, experts, n_ids; /* experts: count in the file's tensors */
+    int32_t quant[3];                             /* ggml type ids */
+    uint64_t stride[3];                           /* bytes per expert */
+    const uint8_t *packed[3];                     /* [n_ids][stride] ggml blocks */
+    const float *values[3];                       /* [n_ids][rows * cols] fp32, or NULL */
+    const float *bias[3];                         /* [n_ids][I, I, H] fp32, or NULL if absent */
+    void *owner;
+} umsx_gguf_experts;
+
+umsx_status umsx_gguf_load_experts(const char *first_shard, int layer, const uint32_t *ids, int n_ids,
+                                   int dequantize, umsx_gguf_experts *out);
+void umsx_gguf_experts_free(umsx_gguf_experts *experts);
+
+/* A resident layer straight from a GGUF checkpoint: the router blk.L.ffn_gate_inp.weight
+ * ([E][H], f32/f16/bf16) and .bias, and every expert of blk.L.ffn_{gate,up,down}_exps (read
+ * as umsx_gguf_load_experts does, without its 16-id limit), repacked as umsx_moe_create does.
+ * desc must match the file: hidden, intermediate, experts, quant (all three projections),
+ * has_bias (gate, up and down biases all present) and has_router_bias; fused_gate_up = 1
+ * concatenates each expert's gate rows and up rows.  Biases keep their fp32 values.  No
+ * counterpart in the reference beyond the loader above (the reference hands LoadedExperts to
+ * Mxfp4NativeCudaDown's constructor, quantized_cuda.hpp:38-50). */
+umsx_status umsx_moe_create_gguf(const umsx_moe_desc *desc, const char *first_shard, int layer, int device,
+                                 size_t reserve_bytes, umsx_moe **out);
+
 /* Number of this library's kernels launched by the calling thread since load (graph replays count
  * every kernel they contain). */
 uint64_t umsx_kernel_launches(void);

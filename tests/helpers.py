@@ -76,3 +76,44 @@ def to_cuda_bf16(xb: np.ndarray):
     """bf16 bit patterns (uint16) -> a bf16 CUDA tensor."""
     import torch
     return torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).cuda()
+
+
+def write_layer_gguf(paths, layer: int, w: LayerWeights, quant: int, hidden: int, inter: int, split_at: int = 99,
+                     bias_dtype=np.float32, extra_kv: bool = True):
+    """Writes one layer's router and expert tensors in llama.cpp's GGUF naming
+    (blk.L.ffn_gate_inp.*, blk.L.ffn_{gate,up,down}_exps.*) with gguf-py.  `paths` lists the
+    shard files; tensors after the first `split_at` go to the second shard.  Fused gate_up
+    weights are written as the separate gate and up tensors a GGUF checkpoint holds."""
+    import gguf
+    qt = gguf.GGMLQuantizationType.MXFP4 if quant == U.QUANT_MXFP4 else gguf.GGMLQuantizationType.Q8_0
+    pre = f"blk.{layer}."
+    gate, up = (w.gate, w.up) if w.gate_up is None else (w.gate_up[:, :inter], w.gate_up[:, inter:])
+    tensors = [(pre + "ffn_gate_inp.weight", np.ascontiguousarray(w.router_w, np.float32), None)]
+    if w.router_b is not None:
+        tensors.append((pre + "ffn_gate_inp.bias", np.ascontiguousarray(w.router_b, np.float32), None))
+    tensors += [(pre + "ffn_gate_exps.weight", np.ascontiguousarray(gate, np.uint8), qt),
+                (pre + "ffn_up_exps.weight", np.ascontiguousarray(up, np.uint8), qt),
+                (pre + "ffn_down_exps.weight", np.ascontiguousarray(w.down, np.uint8), qt)]
+    if w.gate_up_bias is not None:
+        gb = bf16_bits_to_f32(w.gate_up_bias)
+        tensors += [(pre + "ffn_gate_exps.bias", np.ascontiguousarray(gb[:, :inter]).astype(bias_dtype), None),
+                    (pre + "ffn_up_exps.bias", np.ascontiguousarray(gb[:, inter:]).astype(bias_dtype), None),
+                    (pre + "ffn_down_exps.bias", bf16_bits_to_f32(w.down_bias).astype(bias_dtype), None)]
+    groups = [tensors[:split_at], tensors[split_at:]] if len(paths) > 1 else [tensors]
+    for path, group in zip(paths, groups):
+        wr = gguf.GGUFWriter(path, "gpt-oss")
+        if extra_kv:
+            wr.add_string("general.name", "umsx test layer")
+            wr.add_uint32("test.count", 7)
+            wr.add_array("test.list", [1, 2, 3])
+            wr.add_array("test.names", ["a", "bc"])
+            wr.add_float32("test.f", 0.5)
+        for name, arr, raw in group:
+            if raw is None:
+                wr.add_tensor(name, arr)
+            else:
+                wr.add_tensor(name, arr, raw_dtype=raw)
+        wr.write_header_to_file()
+        wr.write_kv_data_to_file()
+        wr.write_tensors_to_file()
+        wr.close()

@@ -6,4 +6,4 @@ The directory name is not a Python identifier, so __graft_entry__.load_package()
 registers it as `umsx_b200`.
 """
 from . import configs, umsx  # noqa: F401
-from .umsx import MoeLayer, MoeStack, UmsxError, combine, kernel_launches, lib  # noqa: F401
+from .umsx import MoeLayer, MoeStack, UmsxError, combine, kernel_launches, lib, load_gguf_experts  # noqa: F401

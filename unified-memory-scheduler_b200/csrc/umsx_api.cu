@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -303,6 +304,9 @@ size_t max_expert_bytes(const umsx_moe *m) {
 
 bool resident(const umsx_moe *m, int e) { return e >= m->e_lo && e < m->e_lo + m->e_local; }
 
+umsx_status create_from_host(const umsx_moe_desc *desc, const umsx_moe_weights *w, const float *gu_bias,
+                             const float *down_bias, int device, size_t reserve_bytes, umsx_moe **out);
+
 }  // namespace
 
 extern "C" {
@@ -319,6 +323,28 @@ umsx_status umsx_moe_create(const umsx_moe_desc *desc, const umsx_moe_weights *w
         return fail(UMSX_EINVAL, "missing router, gate/up or down weights");
     if (desc && desc->has_router_bias && !w->router_b) return fail(UMSX_EINVAL, "has_router_bias set but router_b is null");
     if (desc && desc->has_bias && (!w->gate_up_bias || !w->down_bias)) return fail(UMSX_EINVAL, "has_bias set but biases are null");
+    std::vector<float> gb, db;  // bf16 biases widened (exact)
+    if (desc && desc->has_bias && desc->experts > 0 && desc->intermediate > 0 && desc->hidden > 0) {
+        gb.resize((size_t)desc->experts * 2 * desc->intermediate);
+        db.resize((size_t)desc->experts * desc->hidden);
+        for (size_t i = 0; i < gb.size(); ++i) {
+            const uint32_t bits = (uint32_t)w->gate_up_bias[i] << 16;
+            std::memcpy(&gb[i], &bits, 4);
+        }
+        for (size_t i = 0; i < db.size(); ++i) {
+            const uint32_t bits = (uint32_t)w->down_bias[i] << 16;
+            std::memcpy(&db[i], &bits, 4);
+        }
+    }
+    return create_from_host(desc, w, gb.data(), db.data(), device, reserve_bytes, out);
+}
+
+}  // extern "C"
+
+namespace {
+// Creates a layer from host weights with fp32 biases (gu_bias [E][2I]: gate then up; down_bias [E][H]).
+umsx_status create_from_host(const umsx_moe_desc *desc, const umsx_moe_weights *w, const float *gu_bias,
+                             const float *down_bias, int device, size_t reserve_bytes, umsx_moe **out) {
     umsx_moe *m = nullptr;
     if (umsx_status s = make_handle(desc, device, reserve_bytes, &m)) return s;
     const auto &d = m->d;
@@ -337,17 +363,10 @@ umsx_status umsx_moe_create(const umsx_moe_desc *desc, const umsx_moe_weights *w
         }
         if (umsx_status s = upload_matrix(m->down, w->down, m->e_lo, m->e_local, staging)) return s;
         if (d.has_bias) {
-            std::vector<float> gb((size_t)m->e_local * 2 * I), db((size_t)m->e_local * H);
-            for (size_t i = 0; i < gb.size(); ++i) {
-                const uint32_t bits = (uint32_t)w->gate_up_bias[(size_t)m->e_lo * 2 * I + i] << 16;
-                std::memcpy(&gb[i], &bits, 4);
-            }
-            for (size_t i = 0; i < db.size(); ++i) {
-                const uint32_t bits = (uint32_t)w->down_bias[(size_t)m->e_lo * H + i] << 16;
-                std::memcpy(&db[i], &bits, 4);
-            }
-            UMSX_CUDA(cudaMemcpy(m->gu_bias, gb.data(), gb.size() * 4, cudaMemcpyHostToDevice));
-            UMSX_CUDA(cudaMemcpy(m->down_bias, db.data(), db.size() * 4, cudaMemcpyHostToDevice));
+            UMSX_CUDA(cudaMemcpy(m->gu_bias, gu_bias + (size_t)m->e_lo * 2 * I, (size_t)m->e_local * 2 * I * 4,
+                                 cudaMemcpyHostToDevice));
+            UMSX_CUDA(cudaMemcpy(m->down_bias, down_bias + (size_t)m->e_lo * H, (size_t)m->e_local * H * 4,
+                                 cudaMemcpyHostToDevice));
         }
         if (umsx_status s = compute_row_emax(m)) return s;
         UMSX_CUDA(cudaDeviceSynchronize());
@@ -359,6 +378,9 @@ umsx_status umsx_moe_create(const umsx_moe_desc *desc, const umsx_moe_weights *w
     *out = m;
     return UMSX_OK;
 }
+}  // namespace
+
+extern "C" {
 
 umsx_status umsx_moe_create_synthetic(const umsx_moe_desc *desc, uint64_t seed, uint32_t layer, float router_sigma,
                                       float router_bias_sigma, float bias_sigma, int device, size_t reserve_bytes,
@@ -1126,6 +1148,113 @@ umsx_status umsx_stack_stage_times(umsx_stack *st, float *ms, int n_stages) {
         }
     }
     return UMSX_OK;
+}
+
+// ---- GGUF --------------------------------------------------------------------
+
+namespace {
+struct GgufOwner {
+    umsx::GgufExperts e;
+};
+}  // namespace
+
+umsx_status umsx_gguf_load_experts(const char *first_shard, int layer, const uint32_t *ids, int n_ids, int dequantize,
+                                   umsx_gguf_experts *out) {
+    if (!first_shard || !ids || !out || n_ids <= 0) return fail(UMSX_EINVAL, "invalid layer or selected expert IDs");
+    std::memset(out, 0, sizeof(*out));
+    auto *own = new (std::nothrow) GgufOwner;
+    if (!own) return fail(UMSX_EOOM, "host allocation failed");
+    std::string err;
+    try {
+        err = umsx::gguf_load_experts(first_shard, layer, std::vector<uint32_t>(ids, ids + n_ids), dequantize != 0, true,
+                                      own->e);
+    } catch (const std::bad_alloc &) {
+        err = "host allocation failed";
+    }
+    if (!err.empty()) {
+        delete own;
+        return fail(err == "host allocation failed" ? UMSX_EOOM : UMSX_EINVAL, err);
+    }
+    const umsx::GgufExperts &e = own->e;
+    out->hidden = e.hidden;
+    out->intermediate = e.intermediate;
+    out->experts = e.count;
+    out->n_ids = e.n_ids;
+    for (int p = 0; p < 3; ++p) {
+        out->quant[p] = e.type[p];
+        out->stride[p] = e.stride[p];
+        out->packed[p] = e.packed[p].data();
+        out->values[p] = e.values[p].empty() ? nullptr : e.values[p].data();
+        out->bias[p] = e.has_bias[p] ? e.bias[p].data() : nullptr;
+    }
+    out->owner = own;
+    return UMSX_OK;
+}
+
+void umsx_gguf_experts_free(umsx_gguf_experts *e) {
+    if (!e) return;
+    delete static_cast<GgufOwner *>(e->owner);
+    std::memset(e, 0, sizeof(*e));
+}
+
+umsx_status umsx_moe_create_gguf(const umsx_moe_desc *desc, const char *first_shard, int layer, int device,
+                                 size_t reserve_bytes, umsx_moe **out) {
+    if (!desc || !first_shard || !out) return fail(UMSX_EINVAL, "null argument");
+    if (desc->experts <= 0 || desc->experts > 65536) return fail(UMSX_EINVAL, "experts must be in [1, 65536]");
+    try {
+        std::vector<float> rw, rb;
+        int64_t rshape[2] = {0, 0};
+        bool has_rb = false;
+        std::string err = umsx::gguf_load_router(first_shard, layer, rw, rshape, rb, has_rb);
+        if (!err.empty()) return fail(UMSX_EINVAL, err);
+        if (rshape[0] != desc->hidden || rshape[1] != desc->experts)
+            return fail(UMSX_EINVAL, "GGUF router shape does not match the layer descriptor");
+        if (has_rb != (desc->has_router_bias != 0))
+            return fail(UMSX_EINVAL, "GGUF router bias presence does not match has_router_bias");
+        std::vector<uint32_t> all((size_t)desc->experts);
+        for (int i = 0; i < desc->experts; ++i) all[i] = (uint32_t)i;
+        umsx::GgufExperts e;
+        err = umsx::gguf_load_experts(first_shard, layer, all, false, false, e);
+        if (!err.empty()) return fail(UMSX_EINVAL, err);
+        if (e.hidden != desc->hidden || e.intermediate != desc->intermediate || e.count != desc->experts)
+            return fail(UMSX_EINVAL, "GGUF expert shapes do not match the layer descriptor");
+        for (int p = 0; p < 3; ++p)
+            if (e.type[p] != desc->quant) return fail(UMSX_EINVAL, "GGUF expert quantization does not match desc->quant");
+        const bool all_bias = e.has_bias[0] && e.has_bias[1] && e.has_bias[2];
+        const bool any_bias = e.has_bias[0] || e.has_bias[1] || e.has_bias[2];
+        if (any_bias != all_bias || all_bias != (desc->has_bias != 0))
+            return fail(UMSX_EINVAL, "GGUF expert biases do not match has_bias (gate, up and down all or none)");
+        const size_t E = (size_t)desc->experts, I = (size_t)desc->intermediate, H = (size_t)desc->hidden;
+        umsx_moe_weights w{};
+        w.router_w = rw.data();
+        w.router_b = has_rb ? rb.data() : nullptr;
+        std::vector<uint8_t> fused;
+        if (desc->fused_gate_up) {  // per expert: the I gate rows, then the I up rows
+            const size_t sg = e.stride[0], su = e.stride[1];
+            fused.resize(E * (sg + su));
+            for (size_t x = 0; x < E; ++x) {
+                std::memcpy(fused.data() + x * (sg + su), e.packed[0].data() + x * sg, sg);
+                std::memcpy(fused.data() + x * (sg + su) + sg, e.packed[1].data() + x * su, su);
+            }
+            w.gate_up = fused.data();
+        } else {
+            w.gate = e.packed[0].data();
+            w.up = e.packed[1].data();
+        }
+        w.down = e.packed[2].data();
+        std::vector<float> gb, db;
+        if (all_bias) {
+            gb.resize(E * 2 * I);
+            for (size_t x = 0; x < E; ++x) {
+                std::memcpy(gb.data() + x * 2 * I, e.bias[0].data() + x * I, I * 4);
+                std::memcpy(gb.data() + x * 2 * I + I, e.bias[1].data() + x * I, I * 4);
+            }
+            db = e.bias[2];
+        }
+        return create_from_host(desc, &w, gb.data(), db.data(), device, reserve_bytes, out);
+    } catch (const std::bad_alloc &) {
+        return fail(UMSX_EOOM, "host allocation failed");
+    }
 }
 
 }  // extern "C"

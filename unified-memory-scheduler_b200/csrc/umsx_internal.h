@@ -19,6 +19,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+#include <vector>
+
 #include "../../include/umsx.h"
 
 namespace umsx {
@@ -231,5 +234,26 @@ int launch_gen_normal_f32(uint64_t seed, uint64_t stream, uint64_t first, uint64
 int launch_gen_normal_bf16_to_f32(uint64_t seed, uint64_t stream, uint64_t first, uint64_t n, float scale,
                                   float *out, cudaStream_t s);
 int launch_bf16_to_f32(const uint16_t *in, float *out, size_t n, cudaStream_t s);
+
+// GGUF expert slices (umsx_gguf.cpp), the reference's LoadedExperts
+// (tools/engine/gguf_experts.hpp:14-20).  Index p: 0 gate, 1 up, 2 down.
+struct GgufExperts {
+    int hidden = 0, intermediate = 0, count = 0, n_ids = 0;  // count: experts in the file's tensors
+    int type[3] = {-1, -1, -1};                                // ggml type ids
+    int64_t shape[3][3] = {};                                  // ne[0..2] of each weight tensor
+    size_t stride[3] = {};                                     // bytes per expert
+    std::vector<uint8_t> packed[3];                            // [n_ids][stride]
+    std::vector<float> values[3];                              // [n_ids][rows * cols] when dequantized
+    bool has_bias[3] = {};
+    int64_t bias_len[3] = {};
+    std::vector<float> bias[3];                                // [n_ids][bias_len]
+};
+// Reads the slices of experts `ids` of layer `layer`; "" or an error message.  bounded:
+// the reference's limits for a selection (at most 16 ids, 32 Mi values per tensor).
+std::string gguf_load_experts(const std::string &first_shard, int layer, const std::vector<uint32_t> &ids,
+                              bool dequant, bool bounded, GgufExperts &out);
+// The router weight blk.L.ffn_gate_inp.weight ([E][H] fp32; shape = {H, E}) and its bias if present.
+std::string gguf_load_router(const std::string &first_shard, int layer, std::vector<float> &w, int64_t shape[2],
+                             std::vector<float> &b, bool &has_b);
 
 }  // namespace umsx

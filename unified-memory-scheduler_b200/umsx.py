@@ -35,6 +35,7 @@ EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "
            "umsx_combine",
            "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_destroy", "umsx_stack_forward",
            "umsx_stack_forward_host", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_route_static",
+           "umsx_gguf_load_experts", "umsx_gguf_experts_free", "umsx_moe_create_gguf",
            "umsx_kernel_launches", "umsx_last_error", "umsx_version"]
 
 
@@ -55,6 +56,12 @@ class Desc(C.Structure):
 class Weights(C.Structure):
     _fields_ = [("router_w", C.c_void_p), ("router_b", C.c_void_p), ("gate_up", C.c_void_p), ("gate", C.c_void_p),
                 ("up", C.c_void_p), ("down", C.c_void_p), ("gate_up_bias", C.c_void_p), ("down_bias", C.c_void_p)]
+
+
+class GgufExpertsC(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("hidden", "intermediate", "experts", "n_ids")] + \
+               [("quant", C.c_int32 * 3), ("stride", C.c_uint64 * 3), ("packed", C.c_void_p * 3),
+                ("values", C.c_void_p * 3), ("bias", C.c_void_p * 3), ("owner", C.c_void_p)]
 
 
 _lib = None
@@ -89,6 +96,9 @@ def lib():
         "umsx_stack_set_timing": (i32, [vp, i32]),
         "umsx_stack_stage_times": (i32, [vp, C.POINTER(C.c_float), i32]),
         "umsx_route_static": (i32, [vp, i32, i32, vp, vp, i32, i32, i32, i32, C.c_float, vp, vp, vp, vp]),
+        "umsx_gguf_load_experts": (i32, [C.c_char_p, i32, vp, i32, i32, C.POINTER(GgufExpertsC)]),
+        "umsx_gguf_experts_free": (None, [C.POINTER(GgufExpertsC)]),
+        "umsx_moe_create_gguf": (i32, [C.POINTER(Desc), C.c_char_p, i32, i32, sz, C.POINTER(vp)]),
         "umsx_kernel_launches": (u64, []),
         "umsx_last_error": (C.c_char_p, []),
         "umsx_version": (i32, []),
@@ -160,16 +170,52 @@ def route_static(x, router_w, router_b, experts: int, top_k: int, routing: int, 
     return ids, w, counts
 
 
+def load_gguf_experts(first_shard: str, layer: int, ids, dequantize: bool = True) -> dict:
+    """The selected experts of one layer from a GGUF checkpoint (the reference's load_gguf_experts,
+    tools/engine/gguf_experts.cpp:45-140): per projection ("gate", "up", "down") the ggml type, the
+    raw block bytes [n_ids][stride] (uint8), the fp32 values [n_ids][rows][cols] when dequantize,
+    and the fp32 bias [n_ids][len] when the file has one.  Raises UmsxError (EINVAL) on the
+    reference's validation failures."""
+    import numpy as np
+    ids_np = np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))
+    out = GgufExpertsC()
+    L = lib()
+    check(L.umsx_gguf_load_experts(os.fsencode(first_shard), int(layer), ids_np.ctypes.data, int(ids_np.size),
+                                   int(bool(dequantize)), C.byref(out)))
+    try:
+        n, H, I = out.n_ids, out.hidden, out.intermediate
+        res = {"hidden": H, "intermediate": I, "experts": out.experts, "ids": ids_np.copy()}
+        for p, name in enumerate(("gate", "up", "down")):
+            rows, cols = (I, H) if p < 2 else (H, I)
+            stride = int(out.stride[p])
+            d = {"type": int(out.quant[p]), "stride": stride,
+                 "packed": np.ctypeslib.as_array(C.cast(out.packed[p], C.POINTER(C.c_uint8)),
+                                                 shape=(n, stride)).copy()}
+            if out.values[p]:
+                d["values"] = np.ctypeslib.as_array(C.cast(out.values[p], C.POINTER(C.c_float)),
+                                                    shape=(n, rows, cols)).copy()
+            if out.bias[p]:
+                d["bias"] = np.ctypeslib.as_array(C.cast(out.bias[p], C.POINTER(C.c_float)), shape=(n, rows)).copy()
+            res[name] = d
+        return res
+    finally:
+        L.umsx_gguf_experts_free(C.byref(out))
+
+
 class MoeLayer:
     """One MoE layer resident on a GPU (the handle owns the repacked expert weights)."""
 
-    def __init__(self, desc: Desc, weights: dict | None = None, *, synthetic: dict | None = None, device: int = 0,
-                 reserve_bytes: int = 1 << 30):
+    def __init__(self, desc: Desc, weights: dict | None = None, *, synthetic: dict | None = None,
+                 gguf: tuple | None = None, device: int = 0, reserve_bytes: int = 1 << 30):
         self.desc = desc
         self.device = device
         self._h = C.c_void_p()
         L = lib()
-        if synthetic is not None:
+        if gguf is not None:  # (first shard path, layer index)
+            path, layer = gguf
+            check(L.umsx_moe_create_gguf(C.byref(desc), os.fsencode(path), int(layer), device, reserve_bytes,
+                                         C.byref(self._h)))
+        elif synthetic is not None:
             s = synthetic
             check(L.umsx_moe_create_synthetic(C.byref(desc), s["seed"], s.get("layer", 0), s.get("router_sigma", 0.02),
                                               s.get("router_bias_sigma", 0.1), s.get("bias_sigma", 0.02), device,
