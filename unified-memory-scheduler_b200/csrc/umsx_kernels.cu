@@ -39,7 +39,7 @@ __device__ int select_token(const RouterParams &p, const Dispatch &d, int t, int
     const int K = p.top_k;
     int sel;
     float w;
-    select_topk(d.logits + (size_t)t * p.experts, p.experts, K, p.routing, p.routed_scale, lane, sel, w);
+    select_topk_fit(d.logits + (size_t)t * p.experts, p.experts, K, p.routing, p.routed_scale, lane, sel, w);
     if (lane < K) {
         d.ids[(size_t)t * K + lane] = sel;
         d.weights[(size_t)t * K + lane] = w;

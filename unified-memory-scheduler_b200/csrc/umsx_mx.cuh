@@ -87,6 +87,16 @@ __device__ __forceinline__ void select_topk(const float *lg, int E, int K, int r
     w_out = w;
 }
 
+// select_topk with the per-lane value count fitted to E: with 32 values per lane for a
+// 128-expert router the one selecting warp of a token runs a long serial compare chain
+// over slots that hold no expert.
+__device__ __forceinline__ void select_topk_fit(const float *lg, int E, int K, int routing, float routed_scale,
+                                                int lane, int &sel, float &w_out) {
+    if (E <= 128) select_topk<4>(lg, E, K, routing, routed_scale, lane, sel, w_out);
+    else if (E <= 256) select_topk<8>(lg, E, K, routing, routed_scale, lane, sel, w_out);
+    else select_topk<kMaxExperts / 32>(lg, E, K, routing, routed_scale, lane, sel, w_out);
+}
+
 constexpr long long kWaitLimitCycles = 4000000;  // ~2 ms: bounded waits on mbarriers
 __host__ __device__ constexpr int pad4(int n) { return (n + 3) & ~3; }
 

@@ -589,7 +589,7 @@ __global__ void k_select_quant(const void *x, int x_dtype, int tokens, int H, in
     if (t >= tokens) return;
     int sel;
     float wgt;
-    select_topk(d.logits + (size_t)t * E, E, K, routing, routed_scale, lane, sel, wgt);
+    select_topk_fit(d.logits + (size_t)t * E, E, K, routing, routed_scale, lane, sel, wgt);
     if (lane < K) {
         d.ids[(size_t)t * K + lane] = sel;
         d.weights[(size_t)t * K + lane] = wgt;
