@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_decode_tc(const __grid_consta
         if (warp == 0) {
             int sel;
             float w;
-            select_topk_fit(p.logits, E, K, p.routing, p.routed_scale, lane, sel, w);
+            select_topk<8>(p.logits, E, K, p.routing, p.routed_scale, lane, sel, w);
             const bool has = lane < K;
             if (has && (sel < 0 || sel >= E)) {  // cannot happen (selection always picks a valid expert)
                 atomicOr(p.err, 8u);
