@@ -13,6 +13,12 @@ constexpr int kMaxExperts = 1024;
 
 __device__ __forceinline__ bool better(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
 
+// An unsigned key in the order of the float (no NaN): -0 and +0 share a key, as they compare equal.
+__device__ __forceinline__ uint32_t order_key(float f) {
+    const uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 // Warp-wide routing of one token from its E logits (all 32 lanes take part;
 // `lg` was written by other CTAs, so it is read through L2).  Lane r < K ends
 // with the expert of rank r in `sel` and its weight in `w`.  Ties go to the lower
@@ -59,12 +65,13 @@ __device__ __forceinline__ void select_topk(const float *lg, int E, int K, int r
             const int e = lane + 32 * j;
             if (e < E && !((taken >> j) & 1u) && better(v[j], e, bv, be)) { bv = v[j]; be = e; }
         }
-#pragma unroll
-        for (int s = 16; s >= 1; s >>= 1) {
-            const float ov = __shfl_xor_sync(kFull, bv, s);
-            const int oe = __shfl_xor_sync(kFull, be, s);
-            if (better(ov, oe, bv, be)) { bv = ov; be = oe; }
-        }
+        // warp-wide best by (value, lower index): the largest key, then the lowest index holding
+        // it (a lane with no candidate offers key 0, below every value's key), then its value
+        const uint32_t key = be == 0x7fffffff ? 0u : order_key(bv);
+        const uint32_t top = __reduce_max_sync(kFull, key);
+        const int win = (int)__reduce_min_sync(kFull, key == top ? (uint32_t)be : 0xffffffffu);
+        bv = __shfl_sync(kFull, bv, win & 31);
+        be = win;
         if ((be & 31) == lane) taken |= 1u << (be >> 5);
         if (lane == r) { my_sel = be; my_val = bv; }
     }
