@@ -96,9 +96,10 @@ struct DecSmem {
 
 constexpr int kDecRouterRows = 2;  // experts <= 2 * #CTAs
 
-// Ring stages per warp: deep for one token, where the weight stream is the bottleneck;
-// shallower when more tokens need more staging room.
-__host__ __device__ constexpr int ring_stages(int T) { return T == 1 ? 5 : 2; }
+// Ring stages per warp.  One token, 36 GPT-OSS-120B-shaped layers: depths 3 / 4 / 5 / 6 / 7
+// measured 800 / 786 / 771 / 743 / 714 tok/s (more bytes in flight per SM did not pay, less
+// shared memory did); more tokens need the staging room.
+__host__ __device__ constexpr int ring_stages(int T) { return T == 1 ? 3 : 2; }
 
 __host__ __device__ inline size_t decode_smem_layout(int T, int H, int I, size_t off[7]) {
     const size_t nb = H / 32, nbI = I / 32;
