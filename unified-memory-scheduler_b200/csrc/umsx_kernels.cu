@@ -399,19 +399,27 @@ __device__ __forceinline__ void q8_block(uint4 w01, uint4 w23, uint32_t ws16, in
     }
 }
 
-// One warp's weight stream: batches of Geo::kBatch steps (a step is a block pair
-// for MXFP4, 16 bytes per lane; a block for Q8_0, 32 bytes per lane), each batch
-// loaded with every load in flight at once.
+// Steps per load batch.  Q8_0 by jobs per pass: Qwen3-30B-A3B / DeepSeek-V2-Lite-shaped
+// layers measured best with 8 blocks at one job per pass (T = 1: 33.2 / 35.4 us against
+// 35.0 / 38.5 us with 4), 4 at two to four (T = 16), 2 at eight (T = 64: 490 against 572 us).
 template <int QUANT>
+__host__ __device__ constexpr int stream_batch(int mt) {
+    return QUANT == UMSX_QUANT_MXFP4 ? Geo<QUANT>::kBatch : (mt <= 1 ? 8 : (mt <= 4 ? 4 : 2));
+}
+
+// One warp's weight stream: batches of B steps (a step is a block pair for MXFP4,
+// 16 bytes per lane; a block for Q8_0, 32 bytes per lane), each batch loaded with
+// every load in flight at once.
+template <int QUANT, int B_ = Geo<QUANT>::kBatch>
 struct WBatch {
-    static constexpr int B = Geo<QUANT>::kBatch;
+    static constexpr int B = B_;
     uint4 w[B][QUANT == UMSX_QUANT_MXFP4 ? 1 : 2];
     uint32_t s[QUANT == UMSX_QUANT_MXFP4 ? B / 4 : B / 2];
 };
 
-template <int QUANT>
+template <int QUANT, int B_ = Geo<QUANT>::kBatch>
 struct WStream {
-    static constexpr int B = Geo<QUANT>::kBatch;
+    static constexpr int B = B_;
     const uint4 *cp;
     const uint32_t *sp;
     int steps;
@@ -420,7 +428,7 @@ struct WStream {
         sp = reinterpret_cast<const uint32_t *>(scales) + lane;
         steps = QUANT == UMSX_QUANT_MXFP4 ? nb / 2 : nb;
     }
-    __device__ __forceinline__ void load(int s0, WBatch<QUANT> &b) const {
+    __device__ __forceinline__ void load(int s0, WBatch<QUANT, B> &b) const {
         if constexpr (QUANT == UMSX_QUANT_MXFP4) {
 #pragma unroll
             for (int i = 0; i < B; ++i)
@@ -445,17 +453,16 @@ struct WStream {
 // Dot products of one warp's rows against the staged activations.  `cur` holds
 // batch 0 already in flight; the next batch is loaded before the current one is
 // consumed.  Blocks are consumed strictly in order, as the FMA chains require.
-template <int QUANT, int MT>
-__device__ __forceinline__ void warp_dot(const WStream<QUANT> &ws, WBatch<QUANT> cur, int nb, const Staged &a, int m,
-                                         int lane, float (&acc)[MT][8]) {
-    constexpr int B = Geo<QUANT>::kBatch;
+template <int QUANT, int MT, int B>
+__device__ __forceinline__ void warp_dot(const WStream<QUANT, B> &ws, WBatch<QUANT, B> cur, int nb, const Staged &a,
+                                         int m, int lane, float (&acc)[MT][8]) {
 #pragma unroll
     for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int l = 0; l < 8; ++l) acc[t][l] = 0.0f;
     const int half = lane >> 4;
     for (int s0 = 0; s0 < ws.steps; s0 += B) {
-        WBatch<QUANT> nxt;
+        WBatch<QUANT, B> nxt;
         if (s0 + B < ws.steps) ws.load(s0 + B, nxt);
 #pragma unroll
         for (int i = 0; i < B; ++i) {
@@ -550,9 +557,9 @@ __global__ void __launch_bounds__(64 * Geo<QUANT>::kChains) k_gate_up(GateUpPara
     const int nrg = mat.rows / RPW;
     const int rg_half = blockIdx.x * GW + wi;  // row group within the gate (or up) rows
     const int rg = p.fused ? half * (I / RPW) + rg_half : rg_half;
-    WStream<QUANT> ws;
+    WStream<QUANT, stream_batch<QUANT>(MT)> ws;
     ws.init(mat.codes + code_offset(QUANT, e, nrg, rg, nb), mat.scales + scale_offset(QUANT, e, nrg, rg, nb), nb, lane);
-    WBatch<QUANT> first;
+    WBatch<QUANT, stream_batch<QUANT>(MT)> first;
     ws.load(0, first);  // weights stream while the activations are staged
     const int rrow = lane % RPW;            // row within this warp
     const int row = rg_half * RPW + rrow;   // intermediate index
@@ -568,7 +575,7 @@ __global__ void __launch_bounds__(64 * Geo<QUANT>::kChains) k_gate_up(GateUpPara
         stage_internal(d.xq_codes, d.xq_scales, rows_s, m, nb, smem, MT, QUANT == UMSX_QUANT_Q8_0);
         __syncthreads();
         float acc[MT][8];
-        warp_dot<QUANT, MT>(ws, first, nb, st, m, lane, acc);
+        warp_dot<QUANT, MT, stream_batch<QUANT>(MT)>(ws, first, nb, st, m, lane, acc);
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
             if (t < m) {
@@ -622,10 +629,10 @@ __global__ void __launch_bounds__(W * 32) k_gemv(GemvParams p, GemvSrc src, Disp
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rg = blockIdx.x * W + warp;
     const bool active_warp = rg < nrg;
-    WStream<QUANT> ws;
+    WStream<QUANT, stream_batch<QUANT>(MT)> ws;
     ws.init(p.m.codes + code_offset(QUANT, e, nrg, active_warp ? rg : 0, nb),
             p.m.scales + scale_offset(QUANT, e, nrg, active_warp ? rg : 0, nb), nb, lane);
-    WBatch<QUANT> first;
+    WBatch<QUANT, stream_batch<QUANT>(MT)> first;
     if (active_warp) ws.load(0, first);
     if (p.prefetch_early) {  // the weights were chosen two kernels back; the activations come from the last one
         pdl_wait();
@@ -698,7 +705,7 @@ __global__ void __launch_bounds__(W * 32) k_gemv(GemvParams p, GemvSrc src, Disp
         __syncthreads();
         if (active_warp) {
             float acc[MT][8];
-            warp_dot<QUANT, MT>(ws, first, nb, st, m, lane, acc);
+            warp_dot<QUANT, MT, stream_batch<QUANT>(MT)>(ws, first, nb, st, m, lane, acc);
 #pragma unroll
             for (int t = 0; t < MT; ++t) {
                 if (t < m) {
