@@ -91,14 +91,27 @@ __device__ void build_dispatch_cta(const Dispatch &d, int entries, int K, int e_
     }
     __syncthreads();
     for (int sl = n_act_s + tid; sl < e_local; sl += nth) d.slots[sl] = make_int4(-1, 0, 0, 0);
-    for (int j = tid; j < entries; j += nth) {
-        const int e = ids_s[j];
-        if (e < 0 || e >= e_local) continue;
-        int before = 0;
-        for (int i = 0; i < j; ++i) before += ids_s[i] == e;
-        const int pos = off[e] + before;
-        d.job_token[pos] = j / K;
-        d.job_rank[pos] = j % K;
+    for (int e = tid; e < e_local; e += nth) cnt[e] = 0;  // reused: jobs placed so far per expert
+    __syncthreads();
+    // Job lists in (token, rank) order: one warp walks the entries 32 at a time; an entry's
+    // place among the earlier entries of its expert = the count placed by earlier chunks +
+    // the lower lanes of this chunk with the same expert (a match mask).
+    if (tid < 32) {
+        const unsigned below = (1u << tid) - 1u;
+        for (int j0 = 0; j0 < entries; j0 += 32) {
+            const int j = j0 + tid;
+            const int e = j < entries ? ids_s[j] : -1;
+            const bool mine = e >= 0 && e < e_local;
+            const unsigned grp = __match_any_sync(kFull, mine ? e : -1);
+            if (mine) {
+                const int pos = off[e] + cnt[e] + __popc(grp & below);
+                d.job_token[pos] = j / K;
+                d.job_rank[pos] = j % K;
+            }
+            __syncwarp();
+            if (mine && 31 - __clz(grp) == tid) cnt[e] += __popc(grp);  // the group's highest lane
+            __syncwarp();
+        }
     }
 }
 
