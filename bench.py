@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the bounded CPU sample")
+    ap.add_argument("--ref-seconds", type=float, default=150.0, help="timed budget of the --impl reference arm")
+    ap.add_argument("--no-prefill", action="store_true", help="decode line without the prefill sub-record")
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the ranks (prefill)")
     a = ap.parse_args()
     if a.tokens is None:
@@ -92,26 +94,71 @@ def dist_env():
 # ----------------------------------------------------------------------------- clocks
 
 class Clocks:
-    """nvidia-smi samples during the timed region (read-only)."""
+    """SM clock and clock-event reasons sampled every 2 ms during the timed region, read-only, by an
+    NVML polling thread (nvidia_ml_py); nvidia-smi's CSV sampler is the fallback."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, index: int):
-        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
-        self.proc = None
         self.index = index
+        self.rows = []
+        self.thread = None
+        self.stop = False
+        self.nvml = None
+        self.proc = None
+        self.path = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll(self, h):
+        import pynvml
+        mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop:
+            try:
+                self.rows.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), mx, get_reasons(h),
+                                  pynvml.nvmlDeviceGetPowerUsage(h) / 1e3))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+        import threading
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "20"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            h = self._handle()
+            self.nvml = True
+            self.thread = threading.Thread(target=self._poll, args=(h,), daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 1.0:  # the sampler is running before timing starts
+                time.sleep(0.001)
         except Exception:
-            self.proc = None
+            self.nvml = None
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                              "--format=csv,noheader,nounits", "-lms", "20"],
+                                             stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            except Exception:
+                self.proc = None
         return self
 
     def __exit__(self, *exc):
+        self.stop = True
+        if self.thread:
+            self.thread.join(timeout=2)
         if self.proc:
             self.proc.terminate()
             try:
@@ -120,6 +167,13 @@ class Clocks:
                 self.proc.kill()
 
     def summary(self):
+        if self.nvml:
+            if not self.rows:
+                return None
+            sm = [r[0] for r in self.rows]
+            reasons = sorted({name for r in self.rows for bit, name in self.REASONS.items() if r[2] & bit})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in self.rows), "reasons": reasons,
+                    "samples": len(self.rows), "power_w_max": max(r[3] for r in self.rows), "source": "nvml"}
         try:
             rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
             os.unlink(self.path)
@@ -132,59 +186,125 @@ class Clocks:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 # ----------------------------------------------------------------------------- CPU baseline
 
-def cpu_baseline(a, budget_s: float) -> dict:
-    """The reference's exact packed MXFP4 path (oracle/_ref) on this host's cores, bounded sample."""
+REF_HOST_LAYERS = 4   # distinct host layers the CPU legs rotate through (about 1.7 GB each)
+REF_TOKEN_POOL = 16   # seeded tokens cycled over the steps
+
+
+def bench_host_weights(orc, cfg, layer: int, threads: int):
+    """The GPU stack's layer `layer` (the same seeded tensors umsx_moe_create_synthetic draws),
+    drawn on the host with `threads` generator threads."""
     import numpy as np
-    from oracle.oracle import Oracle, OrcDesc, RefKernels
-    from tests.helpers import host_weights, oracle_desc
-    pkg = load_pkg()
-    cfg = pkg.configs.GPT_OSS_120B
-    orc = Oracle()
-    cores = len(os.sched_getaffinity(0))
-    kind = "port"
-    ref = None
+    from oracle.oracle import LayerWeights
+    from tests.helpers import C, U
+    E, H, I, s = cfg.experts, cfg.hidden, cfg.intermediate, cfg.seed
+    gu = np.empty((E, 2 * I, H // 32 * 17), np.uint8)
+    orc.gen_blocks_into(U.QUANT_MXFP4, gu, s, C.stream_id(layer, C.KIND_GATE_UP), 0, E * 2 * I * (H // 32), threads)
+    dn = np.empty((E, H, I // 32 * 17), np.uint8)
+    orc.gen_blocks_into(U.QUANT_MXFP4, dn, s, C.stream_id(layer, C.KIND_DOWN), 0, E * H * (I // 32), threads)
+    rw = orc.gen_normal_f32(s, C.stream_id(layer, C.KIND_ROUTER_W), 0, E * H, cfg.router_sigma).reshape(E, H)
+    rb = orc.gen_normal_f32(s, C.stream_id(layer, C.KIND_ROUTER_B), 0, E, cfg.router_bias_sigma)
+    gub = orc.gen_normal_bf16(s, C.stream_id(layer, C.KIND_GU_BIAS), 0, E * 2 * I, cfg.bias_sigma).reshape(E, 2 * I)
+    db = orc.gen_normal_bf16(s, C.stream_id(layer, C.KIND_DOWN_BIAS), 0, E * H, cfg.bias_sigma).reshape(E, H)
+    return LayerWeights(rw, rb, gu, None, None, dn, gub, db)
+
+
+class ReferenceStack:
+    """The reference's exact packed MXFP4 CPU path (oracle/_ref: tools/trace/exact_packed_cpu.h and
+    cpu_mxfp4_vnni.cpp compiled from the reference sources), or the oracle port where that build is
+    absent, driving the GPT-OSS-120B-shaped stack h <- h + MoE(RMSNorm(h)) on the host cores.  The
+    stack's `layers` layers rotate through REF_HOST_LAYERS distinct host layers (layer l uses host
+    layer l mod 4, each drawn from the generator's seed for that layer index), so consecutive layers
+    touch different expert bytes, as the GPU's 36 distinct layers do."""
+
+    def __init__(self, layers: int):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle.oracle import Oracle, RefKernels
+        from tests.helpers import oracle_desc
+        pkg = load_pkg()
+        self.cfg = pkg.configs.GPT_OSS_120B
+        self.orc = Oracle()
+        self.cores = len(os.sched_getaffinity(0))
+        self.layers = layers
+        self.ref = None
+        try:
+            ref = RefKernels()
+            if ref.supported():
+                self.ref = ref
+        except Exception:
+            self.ref = None
+        self.kind = "reference" if self.ref else "port"
+        self.desc = oracle_desc(self.cfg)
+        t0 = time.time()
+        n = self.n_host = min(REF_HOST_LAYERS, layers)
+        self.host = [bench_host_weights(self.orc, self.cfg, l, self.cores) for l in range(n)]
+        if self.ref:  # the reference driver packs each layer into its own layout (in parallel)
+            with ThreadPoolExecutor(max_workers=n) as ex:
+                self.handles = list(ex.map(lambda w: self.ref.layer(self.desc, w), self.host))
+            self.host = None  # the packed copies are what it reads
+        self.setup_s = time.time() - t0
+
+    def layer(self, l: int, x):
+        if self.ref:
+            return self.ref.layer_forward(self.handles[l % len(self.handles)], x, self.cfg.hidden, self.cores)
+        return self.orc.moe_layer(self.desc, self.host[l % len(self.host)], x, threads=self.cores)["out"]
+
+    def step(self, x):
+        import numpy as np
+        h = x.astype(np.float32)
+        for l in range(self.layers):
+            h = (h + self.layer(l, self.orc.rmsnorm(h, 1e-5))).astype(np.float32)
+        return h
+
+    def timed(self, tokens: int, steps: int, warmup: int, budget_s: float):
+        """Runs `warmup` then up to `steps` timed steps (fewer if the budget runs out); returns the
+        per-step seconds of the steps timed."""
+        import numpy as np
+        rng = np.random.default_rng(7)
+        pool = [rng.standard_normal((tokens, self.cfg.hidden)).astype(np.float32) for _ in range(REF_TOKEN_POOL)]
+        for i in range(warmup):
+            self.step(pool[i % REF_TOKEN_POOL])
+        times = []
+        t_start = time.time()
+        for i in range(steps):
+            s = time.perf_counter()
+            self.step(pool[(warmup + i) % REF_TOKEN_POOL])
+            times.append(time.perf_counter() - s)
+            if time.time() - t_start > budget_s:
+                break
+        return times
+
+    def close(self):
+        if self.ref:
+            for h in self.handles:
+                self.ref.layer_destroy(h)
+            self.handles = []
+
+    def sample_text(self, tokens: int, timed: int, warmup: int):
+        return (f"{tokens} token(s) per step through all {self.layers} layers of the GPT-OSS-120B-shaped stack "
+                f"(RMSNorm + residual; 128 MXFP4 experts per layer, top-4), the layers rotating through "
+                f"{self.n_host} distinct host layers of the seeded weights "
+                f"(about 1.7 GB each) and {REF_TOKEN_POOL} seeded tokens cycling over the steps; {warmup} warm-up "
+                f"and {timed} timed steps on {self.cores} host threads; no extrapolation across layers")
+
+
+def cpu_baseline(a, budget_s: float) -> dict:
+    """A bounded sample of the same workload on the CPU path (see ReferenceStack)."""
+    T = a.tokens if a.mode == "decode" else min(a.tokens, 4)
+    rs = ReferenceStack(a.layers)
     try:
-        ref = RefKernels()
-        if ref.supported():
-            kind = "reference"
-        else:
-            ref = None
-    except Exception:
-        ref = None
-    t0 = time.time()
-    w = host_weights(orc, cfg, layer=0)
-    gen_s = time.time() - t0
-    T = a.tokens if a.mode == "decode" else min(a.tokens, 64)
-    rng = np.random.default_rng(7)
-    x = rng.standard_normal((T, cfg.hidden)).astype(np.float32)
-    desc = oracle_desc(cfg)
-    if kind == "reference":
-        h = ref.layer(desc, w)
-        run = lambda: ref.layer_forward(h, x, cfg.hidden, cores)  # noqa: E731
-    else:
-        run = lambda: orc.moe_layer(desc, w, x, threads=cores)  # noqa: E731
-    run()
-    times = []
-    t_start = time.time()
-    while time.time() - t_start < budget_s and len(times) < 2000:
-        s = time.perf_counter()
-        run()
-        times.append(time.perf_counter() - s)
-    if kind == "reference":
-        ref.layer_destroy(h)
-    layer_s = statistics.median(times)
-    tok_s = T / (layer_s * a.layers)
-    return {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": kind,
-            "sample": (f"{T} token(s) through one seeded GPT-OSS-120B-shaped layer (128 MXFP4 experts, "
-                       f"host-generated in {gen_s:.1f}s), median of {len(times)} passes "
-                       f"({layer_s * 1e3:.3f} ms/layer) scaled to {a.layers} layers"
-                       + ("" if a.mode == "decode" else f"; prefill sampled at T={T} tokens/s")),
-            "layer_ms": layer_s * 1e3}
+        times = rs.timed(T, steps=10 ** 6, warmup=2, budget_s=budget_s)
+    finally:
+        rs.close()
+    step_s = statistics.mean(times)
+    return {"value": T / step_s, "unit": "tokens/s", "cores": rs.cores, "kind": rs.kind,
+            "sample": rs.sample_text(T, len(times), 2) + (f"; prefill sampled at T={T}" if a.mode != "decode" else ""),
+            "ms_per_step": step_s * 1e3, "setup_s": rs.setup_s}
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -348,9 +468,14 @@ def gpu_arm(a):
            "stack_roofline": {"bytes_per_step": stack_bytes, "achieved_gbs": stack_bytes / (ms_step / 1e3) / 1e9,
                               "frac": stack_bytes / (ms_step / 1e3) / 1e9 / peak},
            "stages_ms_per_step": stages, "gpu_launches": launches, "clocks": clocks, "e2e": e2e}
+    if world == 1 and a.mode == "decode" and not a.no_prefill:
+        try:
+            res["prefill"] = prefill_record(pkg, cfg, layers, dev, a)
+        except Exception as exc:  # the decode line must still be printed
+            res["prefill"] = {"error": str(exc)[:200]}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:
-            res["cpu_baseline"] = {k: v for k, v in cpu_baseline(a, a.cpu_seconds).items() if k != "layer_ms"}
+            res["cpu_baseline"] = cpu_baseline(a, a.cpu_seconds)
         except Exception as exc:  # the GPU line must still be printed
             res["cpu_baseline"] = {"value": None, "error": str(exc)[:200]}
     stack.close()
@@ -360,6 +485,51 @@ def gpu_arm(a):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res))
+
+
+def prefill_record(pkg, cfg, layers, dev, a, tokens: int = 4096, steps: int = 5, warmup: int = 3) -> dict:
+    """The metric's second regime on the same 36 layers: one step = `tokens` tokens through the stack
+    (router, tcgen05 grouped GEMMs for gate_up and down, rank-order combine + residual per layer),
+    inputs resident in HBM (far larger than L2), CUDA events on the launching stream."""
+    import numpy as np
+    import torch
+    T, H = tokens, cfg.hidden
+    st = pkg.MoeStack(layers, max_tokens=T)
+    rng = np.random.default_rng(2000)
+    xs = [torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(torch.bfloat16).to(dev)
+          for _ in range(2)]
+    out = torch.empty((T, H), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(warmup):
+        st.forward(xs[i % 2], out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index) as clk:
+        e0.record(stream)
+        for i in range(steps):
+            st.forward(xs[i % 2], out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    st.set_timing(True)
+    st.forward(xs[0], out)
+    stages = {k: v / a.layers for k, v in st.stage_times().items()}
+    st.set_timing(False)
+    st.close()
+    gu_flops = 2.0 * T * cfg.top_k * 2 * cfg.intermediate * H
+    dn_flops = 2.0 * T * cfg.top_k * H * cfg.intermediate
+    bf16_sus, kind = peaks("bf16_tflops_sustained")
+    gu_tf = gu_flops / (stages["gate_up"] / 1e3) / 1e12
+    return {"tokens_per_step": T, "value": T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "warmup": warmup, "layers": a.layers,
+            "stage_ms_per_layer": stages,
+            "roofline": {"kernel": "k_moe_gemm gate_up (tcgen05 kind::f16, exact f16 MXFP4 weights x hi+lo f16 "
+                                   "Q8_0 activations)", "bound": "tensor",
+                         "achieved": gu_tf, "unit": "TFLOP/s", "useful_flops_per_launch": gu_flops,
+                         "peak": bf16_sus, "frac": gu_tf / bf16_sus, "peak_source": f"{kind} bf16_tflops_sustained",
+                         "frac_of_nominal_fp4_dense_9000": gu_tf / 9000.0},
+            "layer_tflops_useful": (gu_flops + dn_flops) / ((stages["gate_up"] + stages["down"]) / 1e3) / 1e12,
+            "clocks": clk.summary(), "l2": "inputs larger than L2 (61 GB of weights, 4096 x 2880 activations)"}
 
 
 def ep_arm(a):
@@ -480,19 +650,32 @@ def traffic_for(a, kernel: str):
 
 
 def reference_arm(a):
+    """The reference's CPU path on this host's cores, for the GPU arm's metric and config: each
+    step runs the same token count through all stack layers (ReferenceStack), --warmup steps
+    untimed, then up to --steps timed steps within a budget of a few minutes (the line reports the
+    count actually timed)."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    base = cpu_baseline(a, a.cpu_seconds)
-    per_step_ms = a.tokens / base["value"] * 1e3
-    res = {"metric": metric_name(a), "value": base["value"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
-           "warmup": a.warmup, "ms_per_step": per_step_ms, "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
-           "impl": "reference",
+    T = a.tokens if a.mode == "decode" else min(a.tokens, 4)
+    rs = ReferenceStack(a.layers)
+    try:
+        times = rs.timed(T, steps=a.steps, warmup=a.warmup, budget_s=a.ref_seconds)
+    finally:
+        rs.close()
+    step_s = statistics.mean(times)
+    value = T / step_s
+    res = {"metric": metric_name(a), "value": value, "unit": "tokens/s", "n_gpus": world, "steps": len(times),
+           "steps_requested": a.steps, "warmup": a.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate",
+           "data": "synthetic", "impl": "reference",
            "config": {"workload": f"gpt-oss-120b-stack {a.mode}", "layers": a.layers, "experts": 128, "top_k": 4,
-                      "hidden": 2880, "ffn": 2880, "quant": "mxfp4", "tokens_per_step_per_gpu": a.tokens},
-           "cpu_baseline": {k: base[k] for k in ("kind", "cores", "sample", "value", "unit")},
-           "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                      "hidden": 2880, "ffn": 2880, "quant": "mxfp4", "tokens_per_step_per_gpu": T,
+                      "global_batch": T, "parallelism": "single"},
+           "cpu_baseline": {"kind": rs.kind, "cores": rs.cores, "value": value, "unit": "tokens/s",
+                            "sample": rs.sample_text(T, len(times), a.warmup)
+                            + (f"; prefill sampled at T={T}" if a.mode != "decode" else "")},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(res))
 
 

@@ -127,6 +127,13 @@ umsx_status umsx_moe_forward_host(umsx_moe *moe, const void *x, int x_dtype, int
 umsx_status umsx_moe_forward_jobs(umsx_moe *moe, const void *x, int x_dtype, int tokens, int32_t *ids,
                                   float *weights, float *y, umsx_stream stream);
 
+/* Status of the handle's earlier calls on `stream`: synchronises the stream, then reads and clears
+ * the handle's device status word.  UMSX_ENONFINITE if a combined output (the layer's result) was
+ * inf or NaN -- the reference rejects those (ExpertPlan, tools/engine/expert_dispatch.cpp:14-18,
+ * :84-85) -- UMSX_ETIMEOUT if a bounded device wait gave up, else UMSX_OK.  The word is sticky
+ * until read here or by a _host call, which return the same statuses. */
+umsx_status umsx_moe_status(umsx_moe *moe, umsx_stream stream);
+
 /* Router only: logits (fixed fp32 reduction order), softmax/top-k/renormalise per
  * desc.routing, ties to the lowest expert index (topk-tie-probe.cpp:111-113),
  * per-expert counts.  ids [T][k] int32, weights [T][k] fp32, counts [E] int32 (may be NULL). */
@@ -150,7 +157,9 @@ umsx_status umsx_mul_mat_id(umsx_moe *moe, int proj, const float *b, int n_b, co
                             int tokens, float *dst, umsx_stream stream);
 
 /* Weighted combine in rank order from 0.0f without contraction
- * (ExpertPlan::execute, expert_dispatch.cpp:77-87): out[t][i] = sum_r w[t][r] * y[t][r][i]. */
+ * (ExpertPlan::execute, expert_dispatch.cpp:77-87): out[t][i] = sum_r w[t][r] * y[t][r][i].
+ * Handle-free and asynchronous, so it does not check its output for non-finite values (the
+ * layer entry points do, see umsx_moe_status). */
 umsx_status umsx_combine(const float *y, const float *weights, int tokens, int top_k, int width, float *out,
                          umsx_stream stream);
 
@@ -178,10 +187,18 @@ umsx_status umsx_stack_forward(umsx_stack *stack, const void *x, int x_dtype, in
 /* Same with host buffers (pinned for overlap); copies in and out and synchronises. */
 umsx_status umsx_stack_forward_host(umsx_stack *stack, const void *x, int x_dtype, int tokens, float *out,
                                     umsx_stream stream);
+/* umsx_moe_status for a stack: every layer's combined output is checked. */
+umsx_status umsx_stack_status(umsx_stack *stack, umsx_stream stream);
 /* With timing on, each replay timestamps the router, gate_up, down and combine stage of every
  * layer; stage_times returns the four per-stage sums (ms) over the layers of the last replay. */
 umsx_status umsx_stack_set_timing(umsx_stack *stack, int enable);
 umsx_status umsx_stack_stage_times(umsx_stack *stack, float *ms, int n_stages);
+/* Fault injection for failure-detection tests (no counterpart in the reference): the next
+ * one-launch decode forward of the stack runs with CTA `cta` withholding its first grid-barrier
+ * arrival and every grid-barrier wait bounded by wait_limit_cycles SM cycles, so the waits run out,
+ * the kernel ends, and the call reports UMSX_ETIMEOUT (a _host call, or umsx_stack_status).  One
+ * forward only; a CTA index beyond the grid injects nothing. */
+umsx_status umsx_stack_inject_fault(umsx_stack *stack, int cta, int64_t wait_limit_cycles);
 
 /* The router of umsx_route without a handle and without allocating anything (no counterpart
  * in the reference).  For callers that cannot call cudaMalloc: an operator inside a framework
@@ -193,7 +210,9 @@ umsx_status umsx_stack_stage_times(umsx_stack *stack, float *ms, int n_stages);
  * 512 KiB array inside this library that every GPU loading it holds until the process exits;
  * limits: T <= 64, E <= 256, k <= min(8, E), H a multiple of 64 up to 4096 (UMSX_EINVAL
  * beyond).  It runs on the calling thread's current device; the first call on a device looks
- * up the array's device address, so make that first call before any stream capture.  All calls
+ * up the array's device address, so make that first call before any stream capture; a
+ * cudaDeviceReset (or anything else that destroys the device's primary context) invalidates that
+ * address, so a process that resets a device must not call this entry point on it again.  All calls
  * on a device share the array: calls that overlap on the GPU (other streams, other threads)
  * race and must be serialised by the caller.  Errors read back through umsx_last_error(). */
 umsx_status umsx_route_static(const void *x, int x_dtype, int tokens, const float *router_w, const float *router_b,

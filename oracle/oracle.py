@@ -207,6 +207,29 @@ class Oracle:
         self.lib.orc_gen_mxfp4(seed, stream, first, nblocks, e_lo, e_span, _ptr(out, _u8p))
         return out
 
+    def gen_blocks_into(self, quant, out, seed, stream, first, nblocks, threads=1):
+        """Fills the uint8 array `out` (nblocks ggml blocks, C-contiguous) with the generator's blocks
+        first..first+nblocks-1, split over `threads` host threads (the C generator releases the GIL)."""
+        from concurrent.futures import ThreadPoolExecutor
+        bb = BLOCK_BYTES[quant]
+        flat = out.reshape(-1)
+        assert flat.size == nblocks * bb and flat.flags["C_CONTIGUOUS"]
+        per = max(1, (nblocks + threads - 1) // threads)
+
+        def run(i):
+            lo, hi = i * per, min(nblocks, (i + 1) * per)
+            if lo >= hi:
+                return
+            ptr = flat[lo * bb:].ctypes.data_as(_u8p)
+            if quant == QUANT_MXFP4:
+                self.lib.orc_gen_mxfp4(seed, stream, first + lo, hi - lo, 119, 5, ptr)
+            else:
+                self.lib.orc_gen_q8_0(seed, stream, first + lo, hi - lo, ptr)
+
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(run, range(threads)))
+        return out
+
     def gen_q8_0(self, seed, stream, first, nblocks):
         out = np.empty(nblocks * 34, np.uint8)
         self.lib.orc_gen_q8_0(seed, stream, first, nblocks, _ptr(out, _u8p))

@@ -117,3 +117,49 @@ def write_layer_gguf(paths, layer: int, w: LayerWeights, quant: int, hidden: int
         wr.write_kv_data_to_file()
         wr.write_tensors_to_file()
         wr.close()
+
+
+def selected_host_weights(orc, cfg, layer: int, experts) -> LayerWeights:
+    """host_weights with only the listed experts' blocks drawn (the others stay zero): enough for the
+    oracle, which reads only the experts its routing selects, at full BASELINE shapes."""
+    E, H, I = cfg.experts, cfg.hidden, cfg.intermediate
+    s, sid = cfg.seed, C.stream_id
+    bb = U.BLOCK_BYTES[cfg.quant]
+
+    def blocks(kind, rows, cols):
+        out = np.zeros((E, rows, cols // 32 * bb), np.uint8)
+        per = rows * (cols // 32)
+        for e in sorted({int(v) for v in np.asarray(experts).reshape(-1)}):
+            if cfg.quant == U.QUANT_MXFP4:
+                out[e] = orc.gen_mxfp4(s, sid(layer, kind), e * per, per, 119, 5).reshape(rows, -1)
+            else:
+                out[e] = orc.gen_q8_0(s, sid(layer, kind), e * per, per).reshape(rows, -1)
+        return out
+
+    router_w = orc.gen_normal_f32(s, sid(layer, C.KIND_ROUTER_W), 0, E * H, cfg.router_sigma).reshape(E, H)
+    router_b = orc.gen_normal_f32(s, sid(layer, C.KIND_ROUTER_B), 0, E, cfg.router_bias_sigma) \
+        if cfg.has_router_bias else None
+    gate_up = gate = up = None
+    if cfg.fused_gate_up:
+        gate_up = blocks(C.KIND_GATE_UP, 2 * I, H)
+    else:
+        gate, up = blocks(C.KIND_GATE_UP, I, H), blocks(C.KIND_UP, I, H)
+    down = blocks(C.KIND_DOWN, H, I)
+    gub = db = None
+    if cfg.has_bias:
+        gub = orc.gen_normal_bf16(s, sid(layer, C.KIND_GU_BIAS), 0, E * 2 * I, cfg.bias_sigma).reshape(E, 2 * I)
+        db = orc.gen_normal_bf16(s, sid(layer, C.KIND_DOWN_BIAS), 0, E * H, cfg.bias_sigma).reshape(E, H)
+    return LayerWeights(router_w, router_b, gate_up, gate, up, down, gub, db)
+
+
+def oracle_stack(orc, cfg, xb: np.ndarray, n_layers: int, threads: int = 16, eps: float = 1e-5) -> np.ndarray:
+    """h <- h + MoE_l(RMSNorm(h)) on the oracle at full shapes, drawing only the routed experts."""
+    h = bf16_bits_to_f32(xb).copy()
+    desc = oracle_desc(cfg)
+    for l in range(n_layers):
+        xn = orc.rmsnorm(h, eps)
+        router = selected_host_weights(orc, cfg, l, [])
+        ids, _, _ = orc.route(desc, router, xn)
+        w = selected_host_weights(orc, cfg, l, ids)
+        h = (h + orc.moe_layer(desc, w, xn, threads=threads)["out"]).astype(np.float32)
+    return h

@@ -92,3 +92,49 @@ def test_exchange_plan_is_a_permutation():
             assert sorted(r_jobs.tolist()) == list(range(t0 * K, t1 * K))
             recv_total += len(r_jobs)
         assert sorted(torch.cat(sent).tolist()) == list(range(T * K)) and recv_total == T * K
+
+
+def _loss_worker(rank, world, port, q):
+    """Both ranks exchange once; then rank 1 dies between steps (no collective in flight) and rank
+    0's next exchange must end in an error, not a hang."""
+    import datetime
+    import time
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
+        ep = _ep_module()
+        T, K, H, E = 6, 2, 8, 4
+        ids = torch.tensor([[0, 2], [1, 3], [2, 0], [3, 1], [0, 1], [2, 3]], dtype=torch.int32)
+        y = torch.full((T, K, H), float(rank))
+        ep.exchange(y, ids, E)
+        if rank == 1:
+            q.put((rank, "left"))
+            q.close()
+            q.join_thread()  # the message is out before the process goes
+            os._exit(0)  # the rank is lost between steps
+        time.sleep(1.0)
+        t0 = time.time()
+        try:
+            ep.exchange(y, ids, E)
+            q.put((rank, "no error"))
+        except Exception as exc:  # the expected outcome
+            q.put((rank, f"raised after {time.time() - t0:.1f}s: {type(exc).__name__}"))
+    except Exception as exc:
+        q.put((rank, "setup failed: " + repr(exc)))
+
+
+def test_rank_loss_between_steps_raises_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_loss_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results[1] == "left"
+    assert results[0].startswith("raised after"), results[0]

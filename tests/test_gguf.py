@@ -91,6 +91,16 @@ def test_validation_errors(oracle, tmp_path):
     open(bad, "wb").write(raw[:40])
     with pytest.raises(U.UmsxError, match="could not be read"):
         U.load_gguf_experts(bad, 1, [0])
+    # extents that each pass the per-dimension bound but whose product overflows int64
+    name = b"blk.1.ffn_gate_exps.weight"
+    at = raw.index(name) + len(name)
+    n_dims = int.from_bytes(raw[at:at + 4], "little")
+    assert n_dims == 3
+    huge = (1 << 40).to_bytes(8, "little")
+    patched = raw[:at + 4] + huge + huge + raw[at + 20:]
+    open(bad, "wb").write(patched)
+    with pytest.raises(U.UmsxError, match="element count overflows"):
+        U.load_gguf_experts(bad, 1, [0])
 
 
 def test_create_rejects_a_descriptor_that_does_not_match(oracle, tmp_path):

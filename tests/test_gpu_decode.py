@@ -98,21 +98,16 @@ def test_nan_input_routes_to_valid_experts(oracle, tokens):
     layer.close()
 
 
-# ---- one token: the tensor-core kernel and the SIMT kernel --------------------------------
+# ---- one token: the one-token kernel (k_decode1) at assorted shapes --------------------------
 
-_TC_SHAPES = [dict(), dict(hidden=320, intermediate=128, experts=16, top_k=8), dict(hidden=192, intermediate=320, experts=200, top_k=3)]
+_T1_SHAPES = [dict(), dict(hidden=320, intermediate=128, experts=16, top_k=8), dict(hidden=192, intermediate=320, experts=200, top_k=3)]
 
 
-@pytest.mark.parametrize("path", ["tc", "simt"])
-@pytest.mark.parametrize("shape", range(len(_TC_SHAPES)))
-def test_one_token_layer_bit_exact(oracle, monkeypatch, path, shape):
-    """UMSX_DECODE_PATH=tc (set before the layer is created, which then keeps the tensor-core
-    weight copy) requires the tensor-core kernel (the call fails if it cannot run), =simt the SIMT
-    kernel; both must reproduce the oracle's bits.  The shapes cover a
-    partial last K stage (5 block pairs), top-8, and more experts than a CTA's router rows
-    hold at once."""
-    monkeypatch.setenv("UMSX_DECODE_PATH", path)
-    cfg = small_config(**_TC_SHAPES[shape])
+@pytest.mark.parametrize("shape", range(len(_T1_SHAPES)))
+def test_one_token_layer_bit_exact(oracle, shape):
+    """The shapes cover a partial last ring stage (5 block pairs), top-8, and more experts than
+    CTAs (two router rows on some CTAs)."""
+    cfg = small_config(**_T1_SHAPES[shape])
     w = host_weights(oracle, cfg)
     xb = x_bits(oracle, cfg, 1)
     want = oracle.moe_layer(oracle_desc(cfg), w, bf16_bits_to_f32(xb), threads=8)
@@ -128,9 +123,7 @@ def test_one_token_layer_bit_exact(oracle, monkeypatch, path, shape):
     layer.close()
 
 
-@pytest.mark.parametrize("path", ["tc", "simt"])
-def test_one_token_stack_bit_exact(oracle, monkeypatch, path):
-    monkeypatch.setenv("UMSX_DECODE_PATH", path)
+def test_one_token_stack_bit_exact(oracle):
     cfg = small_config()
     L = 4
     layers = [U.MoeLayer(cfg.desc(1), synthetic=cfg.synthetic(layer=l)) for l in range(L)]
@@ -144,10 +137,9 @@ def test_one_token_stack_bit_exact(oracle, monkeypatch, path):
         l.close()
 
 
-def test_one_token_full_size_gpt_oss_20b_layer(oracle, monkeypatch):
-    """configs[0] shapes (2880 / 2880, 32 experts, top-4) through the tensor-core kernel."""
+def test_one_token_full_size_gpt_oss_20b_layer(oracle):
+    """configs[0] shapes (2880 / 2880, 32 experts, top-4) through the one-token kernel."""
     from tests.helpers import C
-    monkeypatch.setenv("UMSX_DECODE_PATH", "tc")
     cfg = C.GPT_OSS_20B
     w = host_weights(oracle, cfg)
     xb = x_bits(oracle, cfg, 1)
@@ -156,28 +148,3 @@ def test_one_token_full_size_gpt_oss_20b_layer(oracle, monkeypatch):
     out = layer.forward(to_cuda_bf16(xb)).cpu().numpy()
     np.testing.assert_array_equal(bits(out), bits(want["out"]))
     layer.close()
-
-
-def test_tensor_core_decode_matches_simt_gpt_oss_120b_shape(monkeypatch):
-    """Three GPT-OSS-120B-shaped layers: the tensor-core kernel, the SIMT kernel and the
-    per-stage kernels give identical bits for one token."""
-    from tests.helpers import C
-    cfg = C.GPT_OSS_120B
-    monkeypatch.setenv("UMSX_DECODE_PATH", "tc")  # at creation: the layers keep the tensor-core weight copy
-    layers = [U.MoeLayer(cfg.desc(max_tokens=1), synthetic=cfg.synthetic(layer=l)) for l in range(3)]
-    stack = umsx.MoeStack(layers, max_tokens=1)
-    rng = np.random.default_rng(11)
-    for _ in range(2):
-        x = torch.from_numpy(rng.standard_normal((1, cfg.hidden)).astype(np.float32)).to(torch.bfloat16).cuda()
-        outs = []
-        for path in ("tc", "simt"):
-            monkeypatch.setenv("UMSX_DECODE_PATH", path)
-            outs.append(stack.forward(x).cpu().numpy())
-        stack.set_timing(True)
-        outs.append(stack.forward(x).cpu().numpy())
-        stack.set_timing(False)
-        for o in outs[1:]:
-            np.testing.assert_array_equal(bits(outs[0]), bits(o))
-    stack.close()
-    for l in layers:
-        l.close()

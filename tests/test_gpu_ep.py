@@ -1,7 +1,8 @@
 """Expert parallelism on two GPUs (NCCL): each rank holds half of the experts, runs their jobs
 (umsx_moe_forward_jobs), exchanges the job outputs and combines its tokens; the result must equal
 the single-GPU layer bit for bit, on the per-stage path (T = 5) and the tensor-core prefill path
-(T = 80).  Skipped on a box with fewer than two GPUs."""
+(T = 80), on the current stream and on a stream of the caller's own.  Skipped on a box with
+fewer than two GPUs."""
 import os
 import socket
 
@@ -44,7 +45,14 @@ def _worker(rank, world, port, tokens, q):
                             reserve_bytes=1 << 28)
         out, (t0, t1) = ep.ExpertParallelLayer(part).forward(x)
         torch.cuda.synchronize()
-        q.put((rank, np.array_equal(bits(out.cpu().numpy()), bits(want[t0:t1])), t0, t1))
+        ok = np.array_equal(bits(out.cpu().numpy()), bits(want[t0:t1]))
+        # the same on a stream of its own: every step of the layer is ordered on it
+        side = torch.cuda.Stream(device=rank)
+        side.wait_stream(torch.cuda.current_stream(rank))
+        out2, _ = ep.ExpertParallelLayer(part).forward(x, stream=side)
+        side.synchronize()
+        ok = ok and np.array_equal(bits(out2.cpu().numpy()), bits(want[t0:t1]))
+        q.put((rank, ok, t0, t1))
         part.close()
         full.close()
         dist.destroy_process_group()

@@ -104,14 +104,6 @@ struct umsx_moe {
 
 namespace {
 
-// The tensor-core decode kernel reads a second copy of the MXFP4 codes (Matrix::tc_codes, as
-// large as the codes themselves); it is made only when UMSX_DECODE_PATH asks for that kernel
-// ("tc" or "tc-auto") at the time the layer is created.
-bool tc_copy_wanted() {
-    const char *v = std::getenv("UMSX_DECODE_PATH");
-    return v && (!std::strcmp(v, "tc") || !std::strcmp(v, "tc-auto"));
-}
-
 umsx_status validate_desc(const umsx_moe_desc *d) {
     if (!d) return fail(UMSX_EINVAL, "null descriptor");
     if (d->hidden <= 0 || d->hidden % 64 || d->intermediate <= 0 || d->intermediate % 64)
@@ -140,7 +132,6 @@ size_t weight_bytes(const umsx_moe *m, Arena &a) {
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
         mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
-        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 && tc_copy_wanted() ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
     };
     Matrix tmp;
     if (d.fused_gate_up) mat(tmp, 2 * I, H);
@@ -162,7 +153,6 @@ void carve_weights(umsx_moe *m, Arena &a) {
         mm.codes = a.take<uint8_t>(mm.code_bytes_per_expert() * EL);
         mm.scales = a.take<uint8_t>(mm.scale_bytes_per_expert() * EL);
         mm.emax = d.quant == UMSX_QUANT_MXFP4 ? a.take<uint8_t>((size_t)rows * EL) : nullptr;
-        mm.tc_codes = d.quant == UMSX_QUANT_MXFP4 && tc_copy_wanted() ? a.take<uint8_t>(mm.tc_bytes_per_expert() * EL) : nullptr;
     };
     if (d.fused_gate_up) mat(m->gate_up, 2 * I, H);
     else { mat(m->gate, I, H); mat(m->up, I, H); }
@@ -493,16 +483,11 @@ DecodeLayer decode_layer(const umsx_moe *m) {
     L.dn_codes = m->down.codes;
     L.dn_scales = m->down.scales;
     L.dn_bias = m->down_bias;
-    L.gu_tc = m->gate_up.tc_codes;
-    L.dn_tc = m->down.tc_codes;
     return L;
 }
 
 // Layer l of the persistent kernel's stack.
-void set_decode_layer(DecodeParams &p, int l, const umsx_moe *m) {
-    p.layer[l] = decode_layer(m);
-    p.tc_ready = (l == 0 || p.tc_ready) && p.layer[l].gu_tc && p.layer[l].dn_tc;
-}
+void set_decode_layer(DecodeParams &p, int l, const umsx_moe *m) { p.layer[l] = decode_layer(m); }
 
 DecodeParams decode_params(const umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out) {
     const auto &d = m->d;
@@ -530,34 +515,15 @@ DecodeParams decode_params(const umsx_moe *m, Workspace &ws, const void *x, int 
     p.act_rec = ws.act_rec;
     p.act_sc = ws.act_sc;
     p.act_done = ws.act_done;
-    p.act_q8 = reinterpret_cast<int8_t *>(ws.act_codes);
-    p.act_q8_sc = ws.act_scales;
     p.bar = ws.bar;
     p.err = ws.disp.err;
+    p.fault_cta = -1;
     return p;
 }
 
-// UMSX_DECODE_PATH picks the persistent kernel of one-token calls: "tc" requires the
-// tensor-core kernel (a call it cannot serve fails with UMSX_EUNSUPPORTED), "tc-auto" prefers
-// it and falls back; unset or anything else keeps the SIMT kernel.  Both give the same bits.
-int decode_path() {
-    const char *v = std::getenv("UMSX_DECODE_PATH");
-    if (!v) return 1;
-    if (!std::strcmp(v, "tc")) return 2;
-    if (!std::strcmp(v, "tc-auto")) return 0;
-    return 1;
-}
-
 // Launches a persistent kernel: 1 launched; 0 this device cannot hold it resident (the caller
-// then takes the per-stage path); -1 the required tensor-core kernel could not be launched.
+// then takes the per-stage path).
 int try_decode(const DecodeParams &p, cudaStream_t s) {
-    const int path = decode_path();
-    if (path != 1 && p.tc_ready && launch_decode_tc(p, s) > 0) {
-        g_launches += 1;
-        return 1;
-    }
-    (void)cudaGetLastError();
-    if (path == 2) return -1;
     if (launch_decode(p, s) < 0) {
         (void)cudaGetLastError();
         return 0;
@@ -566,7 +532,9 @@ int try_decode(const DecodeParams &p, cudaStream_t s) {
     return 1;
 }
 
-// Reads and clears the device error flag after a synchronised call.
+// Reads and clears the device status word after the stream's work: a bounded wait that gave up
+// (UMSX_ETIMEOUT) outranks a non-finite result (UMSX_ENONFINITE, the reference's rejection of
+// non-finite combined outputs, tools/engine/expert_dispatch.cpp:14-18, :84-85).
 umsx_status check_device_flag(Workspace &ws, cudaStream_t s) {
     uint32_t flag = 0;
     UMSX_CUDA(cudaMemcpyAsync(&flag, ws.disp.err, 4, cudaMemcpyDeviceToHost, s));
@@ -574,7 +542,9 @@ umsx_status check_device_flag(Workspace &ws, cudaStream_t s) {
     if (!flag) return UMSX_OK;
     UMSX_CUDA(cudaMemsetAsync(ws.disp.err, 0, 4, s));
     UMSX_CUDA(cudaStreamSynchronize(s));
-    return fail(UMSX_ETIMEOUT, "a bounded device wait gave up (flag " + std::to_string(flag) + ")");
+    if (flag & ~kErrNonFinite)
+        return fail(UMSX_ETIMEOUT, "a bounded device wait gave up (flag " + std::to_string(flag) + ")");
+    return fail(UMSX_ENONFINITE, "a combined expert output is not finite");
 }
 
 // One layer, out = MoE(x): the persistent kernel for small T, else the per-stage kernels.
@@ -678,7 +648,7 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
         UMSX_LAUNCHED(launch_prefill_scatter(ws.y, ws.inv, ws.disp.ids, m->e_lo, m->e_local, tokens, K, H, y_jobs, s));
         return UMSX_OK;
     }
-    UMSX_LAUNCHED(launch_prefill_combine(ws.y, ws.disp.weights, ws.inv, tokens, K, H, residual, out, s));
+    UMSX_LAUNCHED(launch_prefill_combine(ws.y, ws.disp.weights, ws.inv, tokens, K, H, residual, out, ws.disp.err, s));
     if (ev) if (umsx_status st = mark(ev[4], s)) return st;
     return UMSX_OK;
 }
@@ -748,7 +718,7 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     if (y_jobs) return UMSX_OK;
     if (ev) {  // timed stages keep the combine a kernel of its own so that every stage has a boundary
         if (umsx_status st = mark(ev[3], s)) return st;
-        UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, s));
+        UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, ws.disp.err, s));
         if (umsx_status st = mark(ev[4], s)) return st;
     }
     return UMSX_OK;
@@ -759,9 +729,7 @@ umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, f
         DecodeParams p = decode_params(m, m->ws, x, x_dtype, tokens, out);
         p.ids_out = m->ws.disp.ids;
         p.w_out = m->ws.disp.weights;
-        const int r = try_decode(p, s);
-        if (r > 0) return UMSX_OK;
-        if (r < 0) return fail(UMSX_EUNSUPPORTED, "UMSX_DECODE_PATH=tc: the tensor-core decode kernel cannot serve this call");
+        if (try_decode(p, s) > 0) return UMSX_OK;
     }
     return run_layer(m, m->ws, x, x_dtype, tokens, out, nullptr, 0, 0.0f, s, nullptr);
 }
@@ -814,6 +782,13 @@ umsx_status umsx_moe_forward_host(umsx_moe *m, const void *x, int x_dtype, int t
     if (umsx_status st = forward_layer(m, m->ws.x_dev, x_dtype, tokens, m->ws.out_dev, s)) return st;
     UMSX_CUDA(cudaMemcpyAsync(out, m->ws.out_dev, out_bytes, cudaMemcpyDeviceToHost, s));
     return check_device_flag(m->ws, s);
+}
+
+umsx_status umsx_moe_status(umsx_moe *m, umsx_stream stream) {
+    if (!m) return fail(UMSX_EINVAL, "null handle");
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    return check_device_flag(m->ws, static_cast<cudaStream_t>(stream));
 }
 
 umsx_status umsx_route(umsx_moe *m, const void *x, int x_dtype, int tokens, int32_t *ids, float *weights,
@@ -917,7 +892,7 @@ umsx_status umsx_combine(const float *y, const float *weights, int tokens, int t
                          umsx_stream stream) {
     if (!y || !weights || !out || tokens <= 0 || top_k <= 0 || width <= 0 || width % 4)
         return fail(UMSX_EINVAL, "invalid combine arguments (width must be a multiple of 4)");
-    UMSX_LAUNCHED(launch_combine(y, weights, tokens, top_k, width, nullptr, out, static_cast<cudaStream_t>(stream)));
+    UMSX_LAUNCHED(launch_combine(y, weights, tokens, top_k, width, nullptr, out, nullptr, static_cast<cudaStream_t>(stream)));
     return UMSX_OK;
 }
 
@@ -960,6 +935,8 @@ struct umsx_stack {
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
     std::vector<cudaEvent_t> stage;  // 5 per layer while timing is on
     bool timing = false;
+    int fault_cta = -1;                   // one-shot fault injection (umsx_stack_inject_fault)
+    long long fault_wait_cycles = 0;
     struct Graph { int tokens, dtype; bool timing; cudaGraphExec_t exec; uint64_t kernels; };
     std::vector<Graph> graphs;
     std::mutex mu;
@@ -1026,12 +1003,14 @@ umsx_status stack_run(umsx_stack *st, const void *x, int dtype, int tokens, void
         p.rmsnorm = 1;
         p.residual = 1;
         p.eps = st->eps;
-        const int r = try_decode(p, caller);
-        if (r > 0) {
+        p.fault_cta = st->fault_cta;
+        p.wait_cycles = st->fault_wait_cycles;
+        st->fault_cta = -1;  // one forward only
+        st->fault_wait_cycles = 0;
+        if (try_decode(p, caller) > 0) {
             if (!dev_out) UMSX_CUDA(cudaMemcpyAsync(out, st->h, out_bytes, out_kind, caller));
             return UMSX_OK;
         }
-        if (r < 0) return fail(UMSX_EUNSUPPORTED, "UMSX_DECODE_PATH=tc: the tensor-core decode kernel cannot serve this call");
     }
     UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
     UMSX_CUDA(cudaStreamWaitEvent(st->stream, st->ev_in, 0));
@@ -1121,6 +1100,15 @@ umsx_status umsx_stack_forward_host(umsx_stack *st, const void *x, int x_dtype, 
     return check_device_flag(st->ws, s);
 }
 
+umsx_status umsx_stack_status(umsx_stack *st, umsx_stream stream) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    UMSX_CUDA(cudaStreamSynchronize(st->stream));  // graph replays run on the stack's own stream
+    return check_device_flag(st->ws, s);
+}
+
 umsx_status umsx_stack_set_timing(umsx_stack *st, int enable) {
     if (!st) return fail(UMSX_EINVAL, "null stack");
     std::lock_guard<std::mutex> lock(st->mu);
@@ -1130,6 +1118,16 @@ umsx_status umsx_stack_set_timing(umsx_stack *st, int enable) {
         st->stage.resize(5 * st->layers.size());
         for (auto &e : st->stage) UMSX_CUDA(cudaEventCreate(&e));
     }
+    return UMSX_OK;
+}
+
+umsx_status umsx_stack_inject_fault(umsx_stack *st, int cta, int64_t wait_limit_cycles) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    if (cta < 0 || wait_limit_cycles <= 0 || wait_limit_cycles > 4000000000LL)
+        return fail(UMSX_EINVAL, "need cta >= 0 and 0 < wait_limit_cycles <= 4e9");
+    std::lock_guard<std::mutex> lock(st->mu);
+    st->fault_cta = cta;
+    st->fault_wait_cycles = wait_limit_cycles;
     return UMSX_OK;
 }
 

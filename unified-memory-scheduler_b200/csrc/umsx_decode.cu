@@ -22,8 +22,12 @@
 // the single-CTA selection and the second wave of CTAs.
 //
 // Grid barriers are a monotonic counter with bounded spins: a CTA that waits
-// longer than kGridWaitCycles (or sees the error flag) sets `err` and returns,
-// so a fault elsewhere cannot keep the kernel alive.
+// longer than kGridWaitCycles (or sees another CTA's error bit) sets `err` and
+// returns, so a fault elsewhere cannot keep the kernel alive.  Tests shorten the
+// bound and withhold one CTA's first arrival (DecodeParams::fault_cta) to see the
+// waits run out.  One token (MT = 1) takes its slot list straight from the ranking
+// (k distinct experts: slot r = rank r with the one job r).  The final output is
+// checked for inf / NaN (kErrNonFinite).
 #include <stdint.h>
 
 #include "umsx_device.cuh"
@@ -59,29 +63,34 @@ __device__ __forceinline__ void grid_arrive(unsigned *bar) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
 
+// One thread waits until the counter reaches target; false if the wait ran out (it then sets bit 2
+// of err) or another CTA reported an error (any bit of err; a non-finite output is not an error).
+__device__ __forceinline__ bool grid_spin(unsigned *bar, unsigned target, uint32_t *err, long long limit) {
+    const long long t0 = clock64();
+    for (unsigned it = 0; ld_acquire_gpu(bar) < target; ++it) {
+        if ((it & 63u) == 63u) {
+            if (*reinterpret_cast<volatile uint32_t *>(err) & ~kErrNonFinite) return false;
+            if (clock64() - t0 > limit) { atomicOr(err, 2u); return false; }
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ long long wait_limit(const DecodeParams &p) { return p.wait_cycles > 0 ? p.wait_cycles : kGridWaitCycles; }
+
 // The waiting half: returns false (uniformly within the CTA) if the wait ran out or another
 // CTA reported an error.
-__device__ bool grid_wait(unsigned *bar, unsigned target, uint32_t *err, int *ok_s) {
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        const long long t0 = clock64();
-        for (unsigned it = 0; ld_acquire_gpu(bar) < target; ++it) {
-            if ((it & 63u) == 63u) {
-                if (*reinterpret_cast<volatile uint32_t *>(err)) { ok = 0; break; }
-                if (clock64() - t0 > kGridWaitCycles) { atomicOr(err, 2u); ok = 0; break; }
-            }
-        }
-        *ok_s = ok;
-    }
+__device__ bool grid_wait(const DecodeParams &p, unsigned target, int *ok_s) {
+    if (threadIdx.x == 0) *ok_s = grid_spin(p.bar, target, p.err, wait_limit(p));
     __syncthreads();
     return *ok_s != 0;
 }
 
 // All CTAs arrive, then wait.
-__device__ bool grid_sync(unsigned *bar, unsigned target, uint32_t *err, int *ok_s) {
+__device__ bool grid_sync(const DecodeParams &p, unsigned target, int *ok_s) {
     __syncthreads();
-    if (threadIdx.x == 0) grid_arrive(bar);
-    return grid_wait(bar, target, err, ok_s);
+    if (threadIdx.x == 0) grid_arrive(p.bar);
+    return grid_wait(p, target, ok_s);
 }
 
 struct DecSmem {
@@ -253,9 +262,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             // this CTA's logits are out: it arrives at the grid barrier now and quantizes x (a
             // CTA-local job) while the other CTAs finish
             group_bar(kLogitBar, n_lw * 32);
-            if (tid == 0) grid_arrive(p.bar);
+            if (tid == 0 && !(l == 0 && c == p.fault_cta)) grid_arrive(p.bar);
         } else {
-            if (n_lw == 0 && tid == 0) grid_arrive(p.bar);  // no logits here
+            if (n_lw == 0 && tid == 0 && !(l == 0 && c == p.fault_cta)) grid_arrive(p.bar);  // no logits here
             // Q8_0 records of the normalised rows (the gate_up activations), every CTA its own copy,
             // made by the warps that have no logit to compute
             for (int it = warp - n_lw; it < T * nb; it += kDecWarps - n_lw) {
@@ -272,7 +281,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             return;
         }
         target += nC;
-        if (!grid_wait(p.bar, target, p.err, &ok_s)) return;
+        if (!grid_wait(p, target, &ok_s)) return;
 
         // ---- S: selection and slots (every CTA) -----------------------------------
         if (warp < T) {
@@ -282,7 +291,21 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             if (lane < K) { sel_e[warp * K + lane] = sel; sel_w[warp * K + lane] = w; }
         }
         __syncthreads();
-        if (warp == 0) {
+        if (MT == 1 && warp == 0) {
+            // one token: its k picks are distinct experts, so slot r is rank r with the one job r
+            const bool has = lane < K;
+            int ej = has ? sel_e[lane] : 0;
+            if (has && (ej < 0 || ej >= E)) {  // cannot happen (selection always picks a valid expert); never index with it
+                atomicOr(p.err, 8u);
+                ej = 0;
+            }
+            if (has) { slot_e[lane] = ej; slot_cnt[lane] = 1; slot_first[lane] = lane; job_j[lane] = lane; }
+            if (lane == 0) n_slots_s = K;
+            if (c == 0 && l == p.n_layers - 1 && p.ids_out && has) {
+                p.ids_out[lane] = ej;
+                p.w_out[lane] = sel_w[lane];
+            }
+        } else if (warp == 0) {
             const bool has = lane < N;
             int ej = has ? sel_e[lane] : 0x7fffffff;
             if (has && (ej < 0 || ej >= E)) {  // cannot happen (selection always picks a valid expert); never index with it
@@ -314,8 +337,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
         __syncthreads();
         const int n_slots = n_slots_s;
         const int U1 = n_slots * G1, U2 = n_slots * G2;
-        const int u_lo = (int)((long long)c * U1 / nC), u_hi = (int)((long long)(c + 1) * U1 / nC);
-        const int v_lo = (int)((long long)c * U2 / nC), v_hi = (int)((long long)(c + 1) * U2 / nC);
+        const int u_lo = c * U1 / nC, u_hi = (c + 1) * U1 / nC;  // c * U1 < 2^31 at every supported shape
+        const int v_lo = c * U2 / nC, v_hi = (c + 1) * U2 / nC;
         // ---- G: gate_up units ------------------------------------------------------
         {
             const int gi = warp >> 2, wg = warp & 3, half = wg >> 1, lh = wg & 1, gt = tid & 127;
@@ -393,7 +416,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                     Ld.dn_scales + scale_offset(UMSX_QUANT_MXFP4, e, G2, g, nbI), nbI, lh0, my_ring);
             mx_ring_prime<S>(ws, lane);
         }
-        if (!grid_wait(p.bar, target, p.err, &ok_s)) {
+        if (!grid_wait(p, target, &ok_s)) {
             cp_async_wait<0>();  // the primed copies land before the CTA leaves
             return;
         }
@@ -460,16 +483,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             }
         }
         target += nC;
-        if (!grid_sync(p.bar, target, p.err, &ok_s)) return;
+        if (!grid_sync(p, target, &ok_s)) return;
     }
-    // final fold: each CTA writes its share of the output rows
+    // final fold: each CTA writes its share of the output rows, and records a non-finite value (checking
+    // the last layer suffices: an inf or NaN in h turns the next layer's RMSNorm, and so its output, NaN)
     const int total4 = T * H4;
     const int lo = (int)((long long)c * total4 / nC), hi = (int)((long long)(c + 1) * total4 / nC);
     const float4 *y4 = reinterpret_cast<const float4 *>(p.y);
     for (int i = lo + tid; i < hi; i += kDecThreads) {
         const int t = i / H4;
-        reinterpret_cast<float4 *>(p.out)[i] =
-            fold4(y4, sel_w, t, K, H4, i - t * H4, reinterpret_cast<const float4 *>(sm.hs)[i], p.residual);
+        const float4 v = fold4(y4, sel_w, t, K, H4, i - t * H4, reinterpret_cast<const float4 *>(sm.hs)[i], p.residual);
+        flag_nonfinite4(v, p.err);
+        reinterpret_cast<float4 *>(p.out)[i] = v;
     }
 }
 

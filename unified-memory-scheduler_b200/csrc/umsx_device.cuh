@@ -93,6 +93,18 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, den), u);
 }
 
+// Records a non-finite combined output in the status word (the reference rejects those,
+// tools/engine/expert_dispatch.cpp:84-85); a no-op for finite values or a null word.
+__device__ __forceinline__ void flag_nonfinite(float v, uint32_t *err) {
+    if ((__float_as_uint(v) & 0x7f800000u) == 0x7f800000u && err) atomicOr(err, 16u);
+}
+__device__ __forceinline__ void flag_nonfinite4(float4 v, uint32_t *err) {
+    flag_nonfinite(v.x, err);
+    flag_nonfinite(v.y, err);
+    flag_nonfinite(v.z, err);
+    flag_nonfinite(v.w, err);
+}
+
 // ---- warp reductions --------------------------------------------------------
 
 // The oracle's tree32: v[c] = v[c] + v[c^s] for s = 16..1 (fp add is commutative,

@@ -159,6 +159,13 @@ std::string parse_gguf(const std::string &path, GgufFile &f) {
             if (!r.get(ne) || ne == 0 || ne > (1ull << 40)) return "invalid GGUF tensor shape: " + name;
             t.ne[d] = (int64_t)ne;
         }
+        // every size below is a product of these extents: bound the element count so that no
+        // product (nor its byte count) can overflow
+        int64_t count = 1;
+        for (int d = 0; d < 4; ++d) {
+            if (t.ne[d] > ((int64_t)1 << 56) / count) return "invalid GGUF tensor shape (element count overflows): " + name;
+            count *= t.ne[d];
+        }
         uint32_t type;
         if (!r.get(type) || !r.get(t.offset)) return "GGUF tensor info could not be read: " + path;
         t.type = (int)type;

@@ -30,11 +30,6 @@ struct Matrix {
     uint8_t *codes = nullptr;   // code plane, all local experts
     uint8_t *scales = nullptr;  // exponent / fp16-scale plane
     uint8_t *emax = nullptr;    // MXFP4: largest block exponent of every row [experts][rows] (prefill rebase)
-    // MXFP4 tensor-core copy, pre-swizzled operand tiles: [experts][K stage][row group of 16][8-row half]
-    // [block pair q][8 rows][32 B]; a K stage = 4 block pairs (256 values, e2m1, element 2i in the low
-    // nibble); 16-byte chunk c of row r8 at c ^ ((r8 >> 2) & 1) (the 32-byte swizzle); the last stage
-    // is zero-padded
-    uint8_t *tc_codes = nullptr;
     int rows = 0;               // N per expert
     int cols = 0;               // K
     int quant = 0;
@@ -43,8 +38,6 @@ struct Matrix {
         if (quant == UMSX_QUANT_MXFP4) return (size_t)(rows / 16) * (((cols / 64) + 3) / 4) * 128;
         return (size_t)rows * (cols / 32) * 2;
     }
-    __host__ __device__ int tc_stages() const { return (cols + 255) / 256; }
-    __host__ __device__ size_t tc_bytes_per_expert() const { return (size_t)rows * tc_stages() * 128; }
 };
 
 // Routing/dispatch state that the router writes and the expert kernels read.
@@ -66,8 +59,12 @@ struct Dispatch {
     uint32_t *tile_done; // [T][H/32] combine arrival counters, zero between launches
     uint8_t *xr;         // [T][H/32][64] x as MXFP4 staging records (MXFP4 layers)
     float *xr_sc;        // [T][pad4(H/32)] their scales
-    uint32_t *err;       // [1] set by a kernel whose bounded wait timed out (never cleared by kernels)
+    uint32_t *err;       // [1] status bits set by kernels (never cleared by kernels): kErr*
 };
+
+// Bits of the device status word (Dispatch::err, DecodeParams::err).  The synchronous entry points
+// turn kErrNonFinite into UMSX_ENONFINITE and every other bit into UMSX_ETIMEOUT.
+constexpr uint32_t kErrNonFinite = 16u;  // a combined output (a layer's result) was inf or NaN
 
 struct RouterParams {
     const void *x;
@@ -138,8 +135,6 @@ struct DecodeLayer {
     const uint8_t *dn_codes;  // down planes [E][H][I]
     const uint8_t *dn_scales;
     const float *dn_bias;     // [E][H] or null
-    const uint8_t *gu_tc;     // tensor-core copies (Matrix::tc_codes) or null
-    const uint8_t *dn_tc;
 };
 
 struct DecodeParams {
@@ -163,19 +158,16 @@ struct DecodeParams {
     float *act_sc;     // [T*K][pad4(I/32)]
     uint32_t *act_done;  // [T*K][I/32] arrival counters (zeroed by the launcher)
     unsigned *bar;     // grid barrier counter (zeroed by the launcher)
-    uint32_t *err;     // set when a grid barrier wait ran out
-    // tensor-core variant (one token): plain Q8_0 activation codes and scales
-    int8_t *act_q8;    // [T*K][I]
-    float *act_q8_sc;  // [T*K][I/32]
-    int tc_ready;      // every layer has its tensor-core copies
+    uint32_t *err;     // status bits (kErr*): a grid barrier wait ran out, a non-finite output
+    // fault injection for tests: CTA fault_cta withholds its first grid-barrier arrival (-1: none), so
+    // every wait of that barrier runs out after wait_cycles (0: the default bound) and reports it
+    int fault_cta;
+    long long wait_cycles;
 };
 
 bool decode_supported(int tokens, int hidden, int inter, int experts, int top_k, int n_layers);
 // Returns 1 (kernels launched) or -1 if this device cannot hold the kernel resident on every SM.
 int launch_decode(const DecodeParams &p, cudaStream_t s);
-// The tensor-core variant for one token (gu_tc / dn_tc / act_q8 set); same contract and bits.
-bool decode_tc_supported(int tokens, int hidden, int inter, int experts, int top_k);
-int launch_decode_tc(const DecodeParams &p, cudaStream_t s);
 
 // Prefill grouped GEMM (umsx_prefill.cu): tcgen05 kind::f16 over the experts' job segments.
 constexpr int kPrefillMinTokens = 65;  // from this many tokens an MXFP4 layer takes the tensor-core path
@@ -209,7 +201,7 @@ int launch_prefill_pack(const Dispatch &d, int jobs, const int32_t *n_jobs, int 
 int launch_prefill_scatter(const float *yj, const int32_t *inv, const int32_t *ids, int e_lo, int e_local, int tokens,
                            int K, int width, float *y, cudaStream_t s);
 int launch_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
-                           const float *residual, float *out, cudaStream_t s);
+                           const float *residual, float *out, uint32_t *err, cudaStream_t s);
 int launch_moe_gemm(const MoeGemmParams &p, const void *act_hi, const void *act_lo, int rows_total, cudaStream_t s);
 
 // Thread-local status channel shared by every translation unit (umsx_api.cu).
@@ -223,8 +215,9 @@ int launch_dispatch(const Dispatch &d, int entries, int top_k, int e_lo, int e_l
 int launch_gate_up(const GateUpParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
 int launch_gemv(const GemvParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
 
+// err: status word that records a non-finite output (kErrNonFinite), or null
 int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *residual, float *out,
-                   cudaStream_t s);
+                   uint32_t *err, cudaStream_t s);
 int launch_repack(const Matrix &m, int expert, const uint8_t *ggml, cudaStream_t s);
 int launch_export(const Matrix &m, int expert, uint8_t *ggml, cudaStream_t s);
 int launch_gen_blocks(int quant, uint64_t seed, uint64_t stream, uint64_t first_block, uint64_t nblocks,

@@ -750,6 +750,7 @@ __global__ void __launch_bounds__(W * 32) k_gemv(GemvParams p, GemvSrc src, Disp
                         acc = __fadd_rn(acc, __fmul_rn(__ldcg(p.route_w + (size_t)tok * K + r),
                                                        __ldcg(p.out + ((size_t)tok * K + r) * N + n0 + i)));
                     if (p.residual) acc = __fadd_rn(p.residual[(size_t)tok * N + n0 + i], acc);
+                    flag_nonfinite(acc, d.err);
                     p.combine_out[(size_t)tok * N + n0 + i] = acc;
                 }
                 if (threadIdx.x == 0) p.tile_done[(size_t)tok * gridDim.x + blockIdx.x] = 0;
@@ -1050,6 +1051,7 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
                         acc2 = __fadd_rn(acc2, __fmul_rn(__ldcg(p.route_w + (size_t)tok * K + rr),
                                                          __ldcg(p.out + ((size_t)tok * K + rr) * N + n0 + i)));
                     if (p.residual) acc2 = __fadd_rn(p.residual[(size_t)tok * N + n0 + i], acc2);
+                    flag_nonfinite(acc2, d.err);
                     p.combine_out[(size_t)tok * N + n0 + i] = acc2;
                 }
                 if (threadIdx.x == 0) p.tile_done[(size_t)tok * gridDim.x + blockIdx.x] = 0;
@@ -1063,7 +1065,7 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
 // ============================================================================
 
 __global__ void k_combine(const float *__restrict__ y, const float *__restrict__ w, int tokens, int K, int width,
-                          const float *residual, float *out) {
+                          const float *residual, float *out, uint32_t *err) {
     const int v4 = width / 4;
     const size_t total = (size_t)tokens * v4;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -1084,6 +1086,7 @@ __global__ void k_combine(const float *__restrict__ y, const float *__restrict__
             acc.z = __fadd_rn(r.z, acc.z);
             acc.w = __fadd_rn(r.w, acc.w);
         }
+        flag_nonfinite4(acc, err);
         reinterpret_cast<float4 *>(out + t * width)[c] = acc;
     }
 }
@@ -1108,19 +1111,6 @@ __global__ void k_layout(Matrix m, int expert, uint8_t *ggml) {
             uint8_t *chunk = m.codes + (((size_t)expert * nrg + rg) * np + bp) * 512;
             uint8_t *ex = m.scales + (((size_t)expert * nrg + rg) * nq + (bp >> 2)) * 128 + L * 4 + (bp & 3);
             if (TO_TILE) *ex = blk[0]; else blk[0] = *ex;
-            if (TO_TILE && m.tc_codes) {
-                // tensor-core copy: consecutive elements packed low nibble first; block b is one 16-byte
-                // chunk of its row's 32-byte block-pair slice, placed in the 32-byte-swizzled operand tile
-                const int nst = m.tc_stages(), st = b >> 3, q = (b & 7) >> 1, g = row >> 4, r8 = row & 7;
-                uint8_t *dst = m.tc_codes + (((size_t)expert * nst + st) * (size_t)(m.rows / 16) + g) * 2048 +
-                               ((row >> 3) & 1) * 1024 + q * 256 + r8 * 32 + (((b & 1) ^ ((r8 >> 2) & 1)) << 4);
-                for (int i = 0; i < 16; ++i) {
-                    const int j0 = 2 * i, j1 = 2 * i + 1;
-                    const uint32_t c0 = j0 < 16 ? (blk[1 + j0] & 15u) : (blk[1 + j0 - 16] >> 4);
-                    const uint32_t c1 = j1 < 16 ? (blk[1 + j1] & 15u) : (blk[1 + j1 - 16] >> 4);
-                    dst[i] = (uint8_t)(c0 | (c1 << 4));
-                }
-            }
             for (int lh = 0; lh < 2; ++lh) {
                 uint32_t *words = reinterpret_cast<uint32_t *>(chunk + lh * 256 + L * 8);
                 for (int w = 0; w < 2; ++w) {
@@ -1362,16 +1352,15 @@ int launch_gemv(const GemvParams &p, const Dispatch &d, int slots, int max_per_e
 }
 
 int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *residual, float *out,
+                   uint32_t *err,
                    cudaStream_t s) {
     const size_t n = (size_t)tokens * (width / 4);
-    k_combine<<<grid_for(n, 256), 256, 0, s>>>(y, w, tokens, top_k, width, residual, out);
+    k_combine<<<grid_for(n, 256), 256, 0, s>>>(y, w, tokens, top_k, width, residual, out, err);
     return 1;
 }
 
 int launch_repack(const Matrix &m, int expert, const uint8_t *ggml, cudaStream_t s) {
     const size_t n = (size_t)m.rows * (m.cols / 32);
-    if (m.tc_codes)  // zero the padding of the last stage (an error surfaces as the launch error)
-        (void)cudaMemsetAsync(m.tc_codes + (size_t)expert * m.tc_bytes_per_expert(), 0, m.tc_bytes_per_expert(), s);
     k_layout<true><<<grid_for(n, 256), 256, 0, s>>>(m, expert, const_cast<uint8_t *>(ggml));
     return 1;
 }

@@ -84,11 +84,16 @@ class ExpertParallelLayer:
     def forward(self, x: torch.Tensor, y: torch.Tensor | None = None, stream=None):
         """x [T, H] on this rank's GPU, the same rows on every rank; y: optional [T, k, H] f32
         scratch for the job outputs (reused across calls: only this rank's rows are read).
+        stream: a torch.cuda.Stream (or None for the current stream); every step of the layer --
+        the expert kernels, the host read of the routing, the torch index copies, the all-to-all
+        and the combine -- is ordered on it, so x must be ready on it and the result is ready on it.
         Returns (out [t1 - t0, H] f32 for this rank's tokens, (t0, t1))."""
         from .umsx import combine
-        y, ids, w = self.layer.forward_jobs(x, y=y, stream=stream)
-        mine, (t0, t1) = exchange(y, ids, self.layer.desc.experts, self.group)
-        if t1 == t0:  # fewer tokens than ranks: nothing to combine here
-            return torch.empty((0, self.layer.desc.hidden), dtype=torch.float32, device=x.device), (t0, t1)
-        out = combine(mine, w[t0:t1].contiguous(), stream=stream)
+        s = stream if stream is not None else torch.cuda.current_stream(x.device)
+        with torch.cuda.stream(s):
+            y, ids, w = self.layer.forward_jobs(x, y=y, stream=s)
+            mine, (t0, t1) = exchange(y, ids, self.layer.desc.experts, self.group)
+            if t1 == t0:  # fewer tokens than ranks: nothing to combine here
+                return torch.empty((0, self.layer.desc.hidden), dtype=torch.float32, device=x.device), (t0, t1)
+            out = combine(mine, w[t0:t1].contiguous(), stream=s)
         return out, (t0, t1)

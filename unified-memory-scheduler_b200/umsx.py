@@ -31,10 +31,11 @@ BLOCK_BYTES = {QUANT_Q8_0: 34, QUANT_MXFP4: 17}
 
 # exported symbols of include/umsx.h (the tests check each one is present)
 EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "umsx_moe_forward",
-           "umsx_moe_forward_host", "umsx_moe_forward_jobs", "umsx_route", "umsx_expert_down_q8", "umsx_mul_mat_id",
+           "umsx_moe_forward_host", "umsx_moe_forward_jobs", "umsx_moe_status", "umsx_route", "umsx_expert_down_q8", "umsx_mul_mat_id",
            "umsx_combine",
            "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_destroy", "umsx_stack_forward",
-           "umsx_stack_forward_host", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_route_static",
+           "umsx_stack_forward_host", "umsx_stack_status", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_stack_inject_fault",
+           "umsx_route_static",
            "umsx_gguf_load_experts", "umsx_gguf_experts_free", "umsx_moe_create_gguf",
            "umsx_kernel_launches", "umsx_last_error", "umsx_version"]
 
@@ -84,6 +85,8 @@ def lib():
         "umsx_moe_forward": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "umsx_moe_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
         "umsx_moe_forward_jobs": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
+        "umsx_moe_status": (i32, [vp, vp]),
+        "umsx_stack_status": (i32, [vp, vp]),
         "umsx_route": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "umsx_expert_down_q8": (i32, [vp, vp, vp, i32, vp, vp]),
         "umsx_mul_mat_id": (i32, [vp, i32, vp, i32, vp, i32, i32, vp, vp]),
@@ -95,6 +98,7 @@ def lib():
         "umsx_stack_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
         "umsx_stack_set_timing": (i32, [vp, i32]),
         "umsx_stack_stage_times": (i32, [vp, C.POINTER(C.c_float), i32]),
+        "umsx_stack_inject_fault": (i32, [vp, i32, C.c_int64]),
         "umsx_route_static": (i32, [vp, i32, i32, vp, vp, i32, i32, i32, i32, C.c_float, vp, vp, vp, vp]),
         "umsx_gguf_load_experts": (i32, [C.c_char_p, i32, vp, i32, i32, C.POINTER(GgufExpertsC)]),
         "umsx_gguf_experts_free": (None, [C.POINTER(GgufExpertsC)]),
@@ -266,6 +270,11 @@ class MoeLayer:
                                           _stream(stream)))
         return out_host
 
+    def status(self, stream=None):
+        """Raises UmsxError (ENONFINITE / ETIMEOUT) for what the handle's earlier calls on the stream
+        recorded on the device; clears the record (umsx_moe_status)."""
+        check(lib().umsx_moe_status(self._h, _stream(stream)))
+
     def route(self, x, stream=None):
         import torch
         T, K, E = x.shape[0], self.desc.top_k, self.desc.experts
@@ -340,8 +349,17 @@ class MoeStack:
                                             _ptr(out_host), _stream(stream)))
         return out_host
 
+    def status(self, stream=None):
+        """umsx_stack_status: raises for a non-finite layer output or a wait that gave up."""
+        check(lib().umsx_stack_status(self._h, _stream(stream)))
+
     def set_timing(self, enable: bool = True):
         check(lib().umsx_stack_set_timing(self._h, int(enable)))
+
+    def inject_fault(self, cta: int = 0, wait_limit_cycles: int = 2_000_000):
+        """Test hook (umsx_stack_inject_fault): the next one-launch forward loses CTA `cta`'s first
+        grid-barrier arrival, its bounded waits run out and the call reports ETIMEOUT."""
+        check(lib().umsx_stack_inject_fault(self._h, int(cta), int(wait_limit_cycles)))
 
     def stage_times(self) -> dict:
         ms = (C.c_float * 4)()
