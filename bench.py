@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--ref-seconds", type=float, default=150.0, help="timed budget of the --impl reference arm")
     ap.add_argument("--no-prefill", action="store_true", help="decode line without the prefill sub-record")
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the ranks (prefill)")
+    ap.add_argument("--config", choices=("stack", "skew"), default="stack",
+                    help="stack: configs[2] (the headline); skew: configs[3] load-skew layers at T=4096")
     a = ap.parse_args()
     if a.tokens is None:
         a.tokens = 1 if a.mode == "decode" else 4096
@@ -532,6 +534,62 @@ def prefill_record(pkg, cfg, layers, dev, a, tokens: int = 4096, steps: int = 5,
             "clocks": clk.summary(), "l2": "inputs larger than L2 (61 GB of weights, 4096 x 2880 activations)"}
 
 
+def skew_arm(a):
+    """Qwen3-30B-A3B layer shapes in Q8_0 and MXFP4 with the Zipf(1.2) router bias, T = 4096
+    tokens per step on one GPU: tokens/s, p50 / p99 layer latency over the steps (CUDA events per step,
+    inputs from a pool of 8 seeded batches), per-expert load and the per-GPU load an expert-parallel
+    split over G = 2 / 4 / 8 GPUs would see (contiguous expert blocks): max / mean jobs per GPU."""
+    import numpy as np
+    import torch
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    pkg = load_pkg()
+    T = a.tokens if a.tokens != 1 else 4096
+    out_rec = {}
+    for name in ("qwen3-skew-q8_0", "qwen3-skew-mxfp4"):
+        cfg = pkg.configs.CONFIGS[name]
+        layer = pkg.MoeLayer(cfg.desc(max_tokens=T), synthetic=cfg.synthetic(), device=0)
+        from oracle.oracle import Oracle  # the host twin of the device router weights (generator only)
+        orc = Oracle()
+        rw = orc.gen_normal_f32(cfg.seed, pkg.configs.stream_id(0, pkg.configs.KIND_ROUTER_W), 0,
+                                cfg.experts * cfg.hidden, cfg.router_sigma).reshape(cfg.experts, cfg.hidden)
+        layer.set_router(rw, pkg.configs.zipf_router_bias(cfg.experts, seed=cfg.seed))
+        rng = np.random.default_rng(3000)
+        xs = [torch.from_numpy(rng.standard_normal((T, cfg.hidden)).astype(np.float32)).to(torch.bfloat16).to(dev)
+              for _ in range(8)]
+        out = torch.empty((T, cfg.hidden), dtype=torch.float32, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        for i in range(a.warmup):
+            layer.forward(xs[i % 8], out)
+        torch.cuda.synchronize()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + 1)]
+        with Clocks(0) as clk:
+            evs[0].record(stream)
+            for i in range(a.steps):
+                layer.forward(xs[i % 8], out)
+                evs[i + 1].record(stream)
+            torch.cuda.synchronize()
+        ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(a.steps)]
+        _, _, counts = layer.route(xs[0])
+        c = counts.cpu().numpy().astype(np.int64)
+        per_gpu = {f"G{G}": {"jobs": c.reshape(G, -1).sum(1).tolist(),
+                             "max_over_mean": float(c.reshape(G, -1).sum(1).max() / c.reshape(G, -1).sum(1).mean())}
+                   for G in (2, 4, 8)}
+        out_rec[name] = {"tokens_per_s": T * a.steps / (sum(ms) / 1e3), "layer_ms_p50": float(np.percentile(ms, 50)),
+                         "layer_ms_p99": float(np.percentile(ms, 99)), "layer_ms_mean": float(np.mean(ms)),
+                         "expert_load_max_over_mean": float(c.max() / c.mean()), "experts_unused": int((c == 0).sum()),
+                         "ep_partition": per_gpu, "clocks": clk.summary()}
+        layer.close()
+    res = {"metric": f"MoE-layer tokens/s, configs[3] load skew (Qwen3-30B-A3B shapes, Zipf 1.2 router bias), T={T}",
+           "value": out_rec["qwen3-skew-q8_0"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+           "warmup": a.warmup, "higher_is_better": True, "data": "synthetic",
+           "config": {"workload": "qwen3-30b-a3b skew layer (Q8_0 headline value; MXFP4 in the sub-record)",
+                      "tokens": T, "experts": 128, "top_k": 8, "hidden": 2048, "ffn": 768},
+           "skew": out_rec}
+    print(json.dumps(res))
+
+
 def ep_arm(a):
     """Expert-parallel prefill: every layer's experts split over the ranks (see the module docstring)."""
     import datetime
@@ -681,7 +739,9 @@ def reference_arm(a):
 
 def main():
     a = parse()
-    if a.impl == "reference":
+    if a.config == "skew":
+        skew_arm(a)
+    elif a.impl == "reference":
         reference_arm(a)
     elif a.ep:
         ep_arm(a)

@@ -104,6 +104,12 @@ umsx_status umsx_moe_create_synthetic(const umsx_moe_desc *desc, uint64_t seed, 
 
 void umsx_moe_destroy(umsx_moe *moe);
 
+/* Replaces the router of a resident layer from HOST buffers (router_w [E][H] fp32, router_b [E] fp32,
+ * given exactly when desc.has_router_bias); synchronous.  The expert tensors stay as they are.  Used
+ * for the load-skew configuration, whose router bias follows a Zipf law over the experts (no
+ * counterpart in the reference, which loads its router with the model). */
+umsx_status umsx_moe_set_router(umsx_moe *moe, const float *router_w, const float *router_b);
+
 /* Whole layer, device buffers: out[T][H] = sum_r w[t,r] * expert(ids[t,r], x[t]) in rank order.
  * Replaces build_moe_ffn's expert branch + rank sum (hybrid patch :1394-1683, :1911-1916).
  * x is [T][H] fp32 or bf16 (x_dtype).  Optional ids/weights outputs may be NULL. */
@@ -181,6 +187,15 @@ umsx_status umsx_moe_export_expert(umsx_moe *moe, int proj, int expert, void *ho
  * llama.cpp graph the hybrid patch modifies (llama-b11669-hybrid-experts.patch:1355-1930). */
 typedef struct umsx_stack umsx_stack;
 umsx_status umsx_stack_create(umsx_moe *const *layers, int n_layers, int max_tokens, float rms_eps, umsx_stack **out);
+/* A stack whose layers may differ in shape (same width and device), each optionally with shared
+ * experts: shared[l] (NULL for none) is a one-expert top-1 handle holding the always-on shared FFN
+ * (the reference graph's ffn_{gate,up,down}_shexp, several shared experts as one FFN of their summed
+ * width), and layer l becomes h <- h + ((sum_r w_r y_r) + y_shared): the shared FFN's output is the
+ * term after the k routed ones in the same rank-order combine, as the graph's ggml_add of the shared
+ * branch to the routed sum.  A dense FFN (DeepSeek's layer 0) is a one-expert top-1 layer (its
+ * softmax over one logit is exactly 1.0).  Such stacks run the per-stage kernels (graph replay). */
+umsx_status umsx_stack_create_mixed(umsx_moe *const *layers, umsx_moe *const *shared, int n_layers, int max_tokens,
+                                    float rms_eps, umsx_stack **out);
 void umsx_stack_destroy(umsx_stack *stack);
 /* x [T][H] (device, fp32 or bf16) -> out [T][H] fp32 final hidden state. */
 umsx_status umsx_stack_forward(umsx_stack *stack, const void *x, int x_dtype, int tokens, float *out, umsx_stream stream);

@@ -130,10 +130,7 @@ def selected_host_weights(orc, cfg, layer: int, experts) -> LayerWeights:
         out = np.zeros((E, rows, cols // 32 * bb), np.uint8)
         per = rows * (cols // 32)
         for e in sorted({int(v) for v in np.asarray(experts).reshape(-1)}):
-            if cfg.quant == U.QUANT_MXFP4:
-                out[e] = orc.gen_mxfp4(s, sid(layer, kind), e * per, per, 119, 5).reshape(rows, -1)
-            else:
-                out[e] = orc.gen_q8_0(s, sid(layer, kind), e * per, per).reshape(rows, -1)
+            orc.gen_blocks_into(cfg.quant, out[e], s, sid(layer, kind), e * per, per, threads=8)
         return out
 
     router_w = orc.gen_normal_f32(s, sid(layer, C.KIND_ROUTER_W), 0, E * H, cfg.router_sigma).reshape(E, H)
@@ -162,4 +159,26 @@ def oracle_stack(orc, cfg, xb: np.ndarray, n_layers: int, threads: int = 16, eps
         ids, _, _ = orc.route(desc, router, xn)
         w = selected_host_weights(orc, cfg, l, ids)
         h = (h + orc.moe_layer(desc, w, xn, threads=threads)["out"]).astype(np.float32)
+    return h
+
+
+def oracle_mixed_stack(orc, xb: np.ndarray, n_layers: int, threads: int = 16, eps: float = 1e-5,
+                       first: int = 0) -> np.ndarray:
+    """configs[4] block on the oracle: layer 0 the dense FFN, then h <- h + ((routed) + (shared FFN))
+    per layer (the graph's ggml_add of the shared branch to the routed sum, then the residual);
+    layers first .. first + n_layers - 1."""
+    h = bf16_bits_to_f32(xb).copy()
+    for l in range(first, first + n_layers):
+        xn = orc.rmsnorm(h, eps)
+        if l == 0:
+            d = C.DEEPSEEK_V2_LITE_DENSE
+            out = orc.moe_layer(oracle_desc(d), selected_host_weights(orc, d, 0, [0]), xn, threads=threads)["out"]
+        else:
+            r, sh = C.DEEPSEEK_V2_LITE, C.DEEPSEEK_V2_LITE_SHARED
+            dr = oracle_desc(r)
+            ids, _, _ = orc.route(dr, selected_host_weights(orc, r, l, []), xn)
+            routed = orc.moe_layer(dr, selected_host_weights(orc, r, l, ids), xn, threads=threads)["out"]
+            shared = orc.moe_layer(oracle_desc(sh), selected_host_weights(orc, sh, l, [0]), xn, threads=threads)["out"]
+            out = (routed + shared).astype(np.float32)
+        h = (h + out).astype(np.float32)
     return h

@@ -73,7 +73,7 @@ QWEN3_30B = LayerConfig("qwen3-30b-a3b-layer", 2048, 768, 128, 8, QUANT_Q8_0, RO
 # GPT-OSS-120B-shaped 36-layer stack (weights as configs[0]), RMSNorm + residual
 GPT_OSS_120B = LayerConfig("gpt-oss-120b-stack", 2880, 2880, 128, 4, QUANT_MXFP4, ROUTE_TOPK_SOFTMAX, ACT_SWIGLU_OAI,
                            True, True, True, seed=0, layers=36, tokens=(1, 64, 4096))
-# load skew, Qwen3 shapes in Q8_0 and MXFP4 (router bias set by the caller from a Zipf law)
+# load skew, Qwen3 shapes in Q8_0 and MXFP4; the router bias comes from zipf_router_bias
 QWEN3_SKEW_Q8 = LayerConfig("qwen3-skew-q8_0", 2048, 768, 128, 8, QUANT_Q8_0, ROUTE_SOFTMAX_TOPK_NORM, ACT_SILU,
                             False, False, True, seed=3, tokens=(4096,))
 QWEN3_SKEW_MXFP4 = LayerConfig("qwen3-skew-mxfp4", 2048, 768, 128, 8, QUANT_MXFP4, ROUTE_SOFTMAX_TOPK_NORM, ACT_SILU,
@@ -92,3 +92,17 @@ DEEPSEEK_V2_LITE_SHARED = LayerConfig("deepseek-v2-lite-shared", 2048, 2 * 1408,
 DEEPSEEK_V2_LITE_DENSE = LayerConfig("deepseek-v2-lite-dense", 2048, 10944, 1, 1, QUANT_Q8_0, ROUTE_SOFTMAX_TOPK,
                                      ACT_SILU, False, False, False, seed=4, layers=1, tokens=(1, 2048))
 CONFIGS.update({c.name: c for c in (DEEPSEEK_V2_LITE_SHARED, DEEPSEEK_V2_LITE_DENSE)})
+
+
+def zipf_router_bias(experts: int, alpha: float = 1.2, noise_sigma: float = 0.5, seed: int = 3):
+    """configs[3]'s router bias: log of a Zipf(alpha) expert popularity plus N(0, noise_sigma) noise,
+    float32 [experts].  Popularity rank k (1 = hottest) has weight k^-alpha / sum_j j^-alpha; the
+    ranks are a seeded random permutation of the experts, so the hot experts scatter over any
+    contiguous expert-parallel partition.  With the router's own logits ~N(0, 0.02 * |x|) the top
+    experts receive roughly 20x the mean load."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    ranks = rng.permutation(experts) + 1
+    pop = ranks.astype(np.float64) ** -alpha
+    pop /= pop.sum()
+    return (np.log(pop) + rng.normal(0.0, noise_sigma, experts)).astype(np.float32)

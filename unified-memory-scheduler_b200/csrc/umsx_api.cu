@@ -560,9 +560,10 @@ bool prefill_eligible(const umsx_moe *m, const Workspace &ws, int tokens) {
 
 // y_jobs (expert parallelism): instead of combining, write each resident job's output to
 // y_jobs[t][r][:] and leave the other rows alone.
+// extra: [T][H] added to each token's routed sum before the residual (shared experts), or null.
 umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
                         const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
-                        float *y_jobs = nullptr) {
+                        float *y_jobs = nullptr, const float *extra = nullptr) {
     const auto &d = m->d;
     const int K = d.top_k, H = d.hidden, I = d.intermediate, jobs = tokens * K;
     if (ev) if (umsx_status st = mark(ev[0], s)) return st;
@@ -648,7 +649,7 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
         UMSX_LAUNCHED(launch_prefill_scatter(ws.y, ws.inv, ws.disp.ids, m->e_lo, m->e_local, tokens, K, H, y_jobs, s));
         return UMSX_OK;
     }
-    UMSX_LAUNCHED(launch_prefill_combine(ws.y, ws.disp.weights, ws.inv, tokens, K, H, residual, out, ws.disp.err, s));
+    UMSX_LAUNCHED(launch_prefill_combine(ws.y, ws.disp.weights, ws.inv, tokens, K, H, extra, residual, out, ws.disp.err, s));
     if (ev) if (umsx_status st = mark(ev[4], s)) return st;
     return UMSX_OK;
 }
@@ -668,10 +669,10 @@ static int per_stage_chunk(int tokens, int top_k, int experts) {
 
 umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
                       const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
-                      float *y_jobs = nullptr) {
+                      float *y_jobs = nullptr, const float *extra = nullptr) {
     const auto &d = m->d;
     if (prefill_eligible(m, ws, tokens))
-        return run_prefill(m, ws, x, x_dtype, tokens, out, residual, rmsnorm, eps, s, ev, y_jobs);
+        return run_prefill(m, ws, x, x_dtype, tokens, out, residual, rmsnorm, eps, s, ev, y_jobs, extra);
     if (ev) if (umsx_status st = mark(ev[0], s)) return st;
     if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s, 1)) return st;
     if (ev) if (umsx_status st = mark(ev[1], s)) return st;
@@ -711,6 +712,7 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
         p.combine_out = out;
         p.top_k = d.top_k;
         p.prefetch_early = 1;
+        p.extra = extra;
     }
     if (d.quant == UMSX_QUANT_MXFP4) { p.a_rec = ws.act_rec; p.a_rsc = ws.act_sc; }  // bulk-copied records
     else { p.a_codes = ws.act_codes; p.a_scales = ws.act_scales; }
@@ -718,7 +720,7 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     if (y_jobs) return UMSX_OK;
     if (ev) {  // timed stages keep the combine a kernel of its own so that every stage has a boundary
         if (umsx_status st = mark(ev[3], s)) return st;
-        UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, residual, out, ws.disp.err, s));
+        UMSX_LAUNCHED(launch_combine(ws.y, ws.disp.weights, tokens, d.top_k, d.hidden, extra, residual, out, ws.disp.err, s));
         if (umsx_status st = mark(ev[4], s)) return st;
     }
     return UMSX_OK;
@@ -782,6 +784,18 @@ umsx_status umsx_moe_forward_host(umsx_moe *m, const void *x, int x_dtype, int t
     if (umsx_status st = forward_layer(m, m->ws.x_dev, x_dtype, tokens, m->ws.out_dev, s)) return st;
     UMSX_CUDA(cudaMemcpyAsync(out, m->ws.out_dev, out_bytes, cudaMemcpyDeviceToHost, s));
     return check_device_flag(m->ws, s);
+}
+
+umsx_status umsx_moe_set_router(umsx_moe *m, const float *router_w, const float *router_b) {
+    if (!m || !router_w) return fail(UMSX_EINVAL, "null handle or router weights");
+    if ((router_b != nullptr) != (m->d.has_router_bias != 0))
+        return fail(UMSX_EINVAL, "router_b must be given exactly when the layer has a router bias");
+    std::lock_guard<std::mutex> lock(m->mu);
+    UMSX_CUDA(cudaSetDevice(m->device));
+    UMSX_CUDA(cudaDeviceSynchronize());  // no call of this handle reads the router meanwhile
+    UMSX_CUDA(cudaMemcpy(m->router_w, router_w, (size_t)m->d.experts * m->d.hidden * 4, cudaMemcpyHostToDevice));
+    if (router_b) UMSX_CUDA(cudaMemcpy(m->router_b, router_b, (size_t)m->d.experts * 4, cudaMemcpyHostToDevice));
+    return UMSX_OK;
 }
 
 umsx_status umsx_moe_status(umsx_moe *m, umsx_stream stream) {
@@ -892,7 +906,7 @@ umsx_status umsx_combine(const float *y, const float *weights, int tokens, int t
                          umsx_stream stream) {
     if (!y || !weights || !out || tokens <= 0 || top_k <= 0 || width <= 0 || width % 4)
         return fail(UMSX_EINVAL, "invalid combine arguments (width must be a multiple of 4)");
-    UMSX_LAUNCHED(launch_combine(y, weights, tokens, top_k, width, nullptr, out, nullptr, static_cast<cudaStream_t>(stream)));
+    UMSX_LAUNCHED(launch_combine(y, weights, tokens, top_k, width, nullptr, nullptr, out, nullptr, static_cast<cudaStream_t>(stream)));
     return UMSX_OK;
 }
 
@@ -925,6 +939,9 @@ umsx_status umsx_moe_export_expert(umsx_moe *m, int proj, int expert, void *host
 
 struct umsx_stack {
     std::vector<umsx_moe *> layers;
+    std::vector<umsx_moe *> shared;  // per layer: a one-expert shared-FFN handle added to the routed sum, or null
+    float *y_sh = nullptr;           // [T][H] the current layer's shared-FFN output
+    bool uniform = true;             // every layer has layer 0's shape and no shared FFN
     float eps = 1e-5f;
     int device = 0;
     int max_tokens = 0;
@@ -957,7 +974,15 @@ umsx_status record_stack(umsx_stack *st, int tokens, int dtype, cudaStream_t s) 
         UMSX_CUDA(cudaMemcpyAsync(st->h, st->ws.x_dev, (size_t)tokens * H * 4, cudaMemcpyDeviceToDevice, s));
     for (size_t l = 0; l < st->layers.size(); ++l) {
         const cudaEvent_t *ev = st->timing ? &st->stage[5 * l] : nullptr;
-        if (umsx_status r = run_layer(st->layers[l], st->ws, st->h, UMSX_DTYPE_F32, tokens, st->h, st->h, 1, st->eps, s, ev))
+        umsx_moe *sh = st->shared.empty() ? nullptr : st->shared[l];
+        // the shared FFN first (its output rows land in y_sh), then the routed layer, whose combine
+        // adds them as the term after the k routed ones: h + ((sum_r w_r y_r) + y_shared)
+        if (sh)
+            if (umsx_status r = run_layer(sh, st->ws, st->h, UMSX_DTYPE_F32, tokens, nullptr, nullptr, 1, st->eps, s,
+                                          nullptr, st->y_sh))
+                return r;
+        if (umsx_status r = run_layer(st->layers[l], st->ws, st->h, UMSX_DTYPE_F32, tokens, st->h, st->h, 1, st->eps, s,
+                                      ev, nullptr, sh ? st->y_sh : nullptr))
             return r;
     }
     return UMSX_OK;
@@ -989,7 +1014,7 @@ umsx_status stack_run(umsx_stack *st, const void *x, int dtype, int tokens, void
     const size_t in_bytes = (size_t)tokens * st->hidden * (dtype == UMSX_DTYPE_BF16 ? 2 : 4);
     const size_t out_bytes = (size_t)tokens * st->hidden * 4;
     const int L = (int)st->layers.size();
-    bool eligible = !st->timing;
+    bool eligible = !st->timing && st->uniform;
     for (int l = 0; l < L && eligible; ++l) eligible = decode_eligible(st->layers[l], tokens, L);
     if (eligible) {
         // one persistent launch on the caller's stream, reading x and writing out in place when they are device memory
@@ -1029,30 +1054,59 @@ umsx_status stack_run(umsx_stack *st, const void *x, int dtype, int tokens, void
 
 extern "C" {
 
-umsx_status umsx_stack_create(umsx_moe *const *layers, int n_layers, int max_tokens, float rms_eps, umsx_stack **out) {
+}  // extern "C"
+
+namespace {
+umsx_status stack_create(umsx_moe *const *layers, umsx_moe *const *shared, int n_layers, int max_tokens, float rms_eps,
+                         bool same_shape, umsx_stack **out) {
     if (!out || !layers || n_layers <= 0) return fail(UMSX_EINVAL, "need at least one layer");
     *out = nullptr;
     const umsx_moe *l0 = layers[0];
     if (!l0) return fail(UMSX_EINVAL, "null layer");
+    // the workspace serves every layer: it is carved for the largest of each dimension
+    umsx_moe_desc big = l0->d;
+    int e_local = l0->e_local;
+    bool uniform = true;
+    auto widen = [&](const umsx_moe *m) {
+        big.top_k = std::max(big.top_k, m->d.top_k);
+        big.experts = std::max(big.experts, m->d.experts);
+        big.intermediate = std::max(big.intermediate, m->d.intermediate);
+        if (m->d.quant == UMSX_QUANT_MXFP4) big.quant = UMSX_QUANT_MXFP4;
+        e_local = std::max(e_local, m->e_local);
+    };
     for (int l = 0; l < n_layers; ++l) {
         const umsx_moe *m = layers[l];
-        if (!m || m->device != l0->device || m->d.hidden != l0->d.hidden || m->d.top_k != l0->d.top_k ||
-            m->d.experts != l0->d.experts || m->d.intermediate != l0->d.intermediate || m->e_local != l0->e_local)
-            return fail(UMSX_EINVAL, "stack layers must share device and shape");
+        if (!m || m->device != l0->device || m->d.hidden != l0->d.hidden)
+            return fail(UMSX_EINVAL, "stack layers must share device and width");
+        const bool same = m->d.top_k == l0->d.top_k && m->d.experts == l0->d.experts &&
+                          m->d.intermediate == l0->d.intermediate && m->e_local == l0->e_local;
+        if (same_shape && !same) return fail(UMSX_EINVAL, "stack layers must share device and shape");
+        uniform = uniform && same;
         if (m->e_local != m->d.experts)
             return fail(UMSX_EUNSUPPORTED, "a stack runs whole layers; expert-parallel handles use umsx_moe_forward_jobs");
+        widen(m);
+        const umsx_moe *sh = shared ? shared[l] : nullptr;
+        if (sh) {
+            if (sh->device != l0->device || sh->d.hidden != l0->d.hidden || sh->d.experts != 1 || sh->d.top_k != 1)
+                return fail(UMSX_EINVAL, "a shared-expert handle is a one-expert top-1 layer of the stack's width and device");
+            uniform = false;
+            widen(sh);
+        }
     }
     if (max_tokens <= 0 || max_tokens > 65535) return fail(UMSX_EINVAL, "max_tokens must be in [1, 65535]");
     UMSX_CUDA(cudaSetDevice(l0->device));
     auto *st = new umsx_stack();
     st->layers.assign(layers, layers + n_layers);
+    if (shared) st->shared.assign(shared, shared + n_layers);
+    st->uniform = uniform;
     st->eps = rms_eps;
     st->device = l0->device;
     st->max_tokens = max_tokens;
     st->hidden = l0->d.hidden;
     auto run = [&]() -> umsx_status {
-        if (umsx_status r = alloc_workspace(st->ws, l0->d, l0->e_local, max_tokens, 0)) return r;
+        if (umsx_status r = alloc_workspace(st->ws, big, e_local, max_tokens, 0)) return r;
         UMSX_CUDA(cudaMalloc(&st->h, (size_t)max_tokens * st->hidden * 4));
+        if (!st->shared.empty()) UMSX_CUDA(cudaMalloc(&st->y_sh, (size_t)max_tokens * st->hidden * 4));
         UMSX_CUDA(cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking));
         UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_in, cudaEventDisableTiming));
         UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_out, cudaEventDisableTiming));
@@ -1061,6 +1115,18 @@ umsx_status umsx_stack_create(umsx_moe *const *layers, int n_layers, int max_tok
     if (umsx_status r = run()) { umsx_stack_destroy(st); return r; }
     *out = st;
     return UMSX_OK;
+}
+}  // namespace
+
+extern "C" {
+
+umsx_status umsx_stack_create(umsx_moe *const *layers, int n_layers, int max_tokens, float rms_eps, umsx_stack **out) {
+    return stack_create(layers, nullptr, n_layers, max_tokens, rms_eps, true, out);
+}
+
+umsx_status umsx_stack_create_mixed(umsx_moe *const *layers, umsx_moe *const *shared, int n_layers, int max_tokens,
+                                    float rms_eps, umsx_stack **out) {
+    return stack_create(layers, shared, n_layers, max_tokens, rms_eps, false, out);
 }
 
 void umsx_stack_destroy(umsx_stack *st) {
@@ -1073,6 +1139,7 @@ void umsx_stack_destroy(umsx_stack *st) {
     if (st->ev_out) cudaEventDestroy(st->ev_out);
     if (st->stream) cudaStreamDestroy(st->stream);
     if (st->h) cudaFree(st->h);
+    if (st->y_sh) cudaFree(st->y_sh);
     if (st->ws.mem) cudaFree(st->ws.mem);
     delete st;
 }

@@ -117,6 +117,7 @@ struct GemvParams {
     float *combine_out;     // [T][N]
     int top_k;
     int prefetch_early;     // the slot records were written two kernels back: prefetch weights before waiting
+    const float *extra;     // [T][N] added after the top_k routed terms (the shared experts' output), or null
 };
 
 // Persistent decode kernel (umsx_decode.cu): every layer of a stack, or one layer,
@@ -200,8 +201,9 @@ int launch_prefill_pack(const Dispatch &d, int jobs, const int32_t *n_jobs, int 
 // y[t][r] = yj[inv[t][r]] for the (t, r) whose expert id lies in [e_lo, e_lo + e_local).
 int launch_prefill_scatter(const float *yj, const int32_t *inv, const int32_t *ids, int e_lo, int e_local, int tokens,
                            int K, int width, float *y, cudaStream_t s);
+// extra: [T][width] added after the K routed terms (shared experts), or null
 int launch_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
-                           const float *residual, float *out, uint32_t *err, cudaStream_t s);
+                           const float *extra, const float *residual, float *out, uint32_t *err, cudaStream_t s);
 int launch_moe_gemm(const MoeGemmParams &p, const void *act_hi, const void *act_lo, int rows_total, cudaStream_t s);
 
 // Thread-local status channel shared by every translation unit (umsx_api.cu).
@@ -216,8 +218,8 @@ int launch_gate_up(const GateUpParams &p, const Dispatch &d, int max_slots, int 
 int launch_gemv(const GemvParams &p, const Dispatch &d, int max_slots, int max_per_expert, cudaStream_t s);
 
 // err: status word that records a non-finite output (kErrNonFinite), or null
-int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *residual, float *out,
-                   uint32_t *err, cudaStream_t s);
+int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *extra,
+                   const float *residual, float *out, uint32_t *err, cudaStream_t s);
 int launch_repack(const Matrix &m, int expert, const uint8_t *ggml, cudaStream_t s);
 int launch_export(const Matrix &m, int expert, uint8_t *ggml, cudaStream_t s);
 int launch_gen_blocks(int quant, uint64_t seed, uint64_t stream, uint64_t first_block, uint64_t nblocks,

@@ -749,6 +749,7 @@ __global__ void __launch_bounds__(W * 32) k_gemv(GemvParams p, GemvSrc src, Disp
                     for (int r = 0; r < K; ++r)
                         acc = __fadd_rn(acc, __fmul_rn(__ldcg(p.route_w + (size_t)tok * K + r),
                                                        __ldcg(p.out + ((size_t)tok * K + r) * N + n0 + i)));
+                    if (p.extra) acc = __fadd_rn(acc, __ldcg(p.extra + (size_t)tok * N + n0 + i));
                     if (p.residual) acc = __fadd_rn(p.residual[(size_t)tok * N + n0 + i], acc);
                     flag_nonfinite(acc, d.err);
                     p.combine_out[(size_t)tok * N + n0 + i] = acc;
@@ -1050,6 +1051,7 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
                     for (int rr = 0; rr < K; ++rr)
                         acc2 = __fadd_rn(acc2, __fmul_rn(__ldcg(p.route_w + (size_t)tok * K + rr),
                                                          __ldcg(p.out + ((size_t)tok * K + rr) * N + n0 + i)));
+                    if (p.extra) acc2 = __fadd_rn(acc2, __ldcg(p.extra + (size_t)tok * N + n0 + i));
                     if (p.residual) acc2 = __fadd_rn(p.residual[(size_t)tok * N + n0 + i], acc2);
                     flag_nonfinite(acc2, d.err);
                     p.combine_out[(size_t)tok * N + n0 + i] = acc2;
@@ -1065,7 +1067,7 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
 // ============================================================================
 
 __global__ void k_combine(const float *__restrict__ y, const float *__restrict__ w, int tokens, int K, int width,
-                          const float *residual, float *out, uint32_t *err) {
+                          const float *extra, const float *residual, float *out, uint32_t *err) {
     const int v4 = width / 4;
     const size_t total = (size_t)tokens * v4;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -1078,6 +1080,13 @@ __global__ void k_combine(const float *__restrict__ y, const float *__restrict__
             acc.y = __fadd_rn(acc.y, __fmul_rn(wr, v.y));
             acc.z = __fadd_rn(acc.z, __fmul_rn(wr, v.z));
             acc.w = __fadd_rn(acc.w, __fmul_rn(wr, v.w));
+        }
+        if (extra) {  // the shared experts' output, the (K+1)-th term
+            const float4 v = reinterpret_cast<const float4 *>(extra + t * width)[c];
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
         }
         if (residual) {  // h + moe, the residual stream of the layer stack (may alias out)
             const float4 r = reinterpret_cast<const float4 *>(residual + t * width)[c];
@@ -1351,11 +1360,10 @@ int launch_gemv(const GemvParams &p, const Dispatch &d, int slots, int max_per_e
     return 1;
 }
 
-int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *residual, float *out,
-                   uint32_t *err,
-                   cudaStream_t s) {
+int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *extra,
+                   const float *residual, float *out, uint32_t *err, cudaStream_t s) {
     const size_t n = (size_t)tokens * (width / 4);
-    k_combine<<<grid_for(n, 256), 256, 0, s>>>(y, w, tokens, top_k, width, residual, out, err);
+    k_combine<<<grid_for(n, 256), 256, 0, s>>>(y, w, tokens, top_k, width, extra, residual, out, err);
     return 1;
 }
 

@@ -644,7 +644,7 @@ __global__ void k_prefill_pack(const uint8_t *xq_codes, const float *xq_scales, 
 
 // out[t][n] = (residual[t][n] +) sum_r w[t][r] * y[inv[t][r]][n], rank order from 0.
 __global__ void k_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
-                                  const float *residual, float *out, uint32_t *err) {
+                                  const float *extra, const float *residual, float *out, uint32_t *err) {
     const size_t total = (size_t)tokens * width;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / width), n = (int)(i - (size_t)t * width);
@@ -652,6 +652,7 @@ __global__ void k_prefill_combine(const float *y, const float *w, const int32_t 
         for (int r = 0; r < K; ++r)
             acc = __fadd_rn(acc, __fmul_rn(__ldg(w + (size_t)t * K + r),
                                            __ldcg(y + (size_t)__ldg(inv + (size_t)t * K + r) * width + n)));
+        if (extra) acc = __fadd_rn(acc, extra[i]);  // the shared experts' output, the (K+1)-th term
         const float v = residual ? __fadd_rn(residual[i], acc) : acc;
         flag_nonfinite(v, err);
         out[i] = v;
@@ -736,8 +737,8 @@ int launch_prefill_scatter(const float *yj, const int32_t *inv, const int32_t *i
 }
 
 int launch_prefill_combine(const float *y, const float *w, const int32_t *inv, int tokens, int K, int width,
-                           const float *residual, float *out, uint32_t *err, cudaStream_t s) {
-    k_prefill_combine<<<148 * 8, 256, 0, s>>>(y, w, inv, tokens, K, width, residual, out, err);
+                           const float *extra, const float *residual, float *out, uint32_t *err, cudaStream_t s) {
+    k_prefill_combine<<<148 * 8, 256, 0, s>>>(y, w, inv, tokens, K, width, extra, residual, out, err);
     return 1;
 }
 

@@ -30,10 +30,10 @@ PROJ_GATE_UP, PROJ_GATE, PROJ_UP, PROJ_DOWN = 0, 1, 2, 3
 BLOCK_BYTES = {QUANT_Q8_0: 34, QUANT_MXFP4: 17}
 
 # exported symbols of include/umsx.h (the tests check each one is present)
-EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "umsx_moe_forward",
+EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "umsx_moe_set_router", "umsx_moe_forward",
            "umsx_moe_forward_host", "umsx_moe_forward_jobs", "umsx_moe_status", "umsx_route", "umsx_expert_down_q8", "umsx_mul_mat_id",
            "umsx_combine",
-           "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_destroy", "umsx_stack_forward",
+           "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_create_mixed", "umsx_stack_destroy", "umsx_stack_forward",
            "umsx_stack_forward_host", "umsx_stack_status", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_stack_inject_fault",
            "umsx_route_static",
            "umsx_gguf_load_experts", "umsx_gguf_experts_free", "umsx_moe_create_gguf",
@@ -82,6 +82,7 @@ def lib():
         "umsx_moe_create_synthetic": (i32, [C.POINTER(Desc), u64, C.c_uint32, C.c_float, C.c_float, C.c_float, i32, sz,
                                             C.POINTER(vp)]),
         "umsx_moe_destroy": (None, [vp]),
+        "umsx_moe_set_router": (i32, [vp, vp, vp]),
         "umsx_moe_forward": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "umsx_moe_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
         "umsx_moe_forward_jobs": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
@@ -93,6 +94,7 @@ def lib():
         "umsx_combine": (i32, [vp, vp, i32, i32, i32, vp, vp]),
         "umsx_moe_export_expert": (i32, [vp, i32, i32, vp, sz]),
         "umsx_stack_create": (i32, [C.POINTER(vp), i32, i32, C.c_float, C.POINTER(vp)]),
+        "umsx_stack_create_mixed": (i32, [C.POINTER(vp), C.POINTER(vp), i32, i32, C.c_float, C.POINTER(vp)]),
         "umsx_stack_destroy": (None, [vp]),
         "umsx_stack_forward": (i32, [vp, vp, i32, i32, vp, vp]),
         "umsx_stack_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
@@ -270,6 +272,14 @@ class MoeLayer:
                                           _stream(stream)))
         return out_host
 
+    def set_router(self, router_w, router_b=None):
+        """Replaces the router from host arrays (umsx_moe_set_router): router_w float32 [E, H],
+        router_b float32 [E] exactly when the layer has a router bias."""
+        import numpy as np
+        w = np.ascontiguousarray(router_w, dtype=np.float32)
+        b = None if router_b is None else np.ascontiguousarray(router_b, dtype=np.float32)
+        check(lib().umsx_moe_set_router(self._h, _np_ptr(w), _np_ptr(b)))
+
     def status(self, stream=None):
         """Raises UmsxError (ENONFINITE / ETIMEOUT) for what the handle's earlier calls on the stream
         recorded on the device; clears the record (umsx_moe_status)."""
@@ -316,16 +326,28 @@ class MoeLayer:
 
 
 class MoeStack:
-    """h <- h + MoE_l(RMSNorm(h)) over a list of MoeLayer (one CUDA graph replay per call)."""
+    """h <- h + MoE_l(RMSNorm(h)) over a list of MoeLayer (one CUDA graph replay per call).
+
+    shared: optional list (one entry per layer, None for none) of one-expert top-1 MoeLayer handles
+    holding each layer's shared experts; their output is the term after the routed ones in the
+    layer's rank-order combine (umsx_stack_create_mixed).  With `shared`, the layers may differ in
+    shape (e.g. a dense FFN as layer 0, itself a one-expert top-1 layer)."""
 
     STAGES = ("router", "gate_up", "down", "combine")
 
-    def __init__(self, layers: list, max_tokens: int, rms_eps: float = 1e-5):
+    def __init__(self, layers: list, max_tokens: int, rms_eps: float = 1e-5, shared: list | None = None):
         self.layers = list(layers)
+        self.shared = list(shared) if shared is not None else None
         self.hidden = self.layers[0].desc.hidden
         arr = (C.c_void_p * len(self.layers))(*[l._h for l in self.layers])
         self._h = C.c_void_p()
-        check(lib().umsx_stack_create(arr, len(self.layers), max_tokens, rms_eps, C.byref(self._h)))
+        if self.shared is None:
+            check(lib().umsx_stack_create(arr, len(self.layers), max_tokens, rms_eps, C.byref(self._h)))
+        else:
+            if len(self.shared) != len(self.layers):
+                raise UmsxError(EINVAL, "one shared entry (or None) per layer")
+            sh = (C.c_void_p * len(self.layers))(*[None if x is None else x._h for x in self.shared])
+            check(lib().umsx_stack_create_mixed(arr, sh, len(self.layers), max_tokens, rms_eps, C.byref(self._h)))
 
     def close(self):
         if self._h:
