@@ -10,9 +10,13 @@ tokens drawn from a pool of 16 batches so that routing changes every step.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--mode decode|prefill]
                   [--tokens T] [--layers L] [--impl umsx|reference] [--ep]
 
-With N > 1 (torchrun, one rank per GPU) every rank holds the whole stack and
-runs its own tokens (data-parallel replicas, weak scaling); the value is all
-ranks' tokens over the slowest rank's time.  `--impl reference` times the
+With N > 1 (torchrun, one rank per GPU) decode runs expert-parallel: rank g holds
+experts [g*E/N, (g+1)*E/N) of every layer (61 GB / N) and one token per step
+(global batch N), the router is replicated and the dispatch / combine travel as
+P2P NVLink stores inside the exchange kernels (ep.EpStack); the value is all
+ranks' tokens over the slowest rank's time, and a 2-layer parity check against
+one GPU's whole layers runs first (parity_ok).  `--replicas` runs N independent whole-stack
+replicas instead.  `--impl reference` times the
 reference's own CPU implementation of the path (tools/trace/exact_packed_cpu.h
 packed MXFP4 GEMV compiled from the reference sources into oracle/_ref/) on
 this host's cores, on rank 0 only.
@@ -59,6 +63,8 @@ def parse():
     ap.add_argument("--ref-seconds", type=float, default=150.0, help="timed budget of the --impl reference arm")
     ap.add_argument("--no-prefill", action="store_true", help="decode line without the prefill sub-record")
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the ranks (prefill)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1 decode as independent replicas instead of expert parallelism")
     ap.add_argument("--config", choices=("stack", "skew"), default="stack",
                     help="stack: configs[2] (the headline); skew: configs[3] load-skew layers at T=4096")
     a = ap.parse_args()
@@ -328,12 +334,146 @@ def algorithmic_bytes(cfg, tokens: int):
     return gu, dn, distinct
 
 
+def ep_decode_arm(a):
+    """N > 1 decode: the stack split over the ranks by expert (rank g holds experts [g*E/N, (g+1)*E/N) of
+    every layer, 61 GB / N), one token per rank per step (global batch N), the router replicated, the
+    dispatch and combine exchanged by P2P stores over NVLink inside the kernels (EpStack).  Before
+    timing, every rank's token goes through a 2-layer slice and rank 0 recomputes the same tokens on one
+    GPU with whole layers: the bits must agree (parity_ok); a mismatch ends the run with a non-zero
+    status."""
+    import datetime
+    import importlib
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    pkg = load_pkg()
+    ep = importlib.import_module(pkg.__name__ + ".ep")
+    cfg = pkg.configs.GPT_OSS_120B
+    if a.experts:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, experts=a.experts)
+    H = cfg.hidden
+    layers = [pkg.MoeLayer(cfg.desc(max_tokens=world, ep_rank=rank, ep_world=world), synthetic=cfg.synthetic(layer=l),
+                           device=dev.index, reserve_bytes=2 << 30) for l in range(a.layers)]
+    group = ep.EpGroup(H, cfg.top_k, dev.index)
+    stream = torch.cuda.current_stream(dev)
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # parity: every rank's token through the first two layers, against rank 0's one-GPU recompute of the
+    # same tokens with whole layers (the one-GPU stack is bit-exact with the oracle in the GPU tests)
+    xcheck = torch.from_numpy(np.random.default_rng(99).standard_normal((world, H)).astype(np.float32)).to(dev)
+    slice_st = ep.EpStack(group, layers[:2])
+    got = slice_st.forward(xcheck[rank:rank + 1].contiguous())
+    slice_st.close()
+    gathered = [torch.empty_like(got) for _ in range(world)]
+    dist.all_gather(gathered, got)
+    ok = torch.ones(1, dtype=torch.int32, device=dev)
+    if rank == 0:
+        whole = [pkg.MoeLayer(cfg.desc(max_tokens=world), synthetic=cfg.synthetic(layer=l), device=dev.index,
+                              reserve_bytes=2 << 30) for l in range(2)]
+        ref_st = pkg.MoeStack(whole, max_tokens=world)
+        want = ref_st.forward(xcheck)
+        ok[0] = int(torch.equal(torch.cat(gathered).view(torch.int32), want.view(torch.int32)))
+        ref_st.close()
+        for l in whole:
+            l.close()
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    parity_ok = bool(ok.item())
+
+    est = ep.EpStack(group, layers)
+    pool = 16
+    rng = np.random.default_rng(1000)  # the same batches on every rank: rank g takes row g
+    xs = torch.from_numpy(rng.standard_normal((pool, world, H)).astype(np.float32)).to(torch.bfloat16)
+    xs_dev = xs[:, rank:rank + 1].contiguous().to(dev)
+    out = torch.empty((1, H), dtype=torch.float32, device=dev)
+    for i in range(a.warmup):
+        est.forward(xs_dev[i % pool], out)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = pkg.kernel_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index) as clk:
+        ev0.record(stream)
+        for i in range(a.steps):
+            est.forward(xs_dev[i % pool], out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    launches = pkg.kernel_launches() - launches0
+    est.status()
+    dist.barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_step = ms / a.steps
+    # end to end: the token from pinned host memory, the result back, every step
+    e2e = None
+    if not a.no_e2e:
+        xh = xs[:, rank:rank + 1].contiguous().pin_memory()
+        oh = torch.empty((1, H), dtype=torch.float32).pin_memory()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(a.steps):
+            est.forward_host(xh[i % pool], oh)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": world * a.steps / (ems / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(H * 2),
+               "d2h_bytes_per_step": int(H * 4), "ms_per_step": ems / a.steps,
+               "api": "umsx_ep_stack_forward_host (per rank)"}
+    peak, peak_kind = peaks()
+    E, k = cfg.experts, cfg.top_k
+    distinct = E * (1 - (1 - k / E) ** world)
+    expert_b = cfg.expert_bytes()
+    step_bytes = a.layers * (distinct * expert_b + world * cfg.router_bytes())  # all ranks together
+    per_gpu = step_bytes / world / (ms_step / 1e3) / 1e9
+    xbytes = a.layers * (world * (world - 1) * H * 4 + world * k * H * 4 * (world - 1) / world)
+    res = {"metric": metric_name(a), "value": world * a.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
+           "parity_ok": parity_ok,
+           "config": {"workload": f"gpt-oss-120b-stack {a.mode}, expert parallel", "layers": a.layers,
+                      "experts": cfg.experts, "experts_per_gpu": cfg.experts // world, "top_k": k, "hidden": H,
+                      "ffn": cfg.intermediate, "quant": "mxfp4", "tokens_per_step_per_gpu": 1, "global_batch": world,
+                      "parallelism": f"ep{world}",
+                      "exchange": "P2P NVLink stores inside k_ep_share / k_ep_combine (CUDA IPC mappings), "
+                                  "release/acquire flags; no collective in the data path",
+                      "l2": "inputs larger than L2", "expected_distinct_experts_per_layer": distinct,
+                      "parity": "every rank's token through a 2-layer slice, bit-exact with one GPU running whole layers"},
+           "roofline": {"kernel": "whole decode step per GPU (per-stage exact kernels + exchange kernels)",
+                        "bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                        "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_step_all_gpus": step_bytes,
+                        "traffic": None},
+           "exchange_bytes_per_step": xbytes, "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e}
+    est.close()
+    group.close()
+    for l in layers:
+        l.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res))
+    if not parity_ok:
+        raise SystemExit(3)
+
+
 def gpu_arm(a):
     import numpy as np
     import torch
     import torch.distributed as dist
 
     rank, world, local = dist_env()
+    if world > 1 and a.mode == "decode" and not a.replicas:
+        return ep_decode_arm(a)
     if world > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))

@@ -234,6 +234,39 @@ umsx_status umsx_route_static(const void *x, int x_dtype, int tokens, const floa
                               int hidden, int experts, int top_k, int routing, float routed_scale, int32_t *ids,
                               float *weights, int32_t *counts, umsx_stream stream);
 
+/* ---- Expert parallelism over NVLink (no counterpart in the reference, which refuses more than one
+ * GPU backend: llama-b11669-hybrid-experts.patch:2617-2618) ---------------------------------------
+ * One process per GPU.  A group is one exchange buffer per rank, mapped into every other rank's
+ * process with CUDA IPC: create it on every rank, gather the ranks' handles (umsx_ep_handle) in rank
+ * order with the caller's transport (torch.distributed in the Python binding), then connect.
+ * An expert-parallel stack holds this rank's share of every layer (handles created with
+ * desc.ep_rank / ep_world equal to the group's) and runs a decode step of one token per rank:
+ * per layer, each rank stores its hidden row into every peer's buffer, all ranks route all the
+ * group's tokens (the router is replicated), each runs the jobs of its own experts, stores each
+ * job's output row into the buffer of the rank that owns the token, and that rank combines its
+ * token in rank order with the residual.  Stores are plain P2P stores from inside the exchange
+ * kernels, flags st.release.sys, waits ld.acquire.sys bounded by umsx_ep_set_wait (default about
+ * one second): a rank that never arrives gives the others UMSX_ETIMEOUT from _host calls or
+ * umsx_ep_stack_status, not a hang.  Each token's result has the single-GPU stack's bits.  All ranks
+ * must call forward the same number of times, in step. */
+typedef struct umsx_ep umsx_ep;
+typedef struct umsx_ep_stack umsx_ep_stack;
+umsx_status umsx_ep_create(int rank, int world, int device, int hidden, int top_k, umsx_ep **out);
+/* The rank's IPC handle (size = 64 bytes). */
+umsx_status umsx_ep_handle(umsx_ep *ep, void *handle_out, size_t size);
+/* handles: every rank's handle in rank order (size = world * 64 bytes). */
+umsx_status umsx_ep_connect(umsx_ep *ep, const void *handles, size_t size);
+umsx_status umsx_ep_set_wait(umsx_ep *ep, int64_t wait_limit_cycles);
+void umsx_ep_destroy(umsx_ep *ep);
+umsx_status umsx_ep_stack_create(umsx_ep *ep, umsx_moe *const *layers, int n_layers, float rms_eps,
+                                 umsx_ep_stack **out);
+void umsx_ep_stack_destroy(umsx_ep_stack *stack);
+/* x: this rank's token [1][H] (fp32 or bf16, device) -> out [1][H] fp32 (device). */
+umsx_status umsx_ep_stack_forward(umsx_ep_stack *stack, const void *x, int x_dtype, float *out, umsx_stream stream);
+umsx_status umsx_ep_stack_forward_host(umsx_ep_stack *stack, const void *x, int x_dtype, float *out,
+                                       umsx_stream stream);
+umsx_status umsx_ep_stack_status(umsx_ep_stack *stack, umsx_stream stream);
+
 /* ---- GGUF checkpoints ------------------------------------------------------------------
  * The selected experts of one layer read from a GGUF file or a set of shards named
  * <stem>-00001-of-NNNNN.gguf (pass the first).  Replaces load_gguf_experts

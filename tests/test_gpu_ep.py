@@ -79,3 +79,95 @@ def test_two_gpu_expert_parallel_layer_bit_exact(tokens):
         assert ok is True, (rank, ok)
         covered += t1 - t0
     assert covered == tokens
+
+
+# ---- decode over NVLink: exchange by P2P stores inside the kernels ----------------------------
+
+def _ep_decode_worker(rank, world, port, mode, q):
+    try:
+        import datetime
+        import importlib
+
+        import torch.distributed as dist
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        # no collective carries layer data: the process group only moves the IPC handles at set-up
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        import __graft_entry__ as ge
+        pkg = ge.load_package()
+        ep = importlib.import_module(pkg.__name__ + ".ep")
+        from oracle.oracle import Oracle
+        from tests.helpers import bits, small_config, x_bits
+        cfg = small_config()
+        L = 3
+        xb = x_bits(Oracle(), cfg, world)
+        xs = torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).cuda(rank)
+        full = [pkg.MoeLayer(cfg.desc(world), synthetic=cfg.synthetic(layer=l), device=rank, reserve_bytes=1 << 28)
+                for l in range(L)]
+        stack = pkg.MoeStack(full, max_tokens=world)
+        want = stack.forward(xs).cpu().numpy()[rank]
+        stack.close()
+        parts = [pkg.MoeLayer(cfg.desc(world, ep_rank=rank, ep_world=world), synthetic=cfg.synthetic(layer=l),
+                              device=rank, reserve_bytes=1 << 28) for l in range(L)]
+        group = ep.EpGroup(cfg.hidden, cfg.top_k, rank)
+        est = ep.EpStack(group, parts)
+        ok = True
+        for _ in range(2):  # two steps in a row: the exchange numbers advance in step on both ranks
+            got = est.forward(xs[rank:rank + 1]).cpu().numpy()[0]
+            ok = ok and np.array_equal(bits(got), bits(want))
+        est.status()
+        result = ok
+        if mode == "loss":
+            dist.barrier()  # both ranks are between steps
+            if rank == 1:
+                result = "left"  # rank 1 takes no further step
+            else:
+                xh = xs[0:1].cpu().pin_memory()
+                oh = torch.empty((1, cfg.hidden), dtype=torch.float32).pin_memory()
+                try:
+                    est.forward_host(xh, oh)
+                    result = "no error"
+                except pkg.umsx.UmsxError as e:
+                    result = "timeout" if e.status == pkg.umsx.ETIMEOUT else repr(e)
+            dist.barrier()
+        est.close()
+        group.close()
+        for l in parts + full:
+            l.close()
+        q.put((rank, result))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def _run_ep(mode):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_decode_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    return results
+
+
+def test_two_gpu_ep_decode_stack_bit_exact():
+    """Each rank holds half of every layer's experts and one token; the decode step's dispatch and
+    combine are P2P stores over NVLink inside the exchange kernels.  Every rank's token must come out
+    with the single-GPU stack's bits, on two steps in a row."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    assert _run_ep("exact") == {0: True, 1: True}
+
+
+def test_two_gpu_ep_rank_loss_reports_a_timeout():
+    """After two good steps rank 1 stops (between steps, nothing of it in flight); rank 0's next step
+    waits a bounded time (about a second) for the missing rows and reports UMSX_ETIMEOUT instead of
+    hanging."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    assert _run_ep("loss") == {0: "timeout", 1: "left"}

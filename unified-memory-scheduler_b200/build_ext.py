@@ -14,7 +14,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "..", "_build", "umsx")
 LIB = os.path.join(PKG, "libumsx.so")
-SOURCES = ["umsx_api.cu", "umsx_kernels.cu", "umsx_decode.cu", "umsx_gguf.cpp", "umsx_prefill.cu", "umsx_static.cu"]
+SOURCES = ["umsx_api.cu", "umsx_kernels.cu", "umsx_decode.cu", "umsx_gguf.cpp", "umsx_prefill.cu", "umsx_static.cu", "umsx_ep.cu"]
 HEADERS = ["umsx_internal.h", "umsx_device.cuh", "umsx_mx.cuh", "umsx_tc.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -1323,3 +1323,271 @@ umsx_status umsx_moe_create_gguf(const umsx_moe_desc *desc, const char *first_sh
 }
 
 }  // extern "C"
+
+// ============================================================================
+// Expert parallelism over NVLink: exchange buffers mapped between the ranks' processes with CUDA
+// IPC, and a stack of expert-parallel layers whose decode step exchanges hidden rows and job
+// outputs by P2P stores from inside its kernels (umsx_ep.cu).
+// ============================================================================
+
+struct umsx_ep {
+    int rank = 0, world = 1, device = 0, hidden = 0, top_k = 0;
+    uint8_t *buf = nullptr;  // h_all [world][H] f32 | y_recv [K][H] f32 | flags [world] u32 | epoch u32
+    size_t bytes = 0, off_y = 0, off_flags = 0, off_epoch = 0;
+    cudaIpcMemHandle_t handle{};
+    std::vector<uint8_t *> peers;  // each rank's buffer as mapped here (own entry = buf)
+    bool connected = false;
+    long long wait_cycles = 2000000000LL;  // about a second at 2 GHz
+};
+
+struct umsx_ep_stack {
+    umsx_ep *ep = nullptr;
+    std::vector<umsx_moe *> layers;
+    float eps = 1e-5f;
+    Workspace ws;
+    float *h_own = nullptr, *y_jobs = nullptr, *out_dev = nullptr;
+    void *x_dev = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    struct Graph { int dtype; cudaGraphExec_t exec; uint64_t kernels; };
+    std::vector<Graph> graphs;
+    std::mutex mu;
+};
+
+namespace {
+
+EpParams ep_params(umsx_ep_stack *st, const umsx_moe *m) {
+    const umsx_ep *ep = st->ep;
+    EpParams p{};
+    p.rank = ep->rank;
+    p.world = ep->world;
+    p.hidden = ep->hidden;
+    p.top_k = ep->top_k;
+    p.e_lo = m->e_lo;
+    p.e_local = m->e_local;
+    p.h_own = st->h_own;
+    for (int q = 0; q < ep->world; ++q) {
+        p.peer_h_all[q] = reinterpret_cast<float *>(ep->peers[q]);
+        p.peer_y_recv[q] = reinterpret_cast<float *>(ep->peers[q] + ep->off_y);
+        p.peer_flags[q] = reinterpret_cast<unsigned *>(ep->peers[q] + ep->off_flags);
+    }
+    p.flags = reinterpret_cast<unsigned *>(ep->buf + ep->off_flags);
+    p.epoch = reinterpret_cast<unsigned *>(ep->buf + ep->off_epoch);
+    p.y_recv = reinterpret_cast<const float *>(ep->buf + ep->off_y);
+    p.y_jobs = st->y_jobs;
+    p.ids = st->ws.disp.ids;
+    p.weights = st->ws.disp.weights;
+    p.err = st->ws.disp.err;
+    p.wait_cycles = ep->wait_cycles;
+    return p;
+}
+
+umsx_status record_ep_step(umsx_ep_stack *st, int dtype, cudaStream_t s) {
+    const int H = st->ep->hidden, G = st->ep->world;
+    if (dtype == UMSX_DTYPE_BF16)
+        UMSX_LAUNCHED(launch_bf16_to_f32(static_cast<const uint16_t *>(st->x_dev), st->h_own, (size_t)H, s));
+    else
+        UMSX_CUDA(cudaMemcpyAsync(st->h_own, st->x_dev, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
+    const float *h_all = reinterpret_cast<const float *>(st->ep->buf);
+    for (umsx_moe *m : st->layers) {
+        const EpParams p = ep_params(st, m);
+        UMSX_LAUNCHED(launch_ep_share(p, s));
+        // the replicated router (RMSNorm fused) and this rank's experts for all G tokens
+        if (umsx_status r = run_layer(m, st->ws, h_all, UMSX_DTYPE_F32, G, nullptr, nullptr, 1, st->eps, s, nullptr,
+                                      st->y_jobs))
+            return r;
+        UMSX_LAUNCHED(launch_ep_combine(p, s));
+    }
+    UMSX_CUDA(cudaMemcpyAsync(st->out_dev, st->h_own, (size_t)H * 4, cudaMemcpyDeviceToDevice, s));
+    return UMSX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+umsx_status umsx_ep_create(int rank, int world, int device, int hidden, int top_k, umsx_ep **out) {
+    if (!out) return fail(UMSX_EINVAL, "null output");
+    *out = nullptr;
+    if (world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world)
+        return fail(UMSX_EINVAL, "need 1 <= world <= 8 and 0 <= rank < world");
+    if (hidden <= 0 || hidden % 64 || top_k < 1 || top_k > 32) return fail(UMSX_EINVAL, "invalid hidden or top_k");
+    UMSX_CUDA(cudaSetDevice(device));
+    auto *ep = new umsx_ep();
+    ep->rank = rank;
+    ep->world = world;
+    ep->device = device;
+    ep->hidden = hidden;
+    ep->top_k = top_k;
+    ep->off_y = align_up((size_t)world * hidden * 4);
+    ep->off_flags = align_up(ep->off_y + (size_t)top_k * hidden * 4);
+    ep->off_epoch = ep->off_flags + (size_t)world * 4;
+    ep->bytes = align_up(ep->off_epoch + 4);
+    auto run = [&]() -> umsx_status {
+        UMSX_CUDA(cudaMalloc(&ep->buf, ep->bytes));
+        UMSX_CUDA(cudaMemset(ep->buf, 0, ep->bytes));
+        UMSX_CUDA(cudaIpcGetMemHandle(&ep->handle, ep->buf));
+        UMSX_CUDA(cudaDeviceSynchronize());
+        return UMSX_OK;
+    };
+    if (umsx_status r = run()) { umsx_ep_destroy(ep); return r; }
+    ep->peers.assign(world, nullptr);
+    ep->peers[rank] = ep->buf;
+    *out = ep;
+    return UMSX_OK;
+}
+
+umsx_status umsx_ep_handle(umsx_ep *ep, void *handle_out, size_t size) {
+    if (!ep || !handle_out || size != sizeof(cudaIpcMemHandle_t))
+        return fail(UMSX_EINVAL, "need the group and a buffer of the IPC handle size (64 bytes)");
+    std::memcpy(handle_out, &ep->handle, sizeof(cudaIpcMemHandle_t));
+    return UMSX_OK;
+}
+
+umsx_status umsx_ep_connect(umsx_ep *ep, const void *handles, size_t size) {
+    if (!ep || !handles || size != (size_t)ep->world * sizeof(cudaIpcMemHandle_t))
+        return fail(UMSX_EINVAL, "need every rank's IPC handle (world x 64 bytes, rank order)");
+    if (ep->connected) return fail(UMSX_EINVAL, "already connected");
+    UMSX_CUDA(cudaSetDevice(ep->device));
+    for (int q = 0; q < ep->world; ++q) {
+        if (q == ep->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)q * sizeof(h), sizeof(h));
+        void *p = nullptr;
+        UMSX_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        ep->peers[q] = static_cast<uint8_t *>(p);
+    }
+    ep->connected = true;
+    return UMSX_OK;
+}
+
+umsx_status umsx_ep_set_wait(umsx_ep *ep, int64_t wait_limit_cycles) {
+    if (!ep || wait_limit_cycles <= 0) return fail(UMSX_EINVAL, "need the group and a positive bound");
+    ep->wait_cycles = wait_limit_cycles;
+    return UMSX_OK;
+}
+
+void umsx_ep_destroy(umsx_ep *ep) {
+    if (!ep) return;
+    cudaSetDevice(ep->device);
+    cudaDeviceSynchronize();
+    for (int q = 0; q < (int)ep->peers.size(); ++q)
+        if (q != ep->rank && ep->peers[q]) cudaIpcCloseMemHandle(ep->peers[q]);
+    if (ep->buf) cudaFree(ep->buf);
+    delete ep;
+}
+
+umsx_status umsx_ep_stack_create(umsx_ep *ep, umsx_moe *const *layers, int n_layers, float rms_eps,
+                                 umsx_ep_stack **out) {
+    if (!out || !ep || !layers || n_layers <= 0) return fail(UMSX_EINVAL, "need a group and at least one layer");
+    *out = nullptr;
+    if (!ep->connected) return fail(UMSX_EINVAL, "connect the group first (umsx_ep_connect)");
+    const umsx_moe *l0 = layers[0];
+    for (int l = 0; l < n_layers; ++l) {
+        const umsx_moe *m = layers[l];
+        if (!m || m->device != ep->device || m->d.hidden != ep->hidden || m->d.top_k != ep->top_k ||
+            m->d.experts != l0->d.experts || m->d.intermediate != l0->d.intermediate)
+            return fail(UMSX_EINVAL, "layers must share the group's device, width and top_k, and one shape");
+        if (m->d.ep_world != ep->world || m->d.ep_rank != ep->rank)
+            return fail(UMSX_EINVAL, "layers must be created with the group's ep_rank and ep_world");
+    }
+    UMSX_CUDA(cudaSetDevice(ep->device));
+    auto *st = new umsx_ep_stack();
+    st->ep = ep;
+    st->layers.assign(layers, layers + n_layers);
+    st->eps = rms_eps;
+    const int G = ep->world, H = ep->hidden, K = ep->top_k;
+    auto run = [&]() -> umsx_status {
+        if (umsx_status r = alloc_workspace(st->ws, l0->d, l0->e_local, G, 0)) return r;
+        UMSX_CUDA(cudaMalloc(&st->h_own, (size_t)H * 4));
+        UMSX_CUDA(cudaMalloc(&st->out_dev, (size_t)H * 4));
+        UMSX_CUDA(cudaMalloc(&st->x_dev, (size_t)H * 4));
+        UMSX_CUDA(cudaMalloc(&st->y_jobs, (size_t)G * K * H * 4));
+        UMSX_CUDA(cudaMemset(st->y_jobs, 0, (size_t)G * K * H * 4));
+        UMSX_CUDA(cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking));
+        UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_in, cudaEventDisableTiming));
+        UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_out, cudaEventDisableTiming));
+        return UMSX_OK;
+    };
+    if (umsx_status r = run()) { umsx_ep_stack_destroy(st); return r; }
+    *out = st;
+    return UMSX_OK;
+}
+
+void umsx_ep_stack_destroy(umsx_ep_stack *st) {
+    if (!st) return;
+    cudaSetDevice(st->ep->device);
+    if (st->stream) cudaStreamSynchronize(st->stream);
+    for (auto &g : st->graphs) cudaGraphExecDestroy(g.exec);
+    if (st->ev_in) cudaEventDestroy(st->ev_in);
+    if (st->ev_out) cudaEventDestroy(st->ev_out);
+    if (st->stream) cudaStreamDestroy(st->stream);
+    for (void *p : {(void *)st->h_own, (void *)st->out_dev, st->x_dev, (void *)st->y_jobs, (void *)st->ws.mem})
+        if (p) cudaFree(p);
+    delete st;
+}
+
+}  // extern "C"
+
+namespace {
+umsx_status ep_stack_run(umsx_ep_stack *st, const void *x, int x_dtype, float *out, cudaMemcpyKind in_kind,
+                         cudaMemcpyKind out_kind, cudaStream_t caller) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    if (!x || !out) return fail(UMSX_EINVAL, "null buffer");
+    if (x_dtype != UMSX_DTYPE_F32 && x_dtype != UMSX_DTYPE_BF16) return fail(UMSX_EINVAL, "x_dtype must be F32 or BF16");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->ep->device));
+    const int H = st->ep->hidden;
+    UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
+    UMSX_CUDA(cudaStreamWaitEvent(st->stream, st->ev_in, 0));
+    UMSX_CUDA(cudaMemcpyAsync(st->x_dev, x, (size_t)H * (x_dtype == UMSX_DTYPE_BF16 ? 2 : 4), in_kind, st->stream));
+    umsx_ep_stack::Graph *g = nullptr;
+    for (auto &gg : st->graphs)
+        if (gg.dtype == x_dtype) g = &gg;
+    if (!g) {
+        const uint64_t before = g_launches;
+        UMSX_CUDA(cudaStreamBeginCapture(st->stream, cudaStreamCaptureModeThreadLocal));
+        umsx_status r = record_ep_step(st, x_dtype, st->stream);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(st->stream, &graph);
+        if (r) { if (graph) cudaGraphDestroy(graph); return r; }
+        if (e != cudaSuccess) return fail(UMSX_EDEVICE, std::string("ep capture: ") + cudaGetErrorString(e));
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) return fail(UMSX_EDEVICE, std::string("ep instantiate: ") + cudaGetErrorString(ie));
+        const uint64_t kernels = g_launches - before;
+        g_launches = before;
+        st->graphs.push_back({x_dtype, exec, kernels});
+        g = &st->graphs.back();
+    }
+    UMSX_CUDA(cudaGraphLaunch(g->exec, st->stream));
+    g_launches += g->kernels;
+    UMSX_CUDA(cudaMemcpyAsync(out, st->out_dev, (size_t)H * 4, out_kind, st->stream));
+    UMSX_CUDA(cudaEventRecord(st->ev_out, st->stream));
+    UMSX_CUDA(cudaStreamWaitEvent(caller, st->ev_out, 0));
+    return UMSX_OK;
+}
+}  // namespace
+
+extern "C" {
+
+umsx_status umsx_ep_stack_forward(umsx_ep_stack *st, const void *x, int x_dtype, float *out, umsx_stream stream) {
+    return ep_stack_run(st, x, x_dtype, out, cudaMemcpyDeviceToDevice, cudaMemcpyDeviceToDevice,
+                        static_cast<cudaStream_t>(stream));
+}
+
+umsx_status umsx_ep_stack_forward_host(umsx_ep_stack *st, const void *x, int x_dtype, float *out, umsx_stream stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (umsx_status r = ep_stack_run(st, x, x_dtype, out, cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost, s)) return r;
+    return check_device_flag(st->ws, s);
+}
+
+umsx_status umsx_ep_stack_status(umsx_ep_stack *st, umsx_stream stream) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    UMSX_CUDA(cudaSetDevice(st->ep->device));
+    UMSX_CUDA(cudaStreamSynchronize(st->stream));
+    return check_device_flag(st->ws, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -206,6 +206,29 @@ int launch_prefill_combine(const float *y, const float *w, const int32_t *inv, i
                            const float *extra, const float *residual, float *out, uint32_t *err, cudaStream_t s);
 int launch_moe_gemm(const MoeGemmParams &p, const void *act_hi, const void *act_lo, int rows_total, cudaStream_t s);
 
+// Expert-parallel exchange of a decode step (umsx_ep.cu): one token per rank, peers reached through
+// CUDA IPC mappings of their exchange buffers.
+constexpr int kEpMaxRanks = 8;
+
+struct EpParams {
+    int rank, world, hidden, top_k, e_lo, e_local;
+    float *h_own;                     // [H] this rank's token (its residual stream)
+    float *peer_h_all[kEpMaxRanks];   // each rank's h_all [world][H] (this rank's own entry included)
+    float *peer_y_recv[kEpMaxRanks];  // each rank's y_recv [K][H]
+    unsigned *peer_flags[kEpMaxRanks];  // each rank's flag array [world]
+    unsigned *flags;                  // this rank's flag array
+    unsigned *epoch;                  // this rank's exchange counter
+    const float *y_recv;              // this rank's y_recv
+    const float *y_jobs;              // [world][K][H] outputs of this rank's jobs
+    const int32_t *ids;               // [world][K] routing (replicated)
+    const float *weights;             // [world][K]
+    uint32_t *err;
+    long long wait_cycles;            // bound of every exchange wait
+};
+
+int launch_ep_share(const EpParams &p, cudaStream_t s);
+int launch_ep_combine(const EpParams &p, cudaStream_t s);
+
 // Thread-local status channel shared by every translation unit (umsx_api.cu).
 void record_error(const char *msg);      // the message umsx_last_error() returns
 void record_launches(uint64_t kernels);  // adds to umsx_kernel_launches()

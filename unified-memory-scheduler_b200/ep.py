@@ -97,3 +97,76 @@ class ExpertParallelLayer:
                 return torch.empty((0, self.layer.desc.hidden), dtype=torch.float32, device=x.device), (t0, t1)
             out = combine(mine, w[t0:t1].contiguous(), stream=s)
         return out, (t0, t1)
+
+
+# ---- decode over NVLink: the exchange inside the kernels ----------------------------------------
+
+IPC_HANDLE_BYTES = 64
+
+
+class EpGroup:
+    """This rank's exchange buffer, mapped into every other rank's process (umsx_ep_*).  The IPC
+    handles travel once, at set-up, over the process group (all_gather_object); after that the
+    decode steps exchange rows by P2P stores from inside the kernels, with no collective call."""
+
+    def __init__(self, hidden: int, top_k: int, device: int, group=None, wait_limit_cycles: int | None = None):
+        import ctypes as C
+
+        from .umsx import check, lib
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self._h = C.c_void_p()
+        L = lib()
+        check(L.umsx_ep_create(self.rank, self.world, device, hidden, top_k, C.byref(self._h)))
+        mine = (C.c_uint8 * IPC_HANDLE_BYTES)()
+        check(L.umsx_ep_handle(self._h, mine, IPC_HANDLE_BYTES))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(mine), group=group)
+        buf = (C.c_uint8 * (IPC_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
+        check(L.umsx_ep_connect(self._h, buf, IPC_HANDLE_BYTES * self.world))
+        if wait_limit_cycles:
+            check(L.umsx_ep_set_wait(self._h, int(wait_limit_cycles)))
+        dist.barrier(group=group)  # every rank is mapped before any step stores into a peer
+
+    def close(self):
+        from .umsx import lib
+        if self._h:
+            lib().umsx_ep_destroy(self._h)
+            self._h = None
+
+
+class EpStack:
+    """A decode stack split over the group by expert: h <- h + MoE_l(RMSNorm(h)) for one token per
+    rank (token g on rank g), each layer a handle created with ep_rank / ep_world of the group."""
+
+    def __init__(self, group: EpGroup, layers: list, rms_eps: float = 1e-5):
+        import ctypes as C
+
+        from .umsx import check, lib
+        self.group, self.layers = group, list(layers)
+        self.hidden = self.layers[0].desc.hidden
+        arr = (C.c_void_p * len(self.layers))(*[l._h for l in self.layers])
+        self._h = C.c_void_p()
+        check(lib().umsx_ep_stack_create(group._h, arr, len(self.layers), rms_eps, C.byref(self._h)))
+
+    def forward(self, x, out=None, stream=None):
+        """x: this rank's token [1, H] (CUDA, f32 or bf16) -> out [1, H] f32."""
+        from .umsx import _dtype_code, _ptr, _stream, check, lib
+        out = out if out is not None else torch.empty((1, self.hidden), dtype=torch.float32, device=x.device)
+        check(lib().umsx_ep_stack_forward(self._h, _ptr(x), _dtype_code(x), _ptr(out), _stream(stream)))
+        return out
+
+    def forward_host(self, x_host, out_host, stream=None):
+        from .umsx import _dtype_code, _ptr, _stream, check, lib
+        check(lib().umsx_ep_stack_forward_host(self._h, _ptr(x_host), _dtype_code(x_host), _ptr(out_host),
+                                               _stream(stream)))
+        return out_host
+
+    def status(self, stream=None):
+        from .umsx import _stream, check, lib
+        check(lib().umsx_ep_stack_status(self._h, _stream(stream)))
+
+    def close(self):
+        from .umsx import lib
+        if self._h:
+            lib().umsx_ep_stack_destroy(self._h)
+            self._h = None

@@ -35,7 +35,9 @@ EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "
            "umsx_combine",
            "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_create_mixed", "umsx_stack_destroy", "umsx_stack_forward",
            "umsx_stack_forward_host", "umsx_stack_status", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_stack_inject_fault",
-           "umsx_route_static",
+           "umsx_route_static", "umsx_ep_create", "umsx_ep_handle", "umsx_ep_connect", "umsx_ep_set_wait",
+           "umsx_ep_destroy", "umsx_ep_stack_create", "umsx_ep_stack_destroy", "umsx_ep_stack_forward",
+           "umsx_ep_stack_forward_host", "umsx_ep_stack_status",
            "umsx_gguf_load_experts", "umsx_gguf_experts_free", "umsx_moe_create_gguf",
            "umsx_kernel_launches", "umsx_last_error", "umsx_version"]
 
@@ -102,6 +104,16 @@ def lib():
         "umsx_stack_stage_times": (i32, [vp, C.POINTER(C.c_float), i32]),
         "umsx_stack_inject_fault": (i32, [vp, i32, C.c_int64]),
         "umsx_route_static": (i32, [vp, i32, i32, vp, vp, i32, i32, i32, i32, C.c_float, vp, vp, vp, vp]),
+        "umsx_ep_create": (i32, [i32, i32, i32, i32, i32, C.POINTER(vp)]),
+        "umsx_ep_handle": (i32, [vp, vp, sz]),
+        "umsx_ep_connect": (i32, [vp, vp, sz]),
+        "umsx_ep_set_wait": (i32, [vp, C.c_int64]),
+        "umsx_ep_destroy": (None, [vp]),
+        "umsx_ep_stack_create": (i32, [vp, C.POINTER(vp), i32, C.c_float, C.POINTER(vp)]),
+        "umsx_ep_stack_destroy": (None, [vp]),
+        "umsx_ep_stack_forward": (i32, [vp, vp, i32, vp, vp]),
+        "umsx_ep_stack_forward_host": (i32, [vp, vp, i32, vp, vp]),
+        "umsx_ep_stack_status": (i32, [vp, vp]),
         "umsx_gguf_load_experts": (i32, [C.c_char_p, i32, vp, i32, i32, C.POINTER(GgufExpertsC)]),
         "umsx_gguf_experts_free": (None, [C.POINTER(GgufExpertsC)]),
         "umsx_moe_create_gguf": (i32, [C.POINTER(Desc), C.c_char_p, i32, i32, sz, C.POINTER(vp)]),
