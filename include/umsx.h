@@ -110,6 +110,45 @@ void umsx_moe_destroy(umsx_moe *moe);
  * counterpart in the reference, which loads its router with the model). */
 umsx_status umsx_moe_set_router(umsx_moe *moe, const float *router_w, const float *router_b);
 
+/* Residency bank policies: the reference's VRAMBRIDGE_HYBRID_POLICY "lfu" and "lru"
+ * (hybrid patch :2384-2388). */
+enum { UMSX_BANK_LFU = 0, UMSX_BANK_LRU = 1 };
+#define UMSX_BANK_STATS 9
+
+/* A layer whose experts do not all stay on the device.  Replaces the reference's hybrid expert cache
+ * (llama_moe_cache, hybrid patch :2174-2294; admission :3086-3160; dispatch :3244-3266): every expert
+ * is kept in pinned HOST memory (copied from `weights`, which the caller may free afterwards); the
+ * device holds `slots` bank slots (1..E) plus min(E, max_tokens*k) transient slots.  Each
+ * umsx_moe_forward / umsx_moe_forward_host call routes on the device, reads the top-k back (one
+ * host synchronisation), lets the policy admit experts into the bank (one-token calls only, as the
+ * reference; batches look up), uploads admitted experts into their slots and the remaining misses
+ * into transient slots, and runs the same expert kernels as a resident layer: the output is
+ * bit-identical to umsx_moe_create's layer on the same weights (the reference computes misses on
+ * the CPU instead).  Policies:
+ *   UMSX_BANK_LFU  demand counts capped at 15, halved every window (2..5 bank-fulls of demands); an
+ *                  expert fills a free slot after 1 demand, replaces the least recently used resident
+ *                  (not selected by this dispatch) after 6 demands and with a strictly higher count;
+ *                  at most 4 admissions per dispatch;
+ *   UMSX_BANK_LRU  a miss takes a free slot or the least recently used resident's slot.
+ * ep_world must be 1.  Banked layers run through umsx_moe_forward(_host) only: stacks, EP stacks,
+ * forward_jobs, mul_mat_id, expert_down_q8 and export_expert return UMSX_EUNSUPPORTED. */
+umsx_status umsx_moe_create_banked(const umsx_moe_desc *desc, const umsx_moe_weights *weights, int slots,
+                                   int policy, int device, size_t reserve_bytes, umsx_moe **out);
+
+/* Counters of a banked layer (stats[UMSX_BANK_STATS], may be NULL): dispatches, demands (selected
+ * experts), hits, misses, admissions, evictions, transient uploads, LFU halvings, bytes uploaded
+ * (expert blocks).  slot_of_expert[E] (may be NULL): the bank slot of every expert, -1 if not
+ * resident.  Host-side state: no device synchronisation. */
+umsx_status umsx_moe_bank_stats(umsx_moe *moe, uint64_t *stats, int n, int32_t *slot_of_expert, int n_experts);
+
+/* The bank policy alone, on the host (no device): runs n_dispatches dispatches of `selected`
+ * (concatenated; counts[i] > 0 entries of a one-token dispatch in rank order, admission on;
+ * counts[i] < 0 for -counts[i] distinct experts of a batch, lookup only) and writes each selected
+ * expert's slot after its dispatch to slot_out (-1 = transient), and stats[UMSX_BANK_STATS]
+ * (bytes uploaded 0).  Used to test the policy against a restatement of the reference's rules. */
+umsx_status umsx_bank_simulate(int experts, int slots, int policy, int n_dispatches, const int32_t *counts,
+                               const int32_t *selected, int32_t *slot_out, uint64_t *stats);
+
 /* Whole layer, device buffers: out[T][H] = sum_r w[t,r] * expert(ids[t,r], x[t]) in rank order.
  * Replaces build_moe_ffn's expert branch + rank sum (hybrid patch :1394-1683, :1911-1916).
  * x is [T][H] fp32 or bf16 (x_dtype).  Optional ids/weights outputs may be NULL. */

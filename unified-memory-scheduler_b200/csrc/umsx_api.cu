@@ -13,6 +13,7 @@
 #include <string>
 #include <vector>
 
+#include "umsx_bank.h"
 #include "umsx_internal.h"
 
 using namespace umsx;
@@ -100,6 +101,18 @@ struct umsx_moe {
     uint8_t *weights_mem = nullptr;
     Workspace ws;
     std::mutex mu;
+    // Residency bank (umsx_moe_create_banked): the device planes hold bank_slots experts admitted by
+    // the policy plus bank_total - bank_slots transient slots for the misses of one call; every expert
+    // stays in pinned host memory (ggml blocks) and is uploaded on admission or on demand.
+    bool banked = false;
+    int bank_slots = 0, bank_total = 0;
+    umsx::BankPolicy *policy = nullptr;
+    uint8_t *host_blocks[3] = {};  // [E][per] ggml blocks: gate_up or gate, up (separate), down
+    size_t host_per[3] = {};
+    float *host_gu_bias = nullptr, *host_dn_bias = nullptr;  // [E][2I], [E][H] fp32
+    int32_t *d_map = nullptr;       // [E] expert -> device slot for the current call
+    uint8_t *bank_staging = nullptr;
+    uint64_t upload_bytes = 0;
 };
 
 namespace {
@@ -122,7 +135,7 @@ umsx_status validate_desc(const umsx_moe_desc *d) {
 
 size_t weight_bytes(const umsx_moe *m, Arena &a) {
     const auto &d = m->d;
-    const int H = d.hidden, I = d.intermediate, E = d.experts, EL = m->e_local;
+    const int H = d.hidden, I = d.intermediate, E = d.experts, EL = m->banked ? m->bank_total : m->e_local;
     a.take<float>((size_t)E * H);
     if (d.has_router_bias) a.take<float>(E);
     auto mat = [&](Matrix &mm, int rows, int cols) {
@@ -143,7 +156,7 @@ size_t weight_bytes(const umsx_moe *m, Arena &a) {
 
 void carve_weights(umsx_moe *m, Arena &a) {
     const auto &d = m->d;
-    const int H = d.hidden, I = d.intermediate, E = d.experts, EL = m->e_local;
+    const int H = d.hidden, I = d.intermediate, E = d.experts, EL = m->banked ? m->bank_total : m->e_local;
     m->router_w = a.take<float>((size_t)E * H);
     if (d.has_router_bias) m->router_b = a.take<float>(E);
     auto mat = [&](Matrix &mm, int rows, int cols) {
@@ -234,7 +247,7 @@ umsx_status allocate(umsx_moe *m, size_t reserve) {
     return alloc_workspace(m->ws, m->d, m->e_local, m->d.max_tokens, reserve);
 }
 
-umsx_status make_handle(const umsx_moe_desc *desc, int device, size_t reserve, umsx_moe **out) {
+umsx_status make_handle(const umsx_moe_desc *desc, int device, size_t reserve, umsx_moe **out, int bank_slots = 0) {
     if (!out) return fail(UMSX_EINVAL, "null output handle pointer");
     *out = nullptr;
     if (umsx_status s = validate_desc(desc)) return s;
@@ -244,6 +257,11 @@ umsx_status make_handle(const umsx_moe_desc *desc, int device, size_t reserve, u
     UMSX_CUDA(cudaSetDevice(device));
     auto *m = new umsx_moe();
     m->d = *desc;
+    if (bank_slots > 0) {
+        m->banked = true;
+        m->bank_slots = bank_slots;
+        m->bank_total = bank_slots + std::min(desc->experts, desc->max_tokens * desc->top_k);
+    }
     if (m->d.ep_world <= 0) m->d.ep_world = 1;
     m->device = device;
     m->e_local = desc->experts / m->d.ep_world;
@@ -327,6 +345,99 @@ umsx_status umsx_moe_create(const umsx_moe_desc *desc, const umsx_moe_weights *w
         }
     }
     return create_from_host(desc, w, gb.data(), db.data(), device, reserve_bytes, out);
+}
+
+umsx_status umsx_moe_create_banked(const umsx_moe_desc *desc, const umsx_moe_weights *w, int slots, int policy,
+                                   int device, size_t reserve_bytes, umsx_moe **out) {
+    if (out) *out = nullptr;
+    if (!w || !w->router_w || !w->down || (desc && desc->fused_gate_up ? !w->gate_up : (!w->gate || !w->up)))
+        return fail(UMSX_EINVAL, "missing router, gate/up or down weights");
+    if (desc && desc->has_router_bias && !w->router_b) return fail(UMSX_EINVAL, "has_router_bias set but router_b is null");
+    if (desc && desc->has_bias && (!w->gate_up_bias || !w->down_bias)) return fail(UMSX_EINVAL, "has_bias set but biases are null");
+    if (policy != UMSX_BANK_LFU && policy != UMSX_BANK_LRU) return fail(UMSX_EINVAL, "unknown bank policy");
+    if (desc && desc->ep_world > 1) return fail(UMSX_EINVAL, "a banked layer holds every expert of its layer (ep_world 1)");
+    if (!desc || slots < 1 || slots > desc->experts) return fail(UMSX_EINVAL, "bank slots must be in [1, experts]");
+    umsx_moe *m = nullptr;
+    if (umsx_status s = make_handle(desc, device, reserve_bytes, &m, slots)) return s;
+    const auto &d = m->d;
+    const size_t H = d.hidden, I = d.intermediate, E = d.experts;
+    auto run = [&]() -> umsx_status {
+        UMSX_CUDA(cudaMemcpy(m->router_w, w->router_w, E * H * sizeof(float), cudaMemcpyHostToDevice));
+        if (d.has_router_bias) UMSX_CUDA(cudaMemcpy(m->router_b, w->router_b, E * sizeof(float), cudaMemcpyHostToDevice));
+        const void *src[3] = {d.fused_gate_up ? w->gate_up : w->gate, d.fused_gate_up ? nullptr : w->up, w->down};
+        const Matrix *mats[3] = {d.fused_gate_up ? &m->gate_up : &m->gate, &m->up, &m->down};
+        for (int i = 0; i < 3; ++i) {
+            if (!src[i]) continue;
+            m->host_per[i] = (size_t)mats[i]->rows * (mats[i]->cols / 32) * block_bytes(d.quant);
+            UMSX_CUDA(cudaMallocHost(&m->host_blocks[i], E * m->host_per[i]));
+            std::memcpy(m->host_blocks[i], src[i], E * m->host_per[i]);
+        }
+        if (d.has_bias) {  // bf16 biases widened (exact)
+            UMSX_CUDA(cudaMallocHost(&m->host_gu_bias, E * 2 * I * 4));
+            UMSX_CUDA(cudaMallocHost(&m->host_dn_bias, E * H * 4));
+            for (size_t i = 0; i < E * 2 * I; ++i) {
+                const uint32_t bits = (uint32_t)w->gate_up_bias[i] << 16;
+                std::memcpy(&m->host_gu_bias[i], &bits, 4);
+            }
+            for (size_t i = 0; i < E * H; ++i) {
+                const uint32_t bits = (uint32_t)w->down_bias[i] << 16;
+                std::memcpy(&m->host_dn_bias[i], &bits, 4);
+            }
+        }
+        UMSX_CUDA(cudaMalloc(&m->bank_staging, max_expert_bytes(m)));
+        UMSX_CUDA(cudaMalloc(&m->d_map, E * sizeof(int32_t)));
+        m->policy = new BankPolicy((int)E, slots, policy == UMSX_BANK_LFU ? kBankLfu : kBankLru);
+        UMSX_CUDA(cudaDeviceSynchronize());
+        return UMSX_OK;
+    };
+    if (umsx_status st = run()) { umsx_moe_destroy(m); return st; }
+    *out = m;
+    return UMSX_OK;
+}
+
+umsx_status umsx_moe_bank_stats(umsx_moe *m, uint64_t *stats, int n, int32_t *slot_of_expert, int n_experts) {
+    if (!m || !m->banked) return fail(UMSX_EINVAL, "not a banked layer");
+    if ((stats && n < UMSX_BANK_STATS) || (slot_of_expert && n_experts < m->d.experts))
+        return fail(UMSX_EINVAL, "output arrays too small");
+    std::lock_guard<std::mutex> lock(m->mu);
+    if (stats) {
+        const BankStats &b = m->policy->stats();
+        const uint64_t v[UMSX_BANK_STATS] = {b.dispatches, b.demands, b.hits, b.misses, b.admissions,
+                                             b.evictions, b.transient, b.halvings, m->upload_bytes};
+        std::memcpy(stats, v, sizeof(v));
+    }
+    if (slot_of_expert)
+        for (int e = 0; e < m->d.experts; ++e) slot_of_expert[e] = m->policy->slot_of(e);
+    return UMSX_OK;
+}
+
+umsx_status umsx_bank_simulate(int experts, int slots, int policy, int n_dispatches, const int32_t *counts,
+                               const int32_t *selected, int32_t *slot_out, uint64_t *stats) {
+    if (experts < 1 || slots < 1 || slots > experts || n_dispatches < 0 || (n_dispatches && (!counts || !selected)))
+        return fail(UMSX_EINVAL, "bad bank simulation arguments");
+    if (policy != UMSX_BANK_LFU && policy != UMSX_BANK_LRU) return fail(UMSX_EINVAL, "unknown bank policy");
+    BankPolicy bank(experts, slots, policy == UMSX_BANK_LFU ? kBankLfu : kBankLru);
+    std::vector<std::pair<int, int>> admitted;
+    std::vector<int> evicted;
+    size_t at = 0;
+    for (int i = 0; i < n_dispatches; ++i) {
+        if (counts[i] == 0) return fail(UMSX_EINVAL, "empty dispatch");
+        // counts[i] > 0: one token's top-k (admission); counts[i] < 0: the distinct experts of a batch
+        const int c = counts[i] < 0 ? -counts[i] : counts[i];
+        std::vector<int> sel(selected + at, selected + at + c);
+        for (int e : sel)
+            if (e < 0 || e >= experts) return fail(UMSX_EINVAL, "expert index out of range");
+        const std::vector<int> sl = bank.dispatch(sel, admitted, evicted, counts[i] > 0);
+        if (slot_out) std::copy(sl.begin(), sl.end(), slot_out + at);
+        at += c;
+    }
+    if (stats) {
+        const BankStats &b = bank.stats();
+        const uint64_t v[UMSX_BANK_STATS] = {b.dispatches, b.demands, b.hits, b.misses, b.admissions,
+                                             b.evictions, b.transient, b.halvings, 0};
+        std::memcpy(stats, v, sizeof(v));
+    }
+    return UMSX_OK;
 }
 
 }  // extern "C"
@@ -415,6 +526,13 @@ void umsx_moe_destroy(umsx_moe *m) {
     cudaDeviceSynchronize();
     if (m->weights_mem) cudaFree(m->weights_mem);
     if (m->ws.mem) cudaFree(m->ws.mem);
+    for (uint8_t *p : m->host_blocks)
+        if (p) cudaFreeHost(p);
+    if (m->host_gu_bias) cudaFreeHost(m->host_gu_bias);
+    if (m->host_dn_bias) cudaFreeHost(m->host_dn_bias);
+    if (m->d_map) cudaFree(m->d_map);
+    if (m->bank_staging) cudaFree(m->bank_staging);
+    delete m->policy;
     delete m;
 }
 
@@ -469,7 +587,7 @@ umsx_status mark(cudaEvent_t ev, cudaStream_t s) {
 // fused-gate_up layer with all experts local and the token count is small.
 bool decode_eligible(const umsx_moe *m, int tokens, int n_layers) {
     const auto &d = m->d;
-    return d.quant == UMSX_QUANT_MXFP4 && d.fused_gate_up && m->e_local == d.experts &&
+    return !m->banked && d.quant == UMSX_QUANT_MXFP4 && d.fused_gate_up && m->e_local == d.experts &&
            decode_supported(tokens, d.hidden, d.intermediate, d.experts, d.top_k, n_layers);
 }
 
@@ -669,12 +787,13 @@ static int per_stage_chunk(int tokens, int top_k, int experts) {
 
 umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
                       const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
-                      float *y_jobs = nullptr, const float *extra = nullptr) {
+                      float *y_jobs = nullptr, const float *extra = nullptr, bool router_done = false) {
     const auto &d = m->d;
-    if (prefill_eligible(m, ws, tokens))
+    if (!m->banked && prefill_eligible(m, ws, tokens))
         return run_prefill(m, ws, x, x_dtype, tokens, out, residual, rmsnorm, eps, s, ev, y_jobs, extra);
     if (ev) if (umsx_status st = mark(ev[0], s)) return st;
-    if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s, 1)) return st;
+    if (!router_done)
+        if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, rmsnorm, eps, s, 1)) return st;
     if (ev) if (umsx_status st = mark(ev[1], s)) return st;
     const int slots = std::min(m->e_local, tokens * d.top_k);
     GateUpParams g{};
@@ -726,7 +845,65 @@ umsx_status run_layer(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, in
     return UMSX_OK;
 }
 
+// Uploads expert e's ggml blocks (through the staging buffer, repacked in place) and biases into
+// device slot `slot`, ordered on s.
+umsx_status bank_upload(umsx_moe *m, int e, int slot, cudaStream_t s) {
+    Matrix *mats[3] = {m->d.fused_gate_up ? &m->gate_up : &m->gate, m->d.fused_gate_up ? nullptr : &m->up, &m->down};
+    for (int i = 0; i < 3; ++i) {
+        if (!mats[i]) continue;
+        UMSX_CUDA(cudaMemcpyAsync(m->bank_staging, m->host_blocks[i] + (size_t)e * m->host_per[i], m->host_per[i],
+                                  cudaMemcpyHostToDevice, s));
+        UMSX_LAUNCHED(launch_repack(*mats[i], slot, m->bank_staging, s));
+        m->upload_bytes += m->host_per[i];
+    }
+    const size_t I = m->d.intermediate, H = m->d.hidden;
+    if (m->d.has_bias) {
+        UMSX_CUDA(cudaMemcpyAsync(m->gu_bias + (size_t)slot * 2 * I, m->host_gu_bias + (size_t)e * 2 * I, 2 * I * 4,
+                                  cudaMemcpyHostToDevice, s));
+        UMSX_CUDA(cudaMemcpyAsync(m->down_bias + (size_t)slot * H, m->host_dn_bias + (size_t)e * H, H * 4,
+                                  cudaMemcpyHostToDevice, s));
+    }
+    return UMSX_OK;
+}
+
+// A banked layer's call: route on the device, read the routing back, let the policy admit experts
+// into the bank (one-token calls) or look them up (several tokens), upload the admitted experts into
+// their slots and the other missing ones into transient slots, point the dispatch's slot records at
+// the device slots, then run the expert kernels.  The call synchronises with the host twice (after
+// routing, and before its host vectors go out of scope).
+umsx_status run_banked(umsx_moe *m, const void *x, int x_dtype, int tokens, float *out, cudaStream_t s) {
+    const int K = m->d.top_k, E = m->d.experts;
+    Workspace &ws = m->ws;
+    if (umsx_status st = run_router(m, ws, x, x_dtype, tokens, 0, 0.0f, s, 1)) return st;
+    std::vector<int32_t> ids((size_t)tokens * K);
+    UMSX_CUDA(cudaMemcpyAsync(ids.data(), ws.disp.ids, ids.size() * 4, cudaMemcpyDeviceToHost, s));
+    UMSX_CUDA(cudaStreamSynchronize(s));
+    std::vector<int> selected;
+    std::vector<char> seen(E, 0);
+    for (int32_t e : ids) {
+        if (e < 0 || e >= E) return fail(UMSX_EDEVICE, "routing produced an expert index out of range");
+        if (!seen[e]) { seen[e] = 1; selected.push_back(e); }
+    }
+    std::vector<std::pair<int, int>> admitted;
+    std::vector<int> evicted;
+    const std::vector<int> slot = m->policy->dispatch(selected, admitted, evicted, tokens == 1);
+    for (const auto &a : admitted)
+        if (umsx_status st = bank_upload(m, a.first, a.second, s)) return st;
+    std::vector<int32_t> map(E, -1);
+    int transient = m->bank_slots;
+    for (size_t i = 0; i < selected.size(); ++i) {
+        if (slot[i] >= 0) { map[selected[i]] = slot[i]; continue; }
+        map[selected[i]] = transient;
+        if (umsx_status st = bank_upload(m, selected[i], transient++, s)) return st;
+    }
+    UMSX_CUDA(cudaMemcpyAsync(m->d_map, map.data(), (size_t)E * 4, cudaMemcpyHostToDevice, s));
+    UMSX_LAUNCHED(launch_bank_remap(ws.disp.slots, m->d_map, std::min(E, tokens * K), s));
+    UMSX_CUDA(cudaStreamSynchronize(s));  // the pageable sources above are read before they go out of scope
+    return run_layer(m, ws, x, x_dtype, tokens, out, nullptr, 0, 0.0f, s, nullptr, nullptr, nullptr, true);
+}
+
 umsx_status forward_layer(umsx_moe *m, const void *x, int x_dtype, int tokens, float *out, cudaStream_t s) {
+    if (m->banked) return run_banked(m, x, x_dtype, tokens, out, s);
     if (decode_eligible(m, tokens, 1)) {
         DecodeParams p = decode_params(m, m->ws, x, x_dtype, tokens, out);
         p.ids_out = m->ws.disp.ids;
@@ -759,6 +936,7 @@ umsx_status umsx_moe_forward(umsx_moe *m, const void *x, int x_dtype, int tokens
 umsx_status umsx_moe_forward_jobs(umsx_moe *m, const void *x, int x_dtype, int tokens, int32_t *ids, float *weights,
                                   float *y, umsx_stream stream) {
     if (umsx_status st = check_call(m, x, x_dtype, tokens, m ? m->d.max_tokens : 0)) return st;
+    if (m->banked) return fail(UMSX_EUNSUPPORTED, "banked layer: call umsx_moe_forward or umsx_moe_forward_host");
     if (!y || reinterpret_cast<uintptr_t>(y) % 16) return fail(UMSX_EINVAL, "y must be a 16-byte aligned device buffer");
     std::lock_guard<std::mutex> lock(m->mu);
     UMSX_CUDA(cudaSetDevice(m->device));
@@ -823,6 +1001,7 @@ umsx_status umsx_route(umsx_moe *m, const void *x, int x_dtype, int tokens, int3
 umsx_status umsx_expert_down_q8(umsx_moe *m, const void *packed_q8, const int32_t *experts, int jobs, float *out,
                                 umsx_stream stream) {
     if (!m) return fail(UMSX_EINVAL, "null handle");
+    if (m->banked) return fail(UMSX_EUNSUPPORTED, "banked layer: call umsx_moe_forward or umsx_moe_forward_host");
     if (jobs < 0 || jobs > m->d.max_tokens * m->d.top_k) return fail(UMSX_EINVAL, "invalid packed Q8 input shape");
     if (jobs == 0) return UMSX_OK;
     if (!packed_q8 || !experts || !out) return fail(UMSX_EINVAL, "null buffer");
@@ -879,6 +1058,7 @@ static const Matrix *projection(umsx_moe *m, int proj) {
 umsx_status umsx_mul_mat_id(umsx_moe *m, int proj, const float *b, int n_b, const int32_t *ids, int n_ids, int tokens,
                             float *dst, umsx_stream stream) {
     if (!m || !b || !ids || !dst) return fail(UMSX_EINVAL, "null argument");
+    if (m->banked) return fail(UMSX_EUNSUPPORTED, "banked layer: call umsx_moe_forward or umsx_moe_forward_host");
     if (tokens <= 0 || n_ids <= 0 || n_ids > m->d.experts || (n_b != 1 && n_b != n_ids) ||
         (size_t)tokens * n_ids > (size_t)m->d.max_tokens * m->d.top_k)
         return fail(UMSX_EINVAL, "invalid MUL_MAT_ID shape");
@@ -912,6 +1092,7 @@ umsx_status umsx_combine(const float *y, const float *weights, int tokens, int t
 
 umsx_status umsx_moe_export_expert(umsx_moe *m, int proj, int expert, void *host_out, size_t size) {
     if (!m || !host_out) return fail(UMSX_EINVAL, "null argument");
+    if (m->banked) return fail(UMSX_EUNSUPPORTED, "banked layer: call umsx_moe_forward or umsx_moe_forward_host");
     const Matrix *mat = projection(m, proj);
     if (!mat) return fail(UMSX_EINVAL, "projection not present in this layer");
     if (!resident(m, expert)) return fail(UMSX_ENOTRESIDENT, "expert out of range or not resident");
@@ -1086,6 +1267,7 @@ umsx_status stack_create(umsx_moe *const *layers, umsx_moe *const *shared, int n
             return fail(UMSX_EUNSUPPORTED, "a stack runs whole layers; expert-parallel handles use umsx_moe_forward_jobs");
         widen(m);
         const umsx_moe *sh = shared ? shared[l] : nullptr;
+        if (m->banked || (sh && sh->banked)) return fail(UMSX_EUNSUPPORTED, "banked layer: call umsx_moe_forward or umsx_moe_forward_host");
         if (sh) {
             if (sh->device != l0->device || sh->d.hidden != l0->d.hidden || sh->d.experts != 1 || sh->d.top_k != 1)
                 return fail(UMSX_EINVAL, "a shared-expert handle is a one-expert top-1 layer of the stack's width and device");
@@ -1490,6 +1672,7 @@ umsx_status umsx_ep_stack_create(umsx_ep *ep, umsx_moe *const *layers, int n_lay
             return fail(UMSX_EINVAL, "layers must share the group's device, width and top_k, and one shape");
         if (m->d.ep_world != ep->world || m->d.ep_rank != ep->rank)
             return fail(UMSX_EINVAL, "layers must be created with the group's ep_rank and ep_world");
+        if (m->banked) return fail(UMSX_EUNSUPPORTED, "banked layer: call umsx_moe_forward or umsx_moe_forward_host");
     }
     UMSX_CUDA(cudaSetDevice(ep->device));
     auto *st = new umsx_ep_stack();

@@ -244,6 +244,7 @@ int launch_gemv(const GemvParams &p, const Dispatch &d, int max_slots, int max_p
 int launch_combine(const float *y, const float *w, int tokens, int top_k, int width, const float *extra,
                    const float *residual, float *out, uint32_t *err, cudaStream_t s);
 int launch_repack(const Matrix &m, int expert, const uint8_t *ggml, cudaStream_t s);
+int launch_bank_remap(int4 *slots, const int32_t *map, int n, cudaStream_t s);
 int launch_export(const Matrix &m, int expert, uint8_t *ggml, cudaStream_t s);
 int launch_gen_blocks(int quant, uint64_t seed, uint64_t stream, uint64_t first_block, uint64_t nblocks,
                       uint8_t *out, cudaStream_t s);

@@ -1402,4 +1402,21 @@ int launch_bf16_to_f32(const uint16_t *in, float *out, size_t n, cudaStream_t s)
     return 1;
 }
 
+// Points the slot records of a banked layer's dispatch at device bank slots: rec.x (an expert index)
+// becomes map[rec.x]; records past the last active one (rec.x < 0) stay as they are.
+__global__ void k_bank_remap(int4 *slots, const int32_t *map, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int4 rec = slots[i];
+    if (rec.x >= 0) {
+        rec.x = map[rec.x];
+        slots[i] = rec;
+    }
+}
+
+int launch_bank_remap(int4 *slots, const int32_t *map, int n, cudaStream_t s) {
+    k_bank_remap<<<(n + 127) / 128, 128, 0, s>>>(slots, map, n);
+    return 1;
+}
+
 }  // namespace umsx

@@ -26,11 +26,15 @@ QUANT_Q8_0, QUANT_MXFP4 = 8, 39
 ROUTE_TOPK_SOFTMAX, ROUTE_SOFTMAX_TOPK_NORM, ROUTE_SOFTMAX_TOPK = 0, 1, 2
 ACT_SILU, ACT_SWIGLU_OAI = 0, 1
 DTYPE_F32, DTYPE_BF16 = 0, 1
+BANK_LFU, BANK_LRU = 0, 1
+BANK_STAT_NAMES = ("dispatches", "demands", "hits", "misses", "admissions", "evictions", "transient", "halvings",
+                   "upload_bytes")
 PROJ_GATE_UP, PROJ_GATE, PROJ_UP, PROJ_DOWN = 0, 1, 2, 3
 BLOCK_BYTES = {QUANT_Q8_0: 34, QUANT_MXFP4: 17}
 
 # exported symbols of include/umsx.h (the tests check each one is present)
 EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "umsx_moe_set_router", "umsx_moe_forward",
+           "umsx_moe_create_banked", "umsx_moe_bank_stats", "umsx_bank_simulate",
            "umsx_moe_forward_host", "umsx_moe_forward_jobs", "umsx_moe_status", "umsx_route", "umsx_expert_down_q8", "umsx_mul_mat_id",
            "umsx_combine",
            "umsx_moe_export_expert", "umsx_stack_create", "umsx_stack_create_mixed", "umsx_stack_destroy", "umsx_stack_forward",
@@ -84,6 +88,9 @@ def lib():
         "umsx_moe_create_synthetic": (i32, [C.POINTER(Desc), u64, C.c_uint32, C.c_float, C.c_float, C.c_float, i32, sz,
                                             C.POINTER(vp)]),
         "umsx_moe_destroy": (None, [vp]),
+        "umsx_moe_create_banked": (i32, [C.POINTER(Desc), C.POINTER(Weights), i32, i32, i32, sz, C.POINTER(vp)]),
+        "umsx_moe_bank_stats": (i32, [vp, vp, i32, vp, i32]),
+        "umsx_bank_simulate": (i32, [i32, i32, i32, i32, vp, vp, vp, vp]),
         "umsx_moe_set_router": (i32, [vp, vp, vp]),
         "umsx_moe_forward": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "umsx_moe_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
@@ -162,6 +169,24 @@ def _dtype_code(t):
     raise UmsxError(EINVAL, f"x must be float32 or bfloat16, got {t.dtype}")
 
 
+def bank_simulate(experts: int, slots: int, policy: int, dispatches):
+    """Runs the bank policy alone on the host (umsx_bank_simulate).  `dispatches` is a list of
+    (expert list, admit) pairs: admit=True for a one-token dispatch (its top-k in rank order),
+    False for a batch's distinct experts (lookup).  Returns (slots per dispatch, stats dict)."""
+    import numpy as np
+    counts = np.array([len(sel) if admit else -len(sel) for sel, admit in dispatches], dtype=np.int32)
+    flat = np.array([e for sel, _ in dispatches for e in sel], dtype=np.int32)
+    out = np.full(len(flat), -2, dtype=np.int32)
+    st = np.zeros(len(BANK_STAT_NAMES), dtype=np.uint64)
+    check(lib().umsx_bank_simulate(experts, slots, policy, len(dispatches), _np_ptr(counts), _np_ptr(flat),
+                                   _np_ptr(out), _np_ptr(st)))
+    res, at = [], 0
+    for sel, _ in dispatches:
+        res.append(out[at:at + len(sel)].tolist())
+        at += len(sel)
+    return res, {k: int(v) for k, v in zip(BANK_STAT_NAMES, st)}
+
+
 def combine(y, weights, out=None, stream=None):
     """out[t] = sum_r w[t,r] * y[t,r] in rank order (y: [T,K,W] f32 CUDA, weights [T,K])."""
     import torch
@@ -224,7 +249,9 @@ class MoeLayer:
     """One MoE layer resident on a GPU (the handle owns the repacked expert weights)."""
 
     def __init__(self, desc: Desc, weights: dict | None = None, *, synthetic: dict | None = None,
-                 gguf: tuple | None = None, device: int = 0, reserve_bytes: int = 1 << 30):
+                 gguf: tuple | None = None, bank: tuple | None = None, device: int = 0, reserve_bytes: int = 1 << 30):
+        """bank = (slots, BANK_LFU | BANK_LRU) with host `weights`: a banked layer (umsx_moe_create_banked)
+        whose experts live in pinned host memory and enter `slots` device slots by the policy."""
         self.desc = desc
         self.device = device
         self._h = C.c_void_p()
@@ -243,7 +270,11 @@ class MoeLayer:
             self._keep = w  # host arrays must stay alive during create
             ws = Weights(*[_np_ptr(w.get(k)) for k in ("router_w", "router_b", "gate_up", "gate", "up", "down",
                                                       "gate_up_bias", "down_bias")])
-            check(L.umsx_moe_create(C.byref(desc), C.byref(ws), device, reserve_bytes, C.byref(self._h)))
+            if bank is not None:
+                check(L.umsx_moe_create_banked(C.byref(desc), C.byref(ws), int(bank[0]), int(bank[1]), device,
+                                               reserve_bytes, C.byref(self._h)))
+            else:
+                check(L.umsx_moe_create(C.byref(desc), C.byref(ws), device, reserve_bytes, C.byref(self._h)))
             self._keep = None
 
     def close(self):
@@ -291,6 +322,17 @@ class MoeLayer:
         w = np.ascontiguousarray(router_w, dtype=np.float32)
         b = None if router_b is None else np.ascontiguousarray(router_b, dtype=np.float32)
         check(lib().umsx_moe_set_router(self._h, _np_ptr(w), _np_ptr(b)))
+
+    def bank_stats(self):
+        """Counters of a banked layer (umsx_moe_bank_stats): a dict of BANK_STAT_NAMES, plus
+        "slot_of_expert" (int32 [E], -1 where not resident)."""
+        import numpy as np
+        st = np.zeros(len(BANK_STAT_NAMES), dtype=np.uint64)
+        slots = np.zeros(self.desc.experts, dtype=np.int32)
+        check(lib().umsx_moe_bank_stats(self._h, _np_ptr(st), len(st), _np_ptr(slots), len(slots)))
+        d = {k: int(v) for k, v in zip(BANK_STAT_NAMES, st)}
+        d["slot_of_expert"] = slots
+        return d
 
     def status(self, stream=None):
         """Raises UmsxError (ENONFINITE / ETIMEOUT) for what the handle's earlier calls on the stream
