@@ -21,11 +21,11 @@ reference's own CPU implementation of the path (tools/trace/exact_packed_cpu.h
 packed MXFP4 GEMV compiled from the reference sources into oracle/_ref/) on
 this host's cores, on rank 0 only.
 
-`--ep` (prefill) splits every layer's experts over the N ranks instead (expert parallelism,
-unified-memory-scheduler_b200/ep.py): all ranks see the same T tokens, each runs its experts'
-jobs, one NCCL all-to-all per layer brings the job outputs to the token's rank, which combines
-them; an all-gather then gives every rank the next layer's input (RMSNorm in torch between
-layers).  Total work is fixed as N grows (strong scaling).
+`--ep` (prefill, T tokens split T/N per rank) splits every layer's experts over the N ranks
+(ep.EpPrefill): per layer the token rows travel to the experts' ranks and the outputs come back as
+P2P NVLink stores inside the exchange kernels; with `--config skew` it runs configs[3] (Qwen3-30B-A3B
+shapes, Zipf(1.2) router bias) and reports every GPU's rows and jobs per layer.  Total work is
+fixed as N grows (strong scaling).
 """
 from __future__ import annotations
 
@@ -731,7 +731,15 @@ def skew_arm(a):
 
 
 def ep_arm(a):
-    """Expert-parallel prefill: every layer's experts split over the ranks (see the module docstring)."""
+    """Expert-parallel prefill (--ep): every layer's experts split over the N ranks (rank g holds
+    [g*E/N, (g+1)*E/N)), the step's T tokens split over the ranks (T/N each, strong scaling), the
+    token rows sent to the experts' ranks and the outputs returned as P2P NVLink stores inside the
+    exchange kernels (ep.EpPrefill); no collective carries layer data.  --config stack: the
+    GPT-OSS-120B-shaped stack; --config skew: configs[3] (Qwen3-30B-A3B shapes with the Zipf(1.2) router
+    bias, Q8_0 headline and MXFP4 sub-record), with every rank's rows and jobs per layer (the per-GPU
+    load the skew produces) and p50 / p99 step latency.  Before timing, rank 0 recomputes the first
+    layers on one GPU with whole layers for every rank's tokens: the bits must agree (parity_ok)."""
+    import dataclasses
     import datetime
     import importlib
 
@@ -747,93 +755,154 @@ def ep_arm(a):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     pkg = load_pkg()
     ep = importlib.import_module(pkg.__name__ + ".ep")
-    cfg = pkg.configs.GPT_OSS_120B
-    if a.experts:
-        import dataclasses
-        cfg = dataclasses.replace(cfg, experts=a.experts)
-    T, H = a.tokens, cfg.hidden
+    T = a.tokens if a.tokens and a.tokens > 1 else 4096
     if T % world:
         raise SystemExit("--ep needs tokens divisible by the number of GPUs")
-    layers = [pkg.MoeLayer(cfg.desc(max_tokens=T, ep_rank=rank, ep_world=world), synthetic=cfg.synthetic(layer=l),
-                           device=dev.index, reserve_bytes=2 << 30) for l in range(a.layers)]
-    epl = [ep.ExpertParallelLayer(l) for l in layers]
-    pool = 4
-    rng = np.random.default_rng(1000)  # the same tokens on every rank
-    xs = torch.from_numpy(rng.standard_normal((pool, T, H)).astype(np.float32))
-    xs_dev = xs.to(dev)
-    full = torch.empty((T, H), dtype=torch.float32, device=dev)
-    yjobs = torch.zeros((T, cfg.top_k, H), dtype=torch.float32, device=dev)
+    Tr = T // world
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if a.config == "skew":
+        names, n_layers = ["qwen3-skew-q8_0", "qwen3-skew-mxfp4"], a.layers if a.layers != 36 else 1
+    else:
+        names, n_layers = ["gpt-oss-120b"], a.layers
     stream = torch.cuda.current_stream(dev)
+    records = {}
+    parity_ok = True
+    for name in names:
+        cfg = pkg.configs.CONFIGS[name] if name in pkg.configs.CONFIGS else pkg.configs.GPT_OSS_120B
+        if a.experts:
+            cfg = dataclasses.replace(cfg, experts=a.experts)
+        H, K = cfg.hidden, cfg.top_k
+        router = None
+        if a.config == "skew":
+            from oracle.oracle import Oracle  # the host twin of the device router weights (generator only)
+            rw = Oracle().gen_normal_f32(cfg.seed, pkg.configs.stream_id(0, pkg.configs.KIND_ROUTER_W), 0,
+                                         cfg.experts * H, cfg.router_sigma).reshape(cfg.experts, H)
+            router = (rw, pkg.configs.zipf_router_bias(cfg.experts, seed=cfg.seed))
 
-    def step(x):
-        h = x
-        for layer in epl:
-            xn = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5)
-            mine, _ = layer.forward(xn, y=yjobs)
-            dist.all_gather_into_tensor(full, mine)
-            h = h + full
-        return h
+        def make(l, **kw):
+            m = pkg.MoeLayer(cfg.desc(max_tokens=kw.pop("max_tokens"), **kw), synthetic=cfg.synthetic(layer=l),
+                             device=dev.index, reserve_bytes=2 << 30)
+            if router is not None:
+                m.set_router(*router)
+            return m
 
-    for i in range(a.warmup):
-        step(xs_dev[i % pool])
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    launches0 = pkg.kernel_launches()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(dev.index) as clk:
-        ev0.record(stream)
-        for i in range(a.steps):
-            step(xs_dev[i % pool])
-        ev1.record(stream)
+        layers = [make(l, max_tokens=T, ep_rank=rank, ep_world=world) for l in range(n_layers)]
+        group = ep.EpGroup(H, K, dev.index)
+        rng = np.random.default_rng(1000)  # the same batches on every rank: rank g takes rows [g*T/N, (g+1)*T/N)
+        pool = 4
+        xs = torch.from_numpy(rng.standard_normal((pool, T, H)).astype(np.float32)).to(torch.bfloat16)
+        # parity: the first (up to) two layers for every rank's tokens against one GPU with whole layers
+        n_chk = min(2, n_layers)
+        chk = ep.EpPrefill(group, layers[:n_chk], max_tokens=Tr)
+        got = chk.forward(xs[0, rank * Tr:(rank + 1) * Tr].contiguous().to(dev))
+        chk.close()
+        gathered = [torch.empty_like(got) for _ in range(world)]
+        dist.all_gather(gathered, got)
+        ok = torch.ones(1, dtype=torch.int32, device=dev)
+        if rank == 0:
+            whole = [make(l, max_tokens=T) for l in range(n_chk)]
+            ref = pkg.MoeStack(whole, max_tokens=T)
+            want = ref.forward(xs[0].to(dev))
+            ok[0] = int(torch.equal(torch.cat(gathered).view(torch.int32), want.view(torch.int32)))
+            ref.close()
+            for l in whole:
+                l.close()
+            torch.cuda.empty_cache()
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        parity_ok = parity_ok and bool(ok.item())
+
+        pf = ep.EpPrefill(group, layers, max_tokens=Tr)
+        xs_dev = xs[:, rank * Tr:(rank + 1) * Tr].contiguous().to(dev)
+        out = torch.empty((Tr, H), dtype=torch.float32, device=dev)
+        for i in range(a.warmup):
+            pf.forward(xs_dev[i % pool], out)
         torch.cuda.synchronize()
-    launches = pkg.kernel_launches() - launches0
-    dist.barrier()
-    t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    ms_step = ms / a.steps
-    # end to end: the tokens come from pinned host memory each step, the rank's rows go back
-    xh = xs.pin_memory()
-    oh = torch.empty((T // world, H), dtype=torch.float32).pin_memory()
-    t0 = rank * (T // world)
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(a.steps):
-        h = step(xh[i % pool].to(dev, non_blocking=True))
-        oh.copy_(h[t0:t0 + T // world], non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    ems = float(te.item())
-    flops = a.layers * 2.0 * T * cfg.top_k * 3 * cfg.intermediate * H  # gate_up (2I x H) + down (H x I) per job
-    tpeak, tkind = peaks("bf16_tflops_sustained")
-    achieved = flops / world / (ms_step / 1e3) / 1e12
-    res = {"metric": metric_name(a) + f", expert-parallel over {world} GPU(s)", "value": T * a.steps / (ms / 1e3),
-           "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step,
-           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-           "dtype": "f16 tensor-core MMA (exact f16 MXFP4 weights x hi+lo f16 Q8_0 activations), fp32 accumulate",
-           "data": "synthetic",
-           "config": {"workload": f"gpt-oss-120b-stack {a.mode}, expert parallel", "layers": a.layers,
-                      "experts": cfg.experts, "experts_per_gpu": cfg.experts // world, "top_k": cfg.top_k,
-                      "hidden": H, "ffn": cfg.intermediate, "quant": "mxfp4", "global_batch": T,
-                      "parallelism": f"ep{world}", "exchange": "NCCL all_to_all_single of job rows + all_gather",
-                      "l2": "inputs larger than L2"},
-           "roofline": {"kernel": "whole step, expert FLOPs per GPU (useful, not the hi+lo MMAs issued)",
-                        "bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
-                        "frac": achieved / tpeak, "peak_source": f"{tkind} bf16_tflops_sustained", "traffic": None},
-           "gpu_launches": launches, "clocks": clk.summary(),
-           "e2e": {"value": T * a.steps / (ems / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(T * H * 4),
-                   "d2h_bytes_per_step": int(T // world * H * 4), "ms_per_step": ems / a.steps,
-                   "api": "MoeLayer.forward_jobs (umsx_moe_forward_jobs) + ep.exchange + umsx_combine"}}
-    for l in layers:
-        l.close()
+        dist.barrier()
+        torch.cuda.synchronize()
+        launches0 = pkg.kernel_launches()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + 1)]
+        with Clocks(dev.index) as clk:
+            evs[0].record(stream)
+            for i in range(a.steps):
+                pf.forward(xs_dev[i % pool], out)
+                evs[i + 1].record(stream)
+            torch.cuda.synchronize()
+        launches = pkg.kernel_launches() - launches0
+        pf.status()
+        dist.barrier()
+        step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(a.steps)]
+        ms = max_over_ranks(sum(step_ms))
+        p50, p99 = max_over_ranks(float(np.percentile(step_ms, 50))), max_over_ranks(float(np.percentile(step_ms, 99)))
+        loads = [None] * world
+        dist.all_gather_object(loads, pf.loads().tolist())
+        jobs = np.array([[lj[1] for lj in r] for r in loads], dtype=np.int64)  # [rank][layer]
+        rows = np.array([[lj[0] for lj in r] for r in loads], dtype=np.int64)
+        e2e = None
+        if not a.no_e2e:
+            xh = xs[:, rank * Tr:(rank + 1) * Tr].contiguous().pin_memory()
+            oh = torch.empty((Tr, H), dtype=torch.float32).pin_memory()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(a.steps):
+                pf.forward_host(xh[i % pool], oh)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ems = max_over_ranks(e0.elapsed_time(e1))
+            e2e = {"value": T * a.steps / (ems / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": int(Tr * H * 2),
+                   "d2h_bytes_per_step": int(Tr * H * 4), "ms_per_step": ems / a.steps,
+                   "api": "umsx_ep_prefill_forward_host (per rank)"}
+        ms_step = ms / a.steps
+        flops = n_layers * 2.0 * T * K * 3 * cfg.intermediate * H  # gate_up (2I x H) + down (H x I) per job
+        tpeak, tkind = peaks("bf16_tflops_sustained")
+        achieved = flops / world / (ms_step / 1e3) / 1e12
+        records[name] = {
+            "tokens_per_s": T * a.steps / (ms / 1e3), "ms_per_step": ms_step, "step_ms_p50": p50, "step_ms_p99": p99,
+            "jobs_per_gpu_per_layer": jobs.tolist(), "rows_received_per_gpu_per_layer": rows.tolist(),
+            "jobs_max_over_mean": float((jobs.max(0) / jobs.mean(0)).max()),
+            "exchange_bytes_per_step": int(rows.sum() * (H + H // 32 * 4 + K * 4 + 8) + T * K * H * 4 * n_layers),
+            "roofline": {"kernel": "whole step, expert FLOPs per GPU (useful, not the hi+lo MMAs issued)",
+                         "bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
+                         "frac": achieved / tpeak, "peak_source": f"{tkind} bf16_tflops_sustained", "traffic": None},
+            "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e,
+            "config": {"layers": n_layers, "experts": cfg.experts, "experts_per_gpu": cfg.experts // world,
+                       "top_k": K, "hidden": H, "ffn": cfg.intermediate,
+                       "quant": "mxfp4" if cfg.quant == pkg.umsx.QUANT_MXFP4 else "q8_0"}}
+        pf.close()
+        group.close()
+        for l in layers:
+            l.close()
+        torch.cuda.empty_cache()
+    head = records[names[0]]
+    workload = ("qwen3-30b-a3b skew layer (configs[3], Zipf 1.2 router bias), prefill, expert parallel"
+                if a.config == "skew" else "gpt-oss-120b-stack prefill, expert parallel")
+    res = {"metric": (f"MoE-layer tokens/s, configs[3] load skew, T={T}, expert parallel over {world} GPU(s)"
+                      if a.config == "skew" else
+                      f"MoE-layer tokens/s, GPT-OSS-120B-shaped {n_layers}-layer MXFP4 stack, prefill T={T}, "
+                      f"expert parallel over {world} GPU(s)"),
+           "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+           "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "f16 tensor-core MMA (exact f16 weights x hi+lo f16 Q8_0 activations), fp32 accumulate",
+           "data": "synthetic", "parity_ok": parity_ok,
+           "config": {"workload": workload, **head["config"], "global_batch": T, "tokens_per_gpu": Tr,
+                      "parallelism": f"ep{world}",
+                      "exchange": "P2P NVLink stores inside k_ep_count / k_ep_dispatch / k_ep_return (CUDA IPC "
+                                  "mappings), release/acquire flags; no collective in the data path",
+                      "l2": "inputs larger than L2",
+                      "parity": "every rank's tokens through the first layers, bit-exact with one GPU"},
+           "roofline": head["roofline"], "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+           "e2e": head["e2e"], "layers_detail": records}
     dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res))
+    if not parity_ok:
+        raise SystemExit(3)
 
 
 def traffic_for(a, kernel: str):
@@ -879,12 +948,12 @@ def reference_arm(a):
 
 def main():
     a = parse()
-    if a.config == "skew":
+    if a.ep and a.impl != "reference":
+        ep_arm(a)
+    elif a.config == "skew":
         skew_arm(a)
     elif a.impl == "reference":
         reference_arm(a)
-    elif a.ep:
-        ep_arm(a)
     else:
         gpu_arm(a)
 

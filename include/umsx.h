@@ -306,6 +306,34 @@ umsx_status umsx_ep_stack_forward_host(umsx_ep_stack *stack, const void *x, int 
                                        umsx_stream stream);
 umsx_status umsx_ep_stack_status(umsx_ep_stack *stack, umsx_stream stream);
 
+/* Expert-parallel prefill: every rank brings its own tokens (up to max_tokens; counts may differ
+ * between ranks) and holds its share of the experts of every layer.  Per layer: each rank routes
+ * its tokens (RMSNorm fused), counts the rows it sends each rank and stores its row of the G x G
+ * count matrix into every rank (exchange 1), stores the Q8_0 row of each token (the experts' exact
+ * input), its expert ids and its origin into the receive buffer of every rank that holds one of its
+ * experts (exchange 2), runs its experts over the rows it received with the tensor-core grouped GEMM,
+ * stores every job's output row into the owner's buffer (exchange 3), and combines its tokens in
+ * rank order with the residual.  All three exchanges are P2P stores from inside the kernels that
+ * compute the rows (umsx_ep.cu) with the group's flags and bounded waits.  Each token's result has
+ * the single-GPU stack's bits on the same path (T >= 65 tokens: the tensor-core prefill).  The
+ * receive buffers are per stack: gather and connect their handles like the group's, after
+ * umsx_ep_connect.  Requires 65 <= max_tokens * world <= 65535 and <= 256 experts per rank. */
+typedef struct umsx_ep_prefill umsx_ep_prefill;
+umsx_status umsx_ep_prefill_create(umsx_ep *ep, umsx_moe *const *layers, int n_layers, int max_tokens,
+                                   float rms_eps, umsx_ep_prefill **out);
+umsx_status umsx_ep_prefill_handle(umsx_ep_prefill *stack, void *handle_out, size_t size);
+umsx_status umsx_ep_prefill_connect(umsx_ep_prefill *stack, const void *handles, size_t size);
+/* x: this rank's tokens [T][H] (fp32 or bf16, device) -> out [T][H] fp32 (device). */
+umsx_status umsx_ep_prefill_forward(umsx_ep_prefill *stack, const void *x, int x_dtype, int tokens, float *out,
+                                    umsx_stream stream);
+umsx_status umsx_ep_prefill_forward_host(umsx_ep_prefill *stack, const void *x, int x_dtype, int tokens,
+                                         float *out, umsx_stream stream);
+/* Per layer of the last call: {rows this rank received, expert jobs it ran} (rows_jobs[2 * layers]);
+ * synchronises the stack's stream.  The per-GPU load of expert parallelism (configs[3] skew). */
+umsx_status umsx_ep_prefill_loads(umsx_ep_prefill *stack, int32_t *rows_jobs, int n);
+umsx_status umsx_ep_prefill_status(umsx_ep_prefill *stack, umsx_stream stream);
+void umsx_ep_prefill_destroy(umsx_ep_prefill *stack);
+
 /* ---- GGUF checkpoints ------------------------------------------------------------------
  * The selected experts of one layer read from a GGUF file or a set of shards named
  * <stem>-00001-of-NNNNN.gguf (pass the first).  Replaces load_gguf_experts

@@ -171,3 +171,111 @@ def test_two_gpu_ep_rank_loss_reports_a_timeout():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     assert _run_ep("loss") == {0: "timeout", 1: "left"}
+
+
+def _ep_prefill_worker(rank, world, port, mode, q):
+    try:
+        import datetime
+        import importlib
+
+        import torch.distributed as dist
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        import __graft_entry__ as ge
+        pkg = ge.load_package()
+        U = pkg.umsx
+        ep = importlib.import_module(pkg.__name__ + ".ep")
+        from oracle.oracle import Oracle
+        from tests.helpers import bits, small_config, x_bits
+        results = {}
+        cfgs = {"mxfp4": small_config(experts=16, top_k=4, seed=31),
+                "q8_0": small_config(name="small-q8", quant=U.QUANT_Q8_0, routing=U.ROUTE_SOFTMAX_TOPK_NORM,
+                                     activation=U.ACT_SILU, fused_gate_up=False, has_bias=False,
+                                     has_router_bias=False, experts=16, top_k=4, seed=12)}
+        split = [70, 50]  # the ranks bring different token counts
+        T = sum(split)
+        t0 = sum(split[:rank])
+        L = 2
+        for name, cfg in cfgs.items():
+            xb = x_bits(Oracle(), cfg, T)
+            xs = torch.from_numpy(xb.view(np.int16).copy()).view(torch.bfloat16).cuda(rank)
+            full = [pkg.MoeLayer(cfg.desc(T), synthetic=cfg.synthetic(layer=l), device=rank, reserve_bytes=1 << 28)
+                    for l in range(L)]
+            stack = pkg.MoeStack(full, max_tokens=T)
+            want = stack.forward(xs).cpu().numpy()[t0:t0 + split[rank]]
+            stack.close()
+            for l in full:
+                l.close()
+            parts = [pkg.MoeLayer(cfg.desc(T, ep_rank=rank, ep_world=world), synthetic=cfg.synthetic(layer=l),
+                                  device=rank, reserve_bytes=1 << 28) for l in range(L)]
+            group = ep.EpGroup(cfg.hidden, cfg.top_k, rank)
+            pf = ep.EpPrefill(group, parts, max_tokens=max(split))
+            ok = True
+            for _ in range(2):  # two calls in a row: the exchange numbers advance in step on both ranks
+                got = pf.forward(xs[t0:t0 + split[rank]]).cpu().numpy()
+                ok = ok and np.array_equal(bits(got), bits(want))
+            pf.status()
+            loads = pf.loads()
+            jobs = [None] * world
+            dist.all_gather_object(jobs, loads[:, 1].tolist())
+            ok = ok and all(sum(j[l] for j in jobs) == T * cfg.top_k for l in range(L))
+            result = ok
+            if mode == "loss" and name == "mxfp4":
+                dist.barrier()  # both ranks are between calls
+                if rank == 1:
+                    result = "left"
+                else:
+                    xh = xs[t0:t0 + split[rank]].cpu().pin_memory()
+                    oh = torch.empty((split[rank], cfg.hidden), dtype=torch.float32).pin_memory()
+                    try:
+                        pf.forward_host(xh, oh)
+                        result = "no error"
+                    except U.UmsxError as e:
+                        result = "timeout" if e.status == U.ETIMEOUT else repr(e)
+                dist.barrier()
+            pf.close()
+            group.close()
+            for l in parts:
+                l.close()
+            results[name] = result
+            if mode == "loss":
+                break
+        q.put((rank, results))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def _run_ep_prefill(mode):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_prefill_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    return results
+
+
+def test_two_gpu_ep_prefill_stack_bit_exact():
+    """Tokens split 70 / 50 over two ranks, each holding half of every layer's experts: the token rows
+    go to the experts' ranks and the outputs come back as P2P stores inside the exchange kernels, the
+    experts run on the tensor-core prefill path.  Every rank's tokens must come out with the single-GPU
+    stack's bits (MXFP4 fused and Q8_0 separate gate/up), twice in a row, and the ranks' job counts must
+    add up to every job of every layer."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    assert _run_ep_prefill("exact") == {0: {"mxfp4": True, "q8_0": True}, 1: {"mxfp4": True, "q8_0": True}}
+
+
+def test_two_gpu_ep_prefill_rank_loss_reports_a_timeout():
+    """Rank 1 stops between calls; rank 0's next prefill call waits a bounded time in its first
+    exchange and reports UMSX_ETIMEOUT instead of hanging."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    assert _run_ep_prefill("loss") == {0: {"mxfp4": "timeout"}, 1: {"mxfp4": "left"}}

@@ -679,35 +679,38 @@ bool prefill_eligible(const umsx_moe *m, const Workspace &ws, int tokens) {
 // y_jobs (expert parallelism): instead of combining, write each resident job's output to
 // y_jobs[t][r][:] and leave the other rows alone.
 // extra: [T][H] added to each token's routed sum before the residual (shared experts), or null.
-umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
-                        const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
-                        float *y_jobs = nullptr, const float *extra = nullptr) {
+// The tiled router over `tokens` rows (RMSNorm fused when rmsnorm): ids, weights, the Q8_0 rows
+// and this handle's expert dispatch.
+umsx_status run_router_tiled(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, int rmsnorm, float eps,
+                             cudaStream_t s) {
     const auto &d = m->d;
-    const int K = d.top_k, H = d.hidden, I = d.intermediate, jobs = tokens * K;
-    if (ev) if (umsx_status st = mark(ev[0], s)) return st;
-    {
-        RouterParams rp{};
-        rp.x = x;
-        rp.x_dtype = x_dtype;
-        rp.tokens = tokens;
-        rp.hidden = H;
-        rp.experts = d.experts;
-        rp.top_k = K;
-        rp.routing = d.routing;
-        rp.routed_scale = d.routed_scale;
-        rp.w = m->router_w;
-        rp.b = m->router_b;
-        rp.e_lo = m->e_lo;
-        rp.e_local = m->e_local;
-        rp.rmsnorm = rmsnorm;
-        rp.eps = eps;
-        const int n = launch_router_tiled(rp, ws.disp, s);
-        if (n < 0) return fail(UMSX_EDEVICE, "prefill router: shared-memory attribute refused");
-        UMSX_LAUNCHED(n);
-    }
-    UMSX_LAUNCHED(launch_prefill_pack(ws.disp, jobs, m->e_local == d.experts ? nullptr : ws.disp.offsets + m->e_local, K, H,
-                                      ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));
-    if (ev) if (umsx_status st = mark(ev[1], s)) return st;
+    RouterParams rp{};
+    rp.x = x;
+    rp.x_dtype = x_dtype;
+    rp.tokens = tokens;
+    rp.hidden = d.hidden;
+    rp.experts = d.experts;
+    rp.top_k = d.top_k;
+    rp.routing = d.routing;
+    rp.routed_scale = d.routed_scale;
+    rp.w = m->router_w;
+    rp.b = m->router_b;
+    rp.e_lo = m->e_lo;
+    rp.e_local = m->e_local;
+    rp.rmsnorm = rmsnorm;
+    rp.eps = eps;
+    const int n = launch_router_tiled(rp, ws.disp, s);
+    if (n < 0) return fail(UMSX_EDEVICE, "prefill router: shared-memory attribute refused");
+    UMSX_LAUNCHED(n);
+    return UMSX_OK;
+}
+
+// The grouped GEMMs of the tensor-core path over `jobs` packed job rows (an upper bound: the
+// experts' segments come from disp.offsets): gate_up + activation into act16, down into ws.y.
+umsx_status run_prefill_gemms(umsx_moe *m, Workspace &ws, const Dispatch &disp, int jobs, cudaStream_t s,
+                              cudaEvent_t const *ev) {
+    const auto &d = m->d;
+    const int H = d.hidden, I = d.intermediate;
     MoeGemmParams g{};
     g.quant = d.quant;
     if (d.fused_gate_up) {
@@ -729,7 +732,7 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
     g.fused = 1;
     g.inter = I;
     g.bias = m->gu_bias;
-    g.offsets = ws.disp.offsets;
+    g.offsets = disp.offsets;
     g.experts = m->e_local;
     g.m_tiles = I / 64;
     g.mode = 0;
@@ -738,7 +741,7 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
     g.limit = d.swiglu_limit;
     g.act_hi = ws.act16;
     g.act_lo = ws.act16 + (size_t)jobs * I;
-    g.err = ws.disp.err;
+    g.err = disp.err;
     int n = launch_moe_gemm(g, ws.a16, ws.a16 + (size_t)jobs * H, jobs, s);
     if (n < 0) return fail(UMSX_EDEVICE, "prefill gate_up: tensor map or launch setup failed");
     UMSX_LAUNCHED(n);
@@ -753,15 +756,29 @@ umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, 
     dn.cols = I;
     dn.fused = 0;
     dn.bias = m->down_bias;
-    dn.offsets = ws.disp.offsets;
+    dn.offsets = disp.offsets;
     dn.experts = m->e_local;
     dn.m_tiles = (H + 127) / 128;
     dn.mode = 1;
     dn.y_out = ws.y;
-    dn.err = ws.disp.err;
+    dn.err = disp.err;
     n = launch_moe_gemm(dn, ws.act16, ws.act16 + (size_t)jobs * I, jobs, s);
     if (n < 0) return fail(UMSX_EDEVICE, "prefill down: tensor map or launch setup failed");
     UMSX_LAUNCHED(n);
+    return UMSX_OK;
+}
+
+umsx_status run_prefill(umsx_moe *m, Workspace &ws, const void *x, int x_dtype, int tokens, float *out,
+                        const float *residual, int rmsnorm, float eps, cudaStream_t s, cudaEvent_t const *ev,
+                        float *y_jobs = nullptr, const float *extra = nullptr) {
+    const auto &d = m->d;
+    const int K = d.top_k, H = d.hidden, jobs = tokens * K;
+    if (ev) if (umsx_status st = mark(ev[0], s)) return st;
+    if (umsx_status st = run_router_tiled(m, ws, x, x_dtype, tokens, rmsnorm, eps, s)) return st;
+    UMSX_LAUNCHED(launch_prefill_pack(ws.disp, jobs, m->e_local == d.experts ? nullptr : ws.disp.offsets + m->e_local, K, H,
+                                      ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));
+    if (ev) if (umsx_status st = mark(ev[1], s)) return st;
+    if (umsx_status st = run_prefill_gemms(m, ws, ws.disp, jobs, s, ev)) return st;
     if (ev) if (umsx_status st = mark(ev[3], s)) return st;
     if (y_jobs) {
         UMSX_LAUNCHED(launch_prefill_scatter(ws.y, ws.inv, ws.disp.ids, m->e_lo, m->e_local, tokens, K, H, y_jobs, s));
@@ -1771,6 +1788,262 @@ umsx_status umsx_ep_stack_status(umsx_ep_stack *st, umsx_stream stream) {
     UMSX_CUDA(cudaSetDevice(st->ep->device));
     UMSX_CUDA(cudaStreamSynchronize(st->stream));
     return check_device_flag(st->ws, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+// ============================================================================
+// Expert-parallel prefill stack: tokens sharded over the ranks, each rank's experts run over the
+// rows the other ranks send it (umsx_ep.cu has the exchange kernels).
+// ============================================================================
+
+struct umsx_ep_prefill {
+    umsx_ep *ep = nullptr;
+    std::vector<umsx_moe *> layers;
+    float eps = 1e-5f;
+    int tokens_max = 0, rows_max = 0;
+    Workspace ws;
+    // exported receive buffers: counts [G][G] | codes [rows][H] | scales [rows][H/32] | ids [rows][K] |
+    // src [rows] int2 | y_back [tokens_max][K][H] f32
+    uint8_t *buf = nullptr;
+    size_t bytes = 0, off_codes = 0, off_scales = 0, off_ids = 0, off_src = 0, off_y = 0;
+    cudaIpcMemHandle_t handle{};
+    std::vector<uint8_t *> peers;
+    bool connected = false;
+    int32_t *pos = nullptr;
+    unsigned *done = nullptr;
+    int2 *loads = nullptr;  // [layers]
+    float *h = nullptr;     // [tokens_max][H] residual stream
+    void *x_stage = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    std::mutex mu;
+};
+
+namespace {
+
+EpPrefillParams ep_prefill_params(umsx_ep_prefill *st, const umsx_moe *m, int tokens) {
+    const umsx_ep *ep = st->ep;
+    EpPrefillParams p{};
+    p.rank = ep->rank;
+    p.world = ep->world;
+    p.hidden = ep->hidden;
+    p.top_k = ep->top_k;
+    p.e_per_rank = m->e_local;
+    p.tokens = tokens;
+    p.tokens_max = st->tokens_max;
+    p.rows_max = st->rows_max;
+    p.ids = st->ws.disp.ids;
+    p.xq_codes = st->ws.disp.xq_codes;
+    p.xq_scales = st->ws.disp.xq_scales;
+    p.pos = st->pos;
+    p.counts = reinterpret_cast<int32_t *>(st->buf);
+    p.done = st->done;
+    for (int q = 0; q < ep->world; ++q) {
+        uint8_t *b = st->peers[q];
+        p.peer_counts[q] = reinterpret_cast<int32_t *>(b);
+        p.peer_codes[q] = b + st->off_codes;
+        p.peer_scales[q] = reinterpret_cast<float *>(b + st->off_scales);
+        p.peer_ids[q] = reinterpret_cast<int32_t *>(b + st->off_ids);
+        p.peer_src[q] = reinterpret_cast<int2 *>(b + st->off_src);
+        p.peer_y_back[q] = reinterpret_cast<float *>(b + st->off_y);
+        p.peer_flags[q] = reinterpret_cast<unsigned *>(ep->peers[q] + ep->off_flags);
+    }
+    p.recv_ids = reinterpret_cast<const int32_t *>(st->buf + st->off_ids);
+    p.recv_src = reinterpret_cast<const int2 *>(st->buf + st->off_src);
+    p.inv = st->ws.inv;
+    p.y_jobs = st->ws.y;
+    p.n_jobs = st->ws.disp.offsets + m->e_local;
+    p.loads = st->loads;
+    p.flags = reinterpret_cast<unsigned *>(ep->buf + ep->off_flags);
+    p.epoch = reinterpret_cast<unsigned *>(ep->buf + ep->off_epoch);
+    p.err = st->ws.disp.err;
+    p.wait_cycles = ep->wait_cycles;
+    return p;
+}
+
+// One layer: route this rank's tokens, send their rows to the experts' ranks, run this rank's
+// experts over the rows received, send the outputs back, combine in rank order with the residual.
+umsx_status record_ep_prefill_layer(umsx_ep_prefill *st, umsx_moe *m, int layer, int tokens, cudaStream_t s) {
+    const int K = m->d.top_k, H = m->d.hidden, jobs = st->rows_max * K;
+    const EpPrefillParams p = ep_prefill_params(st, m, tokens);
+    Workspace &ws = st->ws;
+    // rows past the ones received this layer must read as "no local expert" for the dispatch scan
+    UMSX_CUDA(cudaMemsetAsync(st->buf + st->off_ids, 0xFF, (size_t)jobs * 4, s));
+    if (umsx_status r = run_router_tiled(m, ws, st->h, UMSX_DTYPE_F32, tokens, 1, st->eps, s)) return r;
+    UMSX_LAUNCHED(launch_ep_count(p, s));
+    UMSX_LAUNCHED(launch_ep_wait(p, s));
+    UMSX_LAUNCHED(launch_ep_dispatch(p, s));
+    UMSX_LAUNCHED(launch_ep_wait(p, s));
+    Dispatch dd = ws.disp;  // the received rows take the place of tokens
+    dd.ids = reinterpret_cast<int32_t *>(st->buf + st->off_ids);
+    dd.xq_codes = st->buf + st->off_codes;
+    dd.xq_scales = reinterpret_cast<float *>(st->buf + st->off_scales);
+    UMSX_LAUNCHED(launch_dispatch(dd, jobs, K, m->e_lo, m->e_local, s));
+    UMSX_LAUNCHED(launch_prefill_pack(dd, jobs, dd.offsets + m->e_local, K, H, ws.a16, ws.a16 + (size_t)jobs * H, ws.inv, s));
+    if (umsx_status r = run_prefill_gemms(m, ws, dd, jobs, s, nullptr)) return r;
+    UMSX_LAUNCHED(launch_ep_return(p, layer, s));
+    UMSX_LAUNCHED(launch_ep_wait(p, s));
+    UMSX_LAUNCHED(launch_combine(reinterpret_cast<const float *>(st->buf + st->off_y), ws.disp.weights, tokens, K, H,
+                                 nullptr, st->h, st->h, ws.disp.err, s));
+    return UMSX_OK;
+}
+
+umsx_status ep_prefill_run(umsx_ep_prefill *st, const void *x, int x_dtype, int tokens, float *out,
+                           cudaMemcpyKind in_kind, cudaMemcpyKind out_kind, cudaStream_t caller) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    if (!st->connected) return fail(UMSX_EINVAL, "connect the stack first (umsx_ep_prefill_connect)");
+    if (!x || !out) return fail(UMSX_EINVAL, "null buffer");
+    if (x_dtype != UMSX_DTYPE_F32 && x_dtype != UMSX_DTYPE_BF16) return fail(UMSX_EINVAL, "x_dtype must be F32 or BF16");
+    if (tokens < 1 || tokens > st->tokens_max) return fail(UMSX_EINVAL, "tokens must be in [1, max_tokens]");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->ep->device));
+    const size_t n = (size_t)tokens * st->ep->hidden;
+    cudaStream_t s = st->stream;
+    UMSX_CUDA(cudaEventRecord(st->ev_in, caller));
+    UMSX_CUDA(cudaStreamWaitEvent(s, st->ev_in, 0));
+    if (x_dtype == UMSX_DTYPE_BF16) {
+        UMSX_CUDA(cudaMemcpyAsync(st->x_stage, x, n * 2, in_kind, s));
+        UMSX_LAUNCHED(launch_bf16_to_f32(static_cast<const uint16_t *>(st->x_stage), st->h, n, s));
+    } else {
+        UMSX_CUDA(cudaMemcpyAsync(st->h, x, n * 4, in_kind, s));
+    }
+    for (size_t l = 0; l < st->layers.size(); ++l)
+        if (umsx_status r = record_ep_prefill_layer(st, st->layers[l], (int)l, tokens, s)) return r;
+    UMSX_CUDA(cudaMemcpyAsync(out, st->h, n * 4, out_kind, s));
+    UMSX_CUDA(cudaEventRecord(st->ev_out, s));
+    UMSX_CUDA(cudaStreamWaitEvent(caller, st->ev_out, 0));
+    return UMSX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+umsx_status umsx_ep_prefill_create(umsx_ep *ep, umsx_moe *const *layers, int n_layers, int max_tokens, float rms_eps,
+                                   umsx_ep_prefill **out) {
+    if (!out || !ep || !layers || n_layers <= 0) return fail(UMSX_EINVAL, "need a group and at least one layer");
+    *out = nullptr;
+    const umsx_moe *l0 = layers[0];
+    for (int l = 0; l < n_layers; ++l) {
+        const umsx_moe *m = layers[l];
+        if (!m || m->device != ep->device || m->d.hidden != ep->hidden || m->d.top_k != ep->top_k ||
+            m->d.experts != l0->d.experts || m->d.intermediate != l0->d.intermediate || m->d.quant != l0->d.quant)
+            return fail(UMSX_EINVAL, "layers must share the group's device, width and top_k, and one shape");
+        if (m->d.ep_world != ep->world || m->d.ep_rank != ep->rank)
+            return fail(UMSX_EINVAL, "layers must be created with the group's ep_rank and ep_world");
+        if (m->banked) return fail(UMSX_EUNSUPPORTED, "banked layer: call umsx_moe_forward or umsx_moe_forward_host");
+        if (m->e_local > 256) return fail(UMSX_EUNSUPPORTED, "more than 256 experts per rank");
+    }
+    if (max_tokens < 1 || (size_t)max_tokens * ep->world > 65535 || max_tokens * ep->world < kPrefillMinTokens)
+        return fail(UMSX_EINVAL, "max_tokens x world must be in [65, 65535]");
+    UMSX_CUDA(cudaSetDevice(ep->device));
+    auto *st = new umsx_ep_prefill();
+    st->ep = ep;
+    st->layers.assign(layers, layers + n_layers);
+    st->eps = rms_eps;
+    st->tokens_max = max_tokens;
+    st->rows_max = max_tokens * ep->world;
+    const size_t G = ep->world, H = ep->hidden, K = ep->top_k, R = st->rows_max, T = max_tokens;
+    st->off_codes = align_up(G * G * 4);
+    st->off_scales = align_up(st->off_codes + R * H);
+    st->off_ids = align_up(st->off_scales + R * (H / 32) * 4);
+    st->off_src = align_up(st->off_ids + R * K * 4);
+    st->off_y = align_up(st->off_src + R * 8);
+    st->bytes = align_up(st->off_y + T * K * H * 4);
+    auto run = [&]() -> umsx_status {
+        if (umsx_status r = alloc_workspace(st->ws, l0->d, l0->e_local, st->rows_max, 1u << 30)) return r;
+        UMSX_CUDA(cudaMalloc(&st->buf, st->bytes));
+        UMSX_CUDA(cudaMemset(st->buf, 0, st->bytes));
+        UMSX_CUDA(cudaIpcGetMemHandle(&st->handle, st->buf));
+        UMSX_CUDA(cudaMalloc(&st->pos, T * G * 4));
+        UMSX_CUDA(cudaMalloc(&st->done, 4));
+        UMSX_CUDA(cudaMemset(st->done, 0, 4));
+        UMSX_CUDA(cudaMalloc(&st->loads, (size_t)n_layers * sizeof(int2)));
+        UMSX_CUDA(cudaMemset(st->loads, 0, (size_t)n_layers * sizeof(int2)));
+        UMSX_CUDA(cudaMalloc(&st->h, T * H * 4));
+        UMSX_CUDA(cudaMalloc(&st->x_stage, T * H * 2));
+        UMSX_CUDA(cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking));
+        UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_in, cudaEventDisableTiming));
+        UMSX_CUDA(cudaEventCreateWithFlags(&st->ev_out, cudaEventDisableTiming));
+        UMSX_CUDA(cudaDeviceSynchronize());
+        return UMSX_OK;
+    };
+    if (umsx_status r = run()) { umsx_ep_prefill_destroy(st); return r; }
+    st->peers.assign(G, nullptr);
+    st->peers[ep->rank] = st->buf;
+    *out = st;
+    return UMSX_OK;
+}
+
+umsx_status umsx_ep_prefill_handle(umsx_ep_prefill *st, void *handle_out, size_t size) {
+    if (!st || !handle_out || size != sizeof(cudaIpcMemHandle_t))
+        return fail(UMSX_EINVAL, "need the stack and a buffer of the IPC handle size (64 bytes)");
+    std::memcpy(handle_out, &st->handle, sizeof(cudaIpcMemHandle_t));
+    return UMSX_OK;
+}
+
+umsx_status umsx_ep_prefill_connect(umsx_ep_prefill *st, const void *handles, size_t size) {
+    if (!st || !handles || size != (size_t)st->ep->world * sizeof(cudaIpcMemHandle_t))
+        return fail(UMSX_EINVAL, "need every rank's IPC handle (world x 64 bytes, rank order)");
+    if (st->connected) return fail(UMSX_EINVAL, "already connected");
+    if (!st->ep->connected) return fail(UMSX_EINVAL, "connect the group first (umsx_ep_connect)");
+    UMSX_CUDA(cudaSetDevice(st->ep->device));
+    for (int q = 0; q < st->ep->world; ++q) {
+        if (q == st->ep->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)q * sizeof(h), sizeof(h));
+        void *p = nullptr;
+        UMSX_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        st->peers[q] = static_cast<uint8_t *>(p);
+    }
+    st->connected = true;
+    return UMSX_OK;
+}
+
+umsx_status umsx_ep_prefill_forward(umsx_ep_prefill *st, const void *x, int x_dtype, int tokens, float *out,
+                                    umsx_stream stream) {
+    return ep_prefill_run(st, x, x_dtype, tokens, out, cudaMemcpyDeviceToDevice, cudaMemcpyDeviceToDevice,
+                          static_cast<cudaStream_t>(stream));
+}
+
+umsx_status umsx_ep_prefill_forward_host(umsx_ep_prefill *st, const void *x, int x_dtype, int tokens, float *out,
+                                         umsx_stream stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (umsx_status r = ep_prefill_run(st, x, x_dtype, tokens, out, cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost, s))
+        return r;
+    return check_device_flag(st->ws, s);
+}
+
+umsx_status umsx_ep_prefill_loads(umsx_ep_prefill *st, int32_t *rows_jobs, int n) {
+    if (!st || !rows_jobs || n < 2 * (int)st->layers.size()) return fail(UMSX_EINVAL, "need room for 2 x layers values");
+    std::lock_guard<std::mutex> lock(st->mu);
+    UMSX_CUDA(cudaSetDevice(st->ep->device));
+    UMSX_CUDA(cudaStreamSynchronize(st->stream));
+    UMSX_CUDA(cudaMemcpy(rows_jobs, st->loads, st->layers.size() * sizeof(int2), cudaMemcpyDeviceToHost));
+    return UMSX_OK;
+}
+
+umsx_status umsx_ep_prefill_status(umsx_ep_prefill *st, umsx_stream stream) {
+    if (!st) return fail(UMSX_EINVAL, "null stack");
+    UMSX_CUDA(cudaSetDevice(st->ep->device));
+    UMSX_CUDA(cudaStreamSynchronize(st->stream));
+    return check_device_flag(st->ws, static_cast<cudaStream_t>(stream));
+}
+
+void umsx_ep_prefill_destroy(umsx_ep_prefill *st) {
+    if (!st) return;
+    cudaSetDevice(st->ep->device);
+    if (st->stream) cudaStreamSynchronize(st->stream);
+    for (int q = 0; q < (int)st->peers.size(); ++q)
+        if (q != st->ep->rank && st->peers[q]) cudaIpcCloseMemHandle(st->peers[q]);
+    if (st->ev_in) cudaEventDestroy(st->ev_in);
+    if (st->ev_out) cudaEventDestroy(st->ev_out);
+    if (st->stream) cudaStreamDestroy(st->stream);
+    for (void *p : {(void *)st->buf, (void *)st->pos, (void *)st->done, (void *)st->loads, (void *)st->h, st->x_stage,
+                    (void *)st->ws.mem})
+        if (p) cudaFree(p);
+    delete st;
 }
 
 }  // extern "C"

@@ -229,6 +229,41 @@ struct EpParams {
 int launch_ep_share(const EpParams &p, cudaStream_t s);
 int launch_ep_combine(const EpParams &p, cudaStream_t s);
 
+// Expert-parallel prefill (umsx_ep.cu): tokens sharded over the ranks, experts split contiguously
+// (rank g holds [g*E/G, (g+1)*E/G)); token rows go to the ranks that hold their experts and the
+// expert outputs come back, both as P2P stores into the peers' receive buffers.
+struct EpPrefillParams {
+    int rank, world, hidden, top_k, e_per_rank, tokens, tokens_max, rows_max;
+    const int32_t *ids;          // [T][K] routing of this rank's tokens
+    const uint8_t *xq_codes;     // [T][H] Q8_0 codes of this rank's normalised tokens (lane-pair order)
+    const float *xq_scales;      // [T][H/32]
+    int32_t *pos;                // [T][world] row of token t in rank g's receive buffer, -1 if none
+    int32_t *counts;             // [world][world] count matrix (row = source rank), this rank's copy
+    unsigned *done;              // CTA arrival counter (zero between launches)
+    int32_t *peer_counts[kEpMaxRanks];
+    uint8_t *peer_codes[kEpMaxRanks];    // [rows_max][H]
+    float *peer_scales[kEpMaxRanks];     // [rows_max][H/32]
+    int32_t *peer_ids[kEpMaxRanks];      // [rows_max][K] expert ids held by that rank, -1 for the others
+    int2 *peer_src[kEpMaxRanks];         // [rows_max] (source rank, source token)
+    float *peer_y_back[kEpMaxRanks];     // [tokens_max][K][H]
+    const int32_t *recv_ids;     // this rank's receive buffers (its own peer_* entries)
+    const int2 *recv_src;
+    const int32_t *inv;          // [rows_max][K] job row of (received row, rank slot) in y_jobs
+    const float *y_jobs;         // [jobs][H] outputs of this rank's expert jobs (expert order)
+    const int32_t *n_jobs;       // this rank's job count (device)
+    int2 *loads;                 // per layer {rows received, jobs run}, or null
+    unsigned *flags;
+    unsigned *peer_flags[kEpMaxRanks];
+    unsigned *epoch;
+    uint32_t *err;
+    long long wait_cycles;
+};
+
+int launch_ep_count(const EpPrefillParams &p, cudaStream_t s);
+int launch_ep_dispatch(const EpPrefillParams &p, cudaStream_t s);
+int launch_ep_return(const EpPrefillParams &p, int layer, cudaStream_t s);
+int launch_ep_wait(const EpPrefillParams &p, cudaStream_t s);
+
 // Thread-local status channel shared by every translation unit (umsx_api.cu).
 void record_error(const char *msg);      // the message umsx_last_error() returns
 void record_launches(uint64_t kernels);  // adds to umsx_kernel_launches()

@@ -170,3 +170,65 @@ class EpStack:
         if self._h:
             lib().umsx_ep_stack_destroy(self._h)
             self._h = None
+
+
+# ---- prefill over NVLink: tokens sharded over the ranks, rows exchanged inside the kernels -------
+
+class EpPrefill:
+    """A prefill stack split over the group by expert, every rank with its own tokens (umsx_ep_prefill_*):
+    per layer the token rows travel to the ranks that hold their experts and the outputs come back,
+    both as P2P stores from inside the exchange kernels.  The receive buffers' IPC handles travel
+    once, at set-up, over the process group."""
+
+    def __init__(self, group: EpGroup, layers: list, max_tokens: int, rms_eps: float = 1e-5, pg=None):
+        import ctypes as C
+
+        from .umsx import check, lib
+        self.group, self.layers = group, list(layers)
+        self.hidden = self.layers[0].desc.hidden
+        L = lib()
+        arr = (C.c_void_p * len(self.layers))(*[l._h for l in self.layers])
+        self._h = C.c_void_p()
+        check(L.umsx_ep_prefill_create(group._h, arr, len(self.layers), int(max_tokens), rms_eps, C.byref(self._h)))
+        mine = (C.c_uint8 * IPC_HANDLE_BYTES)()
+        check(L.umsx_ep_prefill_handle(self._h, mine, IPC_HANDLE_BYTES))
+        handles = [None] * group.world
+        dist.all_gather_object(handles, bytes(mine), group=pg)
+        buf = (C.c_uint8 * (IPC_HANDLE_BYTES * group.world)).from_buffer_copy(b"".join(handles))
+        check(L.umsx_ep_prefill_connect(self._h, buf, IPC_HANDLE_BYTES * group.world))
+        dist.barrier(group=pg)  # every rank is mapped before any layer stores into a peer
+
+    def forward(self, x, out=None, stream=None):
+        """x: this rank's tokens [T, H] (CUDA, f32 or bf16) -> out [T, H] f32."""
+        from .umsx import _dtype_code, _ptr, _stream, check, lib
+        T = x.shape[0]
+        out = out if out is not None else torch.empty((T, self.hidden), dtype=torch.float32, device=x.device)
+        check(lib().umsx_ep_prefill_forward(self._h, _ptr(x), _dtype_code(x), T, _ptr(out), _stream(stream)))
+        return out
+
+    def forward_host(self, x_host, out_host, stream=None):
+        from .umsx import _dtype_code, _ptr, _stream, check, lib
+        check(lib().umsx_ep_prefill_forward_host(self._h, _ptr(x_host), _dtype_code(x_host), x_host.shape[0],
+                                                 _ptr(out_host), _stream(stream)))
+        return out_host
+
+    def loads(self):
+        """Per layer of the last call: (rows received, expert jobs run) on this rank, int32 [layers, 2]."""
+        import ctypes as C
+
+        import numpy as np
+
+        from .umsx import check, lib
+        a = np.zeros((len(self.layers), 2), dtype=np.int32)
+        check(lib().umsx_ep_prefill_loads(self._h, C.c_void_p(a.ctypes.data), a.size))
+        return a
+
+    def status(self, stream=None):
+        from .umsx import _stream, check, lib
+        check(lib().umsx_ep_prefill_status(self._h, _stream(stream)))
+
+    def close(self):
+        from .umsx import lib
+        if self._h:
+            lib().umsx_ep_prefill_destroy(self._h)
+            self._h = None

@@ -41,7 +41,9 @@ EXPORTS = ["umsx_moe_create", "umsx_moe_create_synthetic", "umsx_moe_destroy", "
            "umsx_stack_forward_host", "umsx_stack_status", "umsx_stack_set_timing", "umsx_stack_stage_times", "umsx_stack_inject_fault",
            "umsx_route_static", "umsx_ep_create", "umsx_ep_handle", "umsx_ep_connect", "umsx_ep_set_wait",
            "umsx_ep_destroy", "umsx_ep_stack_create", "umsx_ep_stack_destroy", "umsx_ep_stack_forward",
-           "umsx_ep_stack_forward_host", "umsx_ep_stack_status",
+           "umsx_ep_stack_forward_host", "umsx_ep_stack_status", "umsx_ep_prefill_create", "umsx_ep_prefill_handle",
+           "umsx_ep_prefill_connect", "umsx_ep_prefill_forward", "umsx_ep_prefill_forward_host", "umsx_ep_prefill_loads",
+           "umsx_ep_prefill_status", "umsx_ep_prefill_destroy",
            "umsx_gguf_load_experts", "umsx_gguf_experts_free", "umsx_moe_create_gguf",
            "umsx_kernel_launches", "umsx_last_error", "umsx_version"]
 
@@ -121,6 +123,14 @@ def lib():
         "umsx_ep_stack_forward": (i32, [vp, vp, i32, vp, vp]),
         "umsx_ep_stack_forward_host": (i32, [vp, vp, i32, vp, vp]),
         "umsx_ep_stack_status": (i32, [vp, vp]),
+        "umsx_ep_prefill_create": (i32, [vp, C.POINTER(vp), i32, i32, C.c_float, C.POINTER(vp)]),
+        "umsx_ep_prefill_handle": (i32, [vp, vp, sz]),
+        "umsx_ep_prefill_connect": (i32, [vp, vp, sz]),
+        "umsx_ep_prefill_forward": (i32, [vp, vp, i32, i32, vp, vp]),
+        "umsx_ep_prefill_forward_host": (i32, [vp, vp, i32, i32, vp, vp]),
+        "umsx_ep_prefill_loads": (i32, [vp, vp, i32]),
+        "umsx_ep_prefill_status": (i32, [vp, vp]),
+        "umsx_ep_prefill_destroy": (None, [vp]),
         "umsx_gguf_load_experts": (i32, [C.c_char_p, i32, vp, i32, i32, C.POINTER(GgufExpertsC)]),
         "umsx_gguf_experts_free": (None, [C.POINTER(GgufExpertsC)]),
         "umsx_moe_create_gguf": (i32, [C.POINTER(Desc), C.c_char_p, i32, i32, sz, C.POINTER(vp)]),
