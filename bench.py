@@ -65,8 +65,9 @@ def parse():
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the ranks (prefill)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1 decode as independent replicas instead of expert parallelism")
-    ap.add_argument("--config", choices=("stack", "skew"), default="stack",
-                    help="stack: configs[2] (the headline); skew: configs[3] load-skew layers at T=4096")
+    ap.add_argument("--config", choices=("stack", "skew", "bank"), default="stack",
+                    help="stack: configs[2] (the headline); skew: configs[3] load-skew layers at T=4096; "
+                         "bank: a residency-banked GPT-OSS-120B-shaped layer (LFU / LRU)")
     a = ap.parse_args()
     if a.tokens is None:
         a.tokens = 1 if a.mode == "decode" else 4096
@@ -674,6 +675,113 @@ def prefill_record(pkg, cfg, layers, dev, a, tokens: int = 4096, steps: int = 5,
             "clocks": clk.summary(), "l2": "inputs larger than L2 (61 GB of weights, 4096 x 2880 activations)"}
 
 
+def skew_router(pkg, cfg):
+    """configs[3]'s router: weights N(0, router_sigma) (seeded numpy draws) and the bias
+    log(Zipf(1.2) popularity) + N(0, 0.5) over the experts (configs.zipf_router_bias)."""
+    import numpy as np
+    rng = np.random.default_rng(cfg.seed + 77)
+    rw = (rng.standard_normal((cfg.experts, cfg.hidden)) * cfg.router_sigma).astype(np.float32)
+    return rw, pkg.configs.zipf_router_bias(cfg.experts, seed=cfg.seed)
+
+
+def random_host_layer(cfg, seed: int) -> dict:
+    """Host weights of one MXFP4 fused layer in ggml layout, drawn with numpy: codes uniform over the
+    16 e2m1 codes, block exponents 119..123 (2^-8 .. 2^-4), bf16 biases N(0, bias_sigma)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    E, H, I = cfg.experts, cfg.hidden, cfg.intermediate
+
+    def blocks(rows, cols):
+        b = rng.integers(0, 256, size=(E, rows, cols // 32, 17), dtype=np.uint8)
+        b[..., 0] = rng.integers(119, 124, size=(E, rows, cols // 32), dtype=np.uint8)
+        return b.reshape(E, rows, cols // 32 * 17)
+
+    def bf16(n):
+        return ((rng.standard_normal(n) * cfg.bias_sigma).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+    return {"router_w": (rng.standard_normal((E, H)) * cfg.router_sigma).astype(np.float32),
+            "router_b": (rng.standard_normal(E) * cfg.router_bias_sigma).astype(np.float32),
+            "gate_up": blocks(2 * I, H), "down": blocks(H, I),
+            "gate_up_bias": bf16(E * 2 * I).reshape(E, 2 * I), "down_bias": bf16(E * H).reshape(E, H)}
+
+
+def bank_arm(a):
+    """Expert residency (the reference's hybrid expert cache, row (f)4): a GPT-OSS-120B-shaped layer
+    (128 MXFP4 experts, 1.7 GB) kept in pinned host memory, `slots` experts resident in a device bank
+    admitted by the reference's LFU or LRU rule, the others uploaded for the call that needs them; one
+    token per call (the reference admits on single-token dispatches), routed by configs[3]'s Zipf(1.2)
+    router bias so that a bank of a quarter or half of the experts can hold the hot ones.  Per policy and
+    bank size: tokens/s (CUDA events around the timed calls; every call synchronises with the host once
+    for its routing), hit rate, uploads per token; the resident layer on the same weights times the same
+    calls for comparison."""
+    import numpy as np
+    import torch
+    pkg = load_pkg()
+    U = pkg.umsx
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = pkg.configs.GPT_OSS_120B
+    if a.experts:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, experts=a.experts)
+    w = random_host_layer(cfg, 2024)
+    rw, rb = skew_router(pkg, cfg)
+    w["router_w"], w["router_b"] = rw, rb
+    steps, warmup = max(a.steps, 64), max(a.warmup, 32)
+    rng = np.random.default_rng(5)
+    pool = warmup + steps  # every call routes a token of its own
+    xs = torch.from_numpy(rng.standard_normal((pool, 1, cfg.hidden)).astype(np.float32)).to(torch.bfloat16).to(dev)
+    out = torch.empty((1, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def run(layer, first, n):
+        for i in range(first, first + n):
+            layer.forward(xs[i % pool], out)
+
+    def timed(layer, first, steps):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run(layer, first, steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    resident = pkg.MoeLayer(cfg.desc(1), w, device=0)
+    run(resident, 0, warmup)
+    res_ms = timed(resident, warmup, steps)
+    resident.close()
+    per_expert = 3 * cfg.intermediate * (cfg.hidden // 32) * 17
+    records = {}
+    with Clocks(0) as clk:
+        for policy, pname in ((U.BANK_LFU, "lfu"), (U.BANK_LRU, "lru")):
+            for slots in (cfg.experts // 8, cfg.experts // 4, cfg.experts // 2):
+                layer = pkg.MoeLayer(cfg.desc(1), w, bank=(slots, policy), device=0)
+                run(layer, 0, warmup)  # the warm-up calls fill the bank
+                before = layer.bank_stats()
+                ms = timed(layer, warmup, steps)
+                after = layer.bank_stats()
+                d = {k: after[k] - before[k] for k in U.BANK_STAT_NAMES}
+                records[f"{pname}_{slots}"] = {
+                    "policy": pname, "slots": slots, "tokens_per_s": 1e3 / ms, "ms_per_token": ms,
+                    "hit_rate": d["hits"] / max(1, d["demands"]), "admissions_per_token": d["admissions"] / steps,
+                    "transient_uploads_per_token": d["transient"] / steps,
+                    "upload_gb_per_s": d["upload_bytes"] / (ms * steps / 1e3) / 1e9,
+                    "upload_bytes_per_token": d["upload_bytes"] / steps}
+                layer.close()
+    head = records[f"lfu_{cfg.experts // 4}"]
+    res = {"metric": "banked MoE-layer tokens/s (GPT-OSS-120B-shaped layer, 128 experts in host memory, "
+                     "one token per call, Zipf(1.2) routing)",
+           "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": warmup,
+           "ms_per_step": head["ms_per_token"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
+           "config": {"workload": "gpt-oss-120b layer, residency bank (LFU, 32 of 128 experts resident)",
+                      "experts": cfg.experts, "top_k": cfg.top_k, "hidden": cfg.hidden, "ffn": cfg.intermediate,
+                      "expert_bytes": per_expert, "routing": "configs[3] Zipf(1.2) router bias"},
+           "resident_ms_per_token": res_ms, "bank": records, "clocks": clk.summary()}
+    print(json.dumps(res))
+
+
 def skew_arm(a):
     """Qwen3-30B-A3B layer shapes in Q8_0 and MXFP4 with the Zipf(1.2) router bias, T = 4096
     tokens per step on one GPU: tokens/s, p50 / p99 layer latency over the steps (CUDA events per step,
@@ -690,11 +798,7 @@ def skew_arm(a):
     for name in ("qwen3-skew-q8_0", "qwen3-skew-mxfp4"):
         cfg = pkg.configs.CONFIGS[name]
         layer = pkg.MoeLayer(cfg.desc(max_tokens=T), synthetic=cfg.synthetic(), device=0)
-        from oracle.oracle import Oracle  # the host twin of the device router weights (generator only)
-        orc = Oracle()
-        rw = orc.gen_normal_f32(cfg.seed, pkg.configs.stream_id(0, pkg.configs.KIND_ROUTER_W), 0,
-                                cfg.experts * cfg.hidden, cfg.router_sigma).reshape(cfg.experts, cfg.hidden)
-        layer.set_router(rw, pkg.configs.zipf_router_bias(cfg.experts, seed=cfg.seed))
+        layer.set_router(*skew_router(pkg, cfg))
         rng = np.random.default_rng(3000)
         xs = [torch.from_numpy(rng.standard_normal((T, cfg.hidden)).astype(np.float32)).to(torch.bfloat16).to(dev)
               for _ in range(8)]
@@ -779,10 +883,7 @@ def ep_arm(a):
         H, K = cfg.hidden, cfg.top_k
         router = None
         if a.config == "skew":
-            from oracle.oracle import Oracle  # the host twin of the device router weights (generator only)
-            rw = Oracle().gen_normal_f32(cfg.seed, pkg.configs.stream_id(0, pkg.configs.KIND_ROUTER_W), 0,
-                                         cfg.experts * H, cfg.router_sigma).reshape(cfg.experts, H)
-            router = (rw, pkg.configs.zipf_router_bias(cfg.experts, seed=cfg.seed))
+            router = skew_router(pkg, cfg)
 
         def make(l, **kw):
             m = pkg.MoeLayer(cfg.desc(max_tokens=kw.pop("max_tokens"), **kw), synthetic=cfg.synthetic(layer=l),
@@ -952,6 +1053,8 @@ def main():
         ep_arm(a)
     elif a.config == "skew":
         skew_arm(a)
+    elif a.config == "bank":
+        bank_arm(a)
     elif a.impl == "reference":
         reference_arm(a)
     else:
