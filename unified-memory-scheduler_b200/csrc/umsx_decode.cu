@@ -287,7 +287,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
         if (warp < T) {
             int sel;
             float w;
-            select_topk<kDecodeMaxExperts / 32>(p.logits + (size_t)warp * E, E, K, p.routing, p.routed_scale, lane, sel, w);
+            // as many candidates per lane as the router has experts (the same picks, a shorter chain)
+            if (E <= 128)
+                select_topk<4>(p.logits + (size_t)warp * E, E, K, p.routing, p.routed_scale, lane, sel, w);
+            else
+                select_topk<kDecodeMaxExperts / 32>(p.logits + (size_t)warp * E, E, K, p.routing, p.routed_scale, lane, sel, w);
             if (lane < K) { sel_e[warp * K + lane] = sel; sel_w[warp * K + lane] = w; }
         }
         __syncthreads();
