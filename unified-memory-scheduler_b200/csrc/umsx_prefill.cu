@@ -301,38 +301,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             const bool valid = mrow < p.rows;
             const int grp = valid ? prow >> 4 : 0, rr = prow & 15;
             const int emax = valid ? __ldg(eb + (size_t)e * p.plane_rows + prow) : 0;
-            const uint8_t *codes = cb + ((size_t)e * nrg + grp) * (size_t)nbK * 256;
-            const uint8_t *scl = sb + ((size_t)e * nrg + grp) * (size_t)quads * 128;
             uint8_t *rowA = sA + r * 128;
-            // this row's raw bytes, kRaw - 1 stages ahead (each thread copies and reads only its own row)
+            // The warp's 32 rows are two 16-row groups of the plane; per K stage (block pair) a row group's
+            // codes are one 512-byte chunk and its exponent quad one 128-byte chunk.  The warp copies them
+            // 16 bytes a lane (cp.async, L2 only) kRaw - 1 stages ahead into its own raw area; each thread
+            // then reads its row's four code words and two exponent words there.
+            const int j = lane >> 4;  // this thread's row group within the warp
+            const uint8_t *chunk_codes[2], *chunk_scl[2];
+            bool rg_valid[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int src_lane = q * 16;  // the first row of row group q
+                const int g_q = __shfl_sync(kFull, grp, src_lane);
+                rg_valid[q] = __shfl_sync(kFull, (int)valid, src_lane) != 0;
+                chunk_codes[q] = cb + ((size_t)e * nrg + g_q) * (size_t)nbK * 256;
+                chunk_scl[q] = sb + ((size_t)e * nrg + g_q) * (size_t)quads * 128;
+            }
+            uint8_t *wraw = reinterpret_cast<uint8_t *>(sRaw) + (size_t)(warp & 3) * 2 * 640;  // [stage stride below]
+            constexpr size_t kRawStage = 4 * 2 * 640;  // four producer warps x two row groups x (512 + 128) bytes
             auto fetch = [&](int kk) {
-                if (kk < nk && valid) {
-                    RawRow *d = sRaw + (kk % kRaw) * kBM + r;
+                if (kk < nk) {
+                    uint8_t *d = wraw + (size_t)(kk % kRaw) * kRawStage;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h)
-#pragma unroll
-                        for (int lh = 0; lh < 2; ++lh)
-                            tc::cp_async8(&d->w[2 * h + lh], codes + (size_t)kk * 512 + lh * 256 + (16 * h + rr) * 8);
-                    tc::cp_async4(&d->e[0], scl + (size_t)(kk >> 2) * 128 + rr * 4);
-                    tc::cp_async4(&d->e[1], scl + (size_t)(kk >> 2) * 128 + (16 + rr) * 4);
+                    for (int q = 0; q < 2; ++q) {
+                        if (!rg_valid[q]) continue;
+                        cp_async16(d + q * 640 + lane * 16, chunk_codes[q] + (size_t)kk * 512 + lane * 16);
+                        if (lane < 8) cp_async16(d + q * 640 + 512 + lane * 16, chunk_scl[q] + (size_t)(kk >> 2) * 128 + lane * 16);
+                    }
                 }
                 cp_async_commit();
             };
 #pragma unroll
-            for (int j = 0; j < kRaw - 1; ++j) fetch(j);
+            for (int jj = 0; jj < kRaw - 1; ++jj) fetch(jj);
             for (int kk = 0; kk < nk; ++kk, ++g) {
                 const int s = g % kStagesA;
                 cp_async_wait<kRaw - 2>();
+                __syncwarp();  // every lane's pieces of stage kk have landed, and stage kk - 1 is read
                 fetch(kk + kRaw - 1);
                 uint2 w[2][2];
                 uint32_t ew = 0;
                 if (valid) {
-                    const RawRow *sr = sRaw + (kk % kRaw) * kBM + r;
+                    const uint8_t *sr = wraw + (size_t)(kk % kRaw) * kRawStage + j * 640;
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
 #pragma unroll
-                        for (int lh = 0; lh < 2; ++lh) w[h][lh] = sr->w[2 * h + lh];
-                    ew = ((sr->e[0] >> (8 * (kk & 3))) & 0xffu) | (((sr->e[1] >> (8 * (kk & 3))) & 0xffu) << 8);
+                        for (int lh = 0; lh < 2; ++lh)
+                            w[h][lh] = *reinterpret_cast<const uint2 *>(sr + lh * 256 + (16 * h + rr) * 8);
+                    const uint32_t e0 = *reinterpret_cast<const uint32_t *>(sr + 512 + rr * 4);
+                    const uint32_t e1 = *reinterpret_cast<const uint32_t *>(sr + 512 + (16 + rr) * 4);
+                    ew = ((e0 >> (8 * (kk & 3))) & 0xffu) | (((e1 >> (8 * (kk & 3))) & 0xffu) << 8);
                 }
                 wait_bar(&empty_a[s], ((g / kStagesA) & 1u) ^ 1u, p.err);
                 uint8_t *dst = rowA + s * kTileBytes;
