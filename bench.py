@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the bounded CPU sample")
     ap.add_argument("--ref-seconds", type=float, default=150.0, help="timed budget of the --impl reference arm")
     ap.add_argument("--no-prefill", action="store_true", help="decode line without the prefill sub-record")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="decode line without the configs[3] skew and residency-bank sub-records")
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the ranks (prefill)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1 decode as independent replicas instead of expert parallelism")
@@ -624,6 +626,21 @@ def gpu_arm(a):
     stack.close()
     for l in layers:
         l.close()
+    if world == 1 and a.mode == "decode" and not a.no_extra:
+        # configs[3] (load skew, T = 4096) and the residency bank, measured in the same run
+        import argparse
+        torch.cuda.empty_cache()
+        for name, fn, steps, warmup in (("skew", skew_arm, 20, 3), ("bank", bank_arm, 128, 64)):
+            sub = argparse.Namespace(**vars(a))
+            sub.steps, sub.warmup, sub.tokens, sub.experts = steps, warmup, 4096, None
+            try:
+                r = fn(sub, emit=False)
+                res[name] = {k: r.get(k) for k in ("metric", "value", "unit", "steps", "warmup", "ms_per_step", "config")}
+                res[name]["detail"] = r.get("skew") or {"resident_ms_per_token": r.get("resident_ms_per_token"),
+                                                        "bank": r.get("bank")}
+            except Exception as exc:  # the decode line must still be printed
+                res[name] = {"error": str(exc)[:200]}
+            torch.cuda.empty_cache()
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
@@ -705,7 +722,7 @@ def random_host_layer(cfg, seed: int) -> dict:
             "gate_up_bias": bf16(E * 2 * I).reshape(E, 2 * I), "down_bias": bf16(E * H).reshape(E, H)}
 
 
-def bank_arm(a):
+def bank_arm(a, emit: bool = True):
     """Expert residency (the reference's hybrid expert cache, row (f)4): a GPT-OSS-120B-shaped layer
     (128 MXFP4 experts, 1.7 GB) kept in pinned host memory, `slots` experts resident in a device bank
     admitted by the reference's LFU or LRU rule, the others uploaded for the call that needs them; one
@@ -779,10 +796,12 @@ def bank_arm(a):
                       "experts": cfg.experts, "top_k": cfg.top_k, "hidden": cfg.hidden, "ffn": cfg.intermediate,
                       "expert_bytes": per_expert, "routing": "configs[3] Zipf(1.2) router bias"},
            "resident_ms_per_token": res_ms, "bank": records, "clocks": clk.summary()}
-    print(json.dumps(res))
+    if emit:
+        print(json.dumps(res))
+    return res
 
 
-def skew_arm(a):
+def skew_arm(a, emit: bool = True):
     """Qwen3-30B-A3B layer shapes in Q8_0 and MXFP4 with the Zipf(1.2) router bias, T = 4096
     tokens per step on one GPU: tokens/s, p50 / p99 layer latency over the steps (CUDA events per step,
     inputs from a pool of 8 seeded batches), per-expert load and the per-GPU load an expert-parallel
@@ -831,7 +850,9 @@ def skew_arm(a):
            "config": {"workload": "qwen3-30b-a3b skew layer (Q8_0 headline value; MXFP4 in the sub-record)",
                       "tokens": T, "experts": 128, "top_k": 8, "hidden": 2048, "ffn": 768},
            "skew": out_rec}
-    print(json.dumps(res))
+    if emit:
+        print(json.dumps(res))
+    return res
 
 
 def ep_arm(a):
