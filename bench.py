@@ -67,9 +67,10 @@ def parse():
     ap.add_argument("--ep", action="store_true", help="expert parallelism over the ranks (prefill)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1 decode as independent replicas instead of expert parallelism")
-    ap.add_argument("--config", choices=("stack", "skew", "bank"), default="stack",
+    ap.add_argument("--config", choices=("stack", "skew", "bank", "configs"), default="stack",
                     help="stack: configs[2] (the headline); skew: configs[3] load-skew layers at T=4096; "
-                         "bank: a residency-banked GPT-OSS-120B-shaped layer (LFU / LRU)")
+                         "bank: a residency-banked GPT-OSS-120B-shaped layer (LFU / LRU); "
+                         "configs: configs[1] (T=1, 16) and configs[4] (27 layers, T=1)")
     a = ap.parse_args()
     if a.tokens is None:
         a.tokens = 1 if a.mode == "decode" else 4096
@@ -630,14 +631,15 @@ def gpu_arm(a):
         # configs[3] (load skew, T = 4096) and the residency bank, measured in the same run
         import argparse
         torch.cuda.empty_cache()
-        for name, fn, steps, warmup in (("skew", skew_arm, 20, 3), ("bank", bank_arm, 128, 64)):
+        for name, fn, steps, warmup in (("skew", skew_arm, 20, 3), ("bank", bank_arm, 128, 64),
+                                        ("configs", configs_record, 64, 8)):
             sub = argparse.Namespace(**vars(a))
             sub.steps, sub.warmup, sub.tokens, sub.experts = steps, warmup, 4096, None
             try:
                 r = fn(sub, emit=False)
                 res[name] = {k: r.get(k) for k in ("metric", "value", "unit", "steps", "warmup", "ms_per_step", "config")}
-                res[name]["detail"] = r.get("skew") or {"resident_ms_per_token": r.get("resident_ms_per_token"),
-                                                        "bank": r.get("bank")}
+                res[name]["detail"] = r.get("skew") or r.get("configs") or {
+                    "resident_ms_per_token": r.get("resident_ms_per_token"), "bank": r.get("bank")}
             except Exception as exc:  # the decode line must still be printed
                 res[name] = {"error": str(exc)[:200]}
             torch.cuda.empty_cache()
@@ -690,6 +692,75 @@ def prefill_record(pkg, cfg, layers, dev, a, tokens: int = 4096, steps: int = 5,
                          "frac_of_nominal_fp4_dense_9000": gu_tf / 9000.0},
             "layer_tflops_useful": (gu_flops + dn_flops) / ((stages["gate_up"] + stages["down"]) / 1e3) / 1e12,
             "clocks": clk.summary(), "l2": "inputs larger than L2 (61 GB of weights, 4096 x 2880 activations)"}
+
+
+def configs_record(a, emit: bool = False) -> dict:
+    """The other BASELINE configurations timed on one GPU through the public API: configs[1] (Qwen3-30B-
+    A3B-shaped Q8_0 layer, T = 1 and 16; four seeded layers cycled so that consecutive calls read other
+    weights) and configs[4] (the DeepSeek-V2-Lite-shaped 27-layer block: dense layer 0, 26 MoE layers
+    with shared experts, T = 1).  Tokens/s, and the HBM roofline fraction of the algorithmic bytes
+    (the expected distinct experts a call touches, the router, and for configs[4] the dense and shared
+    FFNs) over the measured copy peak."""
+    import torch
+    pkg = load_pkg()
+    C = pkg.configs
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(5)
+    peak, kind = peaks()
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+
+    def clocked(fn, steps, warmup):
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            fn(warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    c1 = C.QWEN3_30B
+    layers = [pkg.MoeLayer(c1.desc(16), synthetic=c1.synthetic(layer=l), device=0) for l in range(4)]
+    for T in (1, 16):
+        xs = [torch.randn(T, c1.hidden, device=dev).to(torch.bfloat16) for _ in range(7)]
+        o = torch.empty((T, c1.hidden), dtype=torch.float32, device=dev)
+        ms = clocked(lambda i: layers[i % 4].forward(xs[i % 7], o), max(a.steps, 64), 8)
+        distinct = c1.experts * (1 - (1 - c1.top_k / c1.experts) ** T)
+        b = distinct * c1.expert_bytes() + c1.router_bytes()
+        out[f"qwen3_30b_T{T}"] = {"tokens_per_s": T / (ms / 1e3), "ms_per_layer": ms, "bytes_per_call": b,
+                                 "achieved_gbs": b / (ms / 1e3) / 1e9, "frac": b / (ms / 1e3) / 1e9 / peak}
+    for l in layers:
+        l.close()
+    torch.cuda.empty_cache()
+    import importlib
+    mixed = importlib.import_module(pkg.__name__ + ".mixed")
+    stack, layers, shared = mixed.deepseek_v2_lite_stack(C.DEEPSEEK_V2_LITE.layers, max_tokens=1)
+    xs = [torch.randn(1, C.DEEPSEEK_V2_LITE.hidden, device=dev).to(torch.bfloat16) for _ in range(16)]
+    o = torch.empty((1, C.DEEPSEEK_V2_LITE.hidden), dtype=torch.float32, device=dev)
+    ms = clocked(lambda i: stack.forward(xs[i % 16], o), max(a.steps // 4, 20), 3)
+    r, sh, dn = C.DEEPSEEK_V2_LITE, C.DEEPSEEK_V2_LITE_SHARED, C.DEEPSEEK_V2_LITE_DENSE
+    b = (dn.expert_bytes() + dn.router_bytes() +
+         26 * (r.top_k * r.expert_bytes() + r.router_bytes() + sh.expert_bytes() + sh.router_bytes()))
+    out["deepseek_v2_lite_27_T1"] = {"tokens_per_s": 1e3 / ms, "ms_per_token": ms, "bytes_per_token": b,
+                                     "achieved_gbs": b / (ms / 1e3) / 1e9, "frac": b / (ms / 1e3) / 1e9 / peak}
+    stack.close()
+    for l in layers + [x for x in shared if x is not None]:
+        l.close()
+    torch.cuda.empty_cache()
+    res = {"metric": "MoE tokens/s on the other BASELINE configurations (configs[1], configs[4])",
+           "value": out["qwen3_30b_T1"]["tokens_per_s"], "unit": "tokens/s", "steps": max(a.steps, 64),
+           "warmup": 8, "ms_per_step": out["qwen3_30b_T1"]["ms_per_layer"],
+           "config": {"workload": "configs[1] Qwen3-30B-A3B layer (Q8_0) T=1 headline value; T=16 and "
+                                  "configs[4] DeepSeek-V2-Lite 27-layer T=1 in the detail",
+                      "peak_source": f"{kind} hbm_gbs"},
+           "configs": out}
+    if emit:
+        print(json.dumps(res))
+    return res
 
 
 def skew_router(pkg, cfg):
@@ -1076,6 +1147,8 @@ def main():
         skew_arm(a)
     elif a.config == "bank":
         bank_arm(a)
+    elif a.config == "configs":
+        configs_record(a, emit=True)
     elif a.impl == "reference":
         reference_arm(a)
     else:
