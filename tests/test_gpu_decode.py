@@ -37,6 +37,29 @@ def test_decode_layer_bit_exact(oracle, tokens):
     layer.close()
 
 
+def test_decode_low_block_exponents_bit_exact(oracle):
+    """Blocks with exponent bytes 0, 1 and 2 (subnormal block scales for 0 and 1): such a layer takes
+    the general scale rule instead of the normal-scale form, and the one-launch kernel stays bit-exact."""
+    from tests.helpers import weights_dict
+    cfg = small_config()
+    import dataclasses
+    w = host_weights(oracle, cfg)
+    w = dataclasses.replace(w, gate_up=w.gate_up.copy(), down=w.down.copy())
+    rng = np.random.default_rng(5)
+    for arr in (w.gate_up, w.down):
+        blocks = arr.reshape(-1, 17)
+        idx = rng.choice(blocks.shape[0], size=blocks.shape[0] // 8, replace=False)
+        blocks[idx, 0] = rng.integers(0, 3, size=idx.size, dtype=np.uint8)
+    xb = x_bits(oracle, cfg, 1)
+    want = oracle.moe_layer(oracle_desc(cfg), w, bf16_bits_to_f32(xb), threads=8)
+    layer = U.MoeLayer(cfg.desc(1), weights_dict(w))
+    launches = U.kernel_launches()
+    out = layer.forward(to_cuda_bf16(xb)).cpu().numpy()
+    assert U.kernel_launches() - launches == 1, "expected the single persistent launch"
+    np.testing.assert_array_equal(bits(out), bits(want["out"]))
+    layer.close()
+
+
 @pytest.mark.parametrize("tokens", [1, 3])
 def test_decode_stack_bit_exact(oracle, tokens):
     cfg = small_config()

@@ -294,12 +294,25 @@ umsx_status generate_matrix(Matrix &mm, uint64_t seed, uint64_t stream, int e_gl
     return UMSX_OK;
 }
 
-// Row exponent maxima of the MXFP4 matrices (the prefill path's f16 rebase).
+// Row exponent maxima of the MXFP4 matrices (the prefill path's f16 rebase), and whether every block
+// exponent of a matrix is >= 2 (Matrix::exp_ge2: the decode kernels then take the normal-scale form).
 umsx_status compute_row_emax(umsx_moe *m) {
     if (m->d.quant != UMSX_QUANT_MXFP4) return UMSX_OK;
-    for (Matrix *mm : {&m->gate_up, &m->gate, &m->up, &m->down})
-        if (mm->codes) UMSX_LAUNCHED(launch_row_emax(*mm, m->e_local, mm->emax, 0));
-    return UMSX_OK;
+    uint32_t *low = nullptr;
+    UMSX_CUDA(cudaMalloc(&low, 4 * 4));
+    auto run = [&]() -> umsx_status {
+        UMSX_CUDA(cudaMemset(low, 0, 4 * 4));
+        Matrix *mats[4] = {&m->gate_up, &m->gate, &m->up, &m->down};
+        for (int i = 0; i < 4; ++i)
+            if (mats[i]->codes) UMSX_LAUNCHED(launch_row_emax(*mats[i], m->e_local, mats[i]->emax, low + i, 0));
+        uint32_t h[4] = {1, 1, 1, 1};
+        UMSX_CUDA(cudaMemcpy(h, low, sizeof(h), cudaMemcpyDeviceToHost));
+        for (int i = 0; i < 4; ++i) mats[i]->exp_ge2 = mats[i]->codes && h[i] == 0;
+        return UMSX_OK;
+    };
+    const umsx_status st = run();
+    cudaFree(low);
+    return st;
 }
 
 size_t max_expert_bytes(const umsx_moe *m) {
@@ -601,6 +614,8 @@ DecodeLayer decode_layer(const umsx_moe *m) {
     L.dn_codes = m->down.codes;
     L.dn_scales = m->down.scales;
     L.dn_bias = m->down_bias;
+    L.gu_ge2 = m->gate_up.exp_ge2;
+    L.dn_ge2 = m->down.exp_ge2;
     return L;
 }
 

@@ -366,7 +366,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
 #pragma unroll
                     for (int t = 0; t < MT; ++t) trow[t] = t < m ? job_j[jf + c0 + t] / K : 0;
                     float acc[MT][4];
-                    mx_warp_dot_ring<MT, S>(ws, lh, xs, nb, m, lane, acc, trow);
+                    if (Ld.gu_ge2) mx_warp_dot_ring<MT, S, true>(ws, lh, xs, nb, m, lane, acc, trow);
+                    else mx_warp_dot_ring<MT, S, false>(ws, lh, xs, nb, m, lane, acc, trow);
                     mx_chain_combine<MT>(acc);
                     if (lh == 1 && lane < 16)
 #pragma unroll
@@ -465,7 +466,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
 #pragma unroll
                     for (int t = 0; t < MT; ++t) trow[t] = t < m ? jf + c0 + t - jb : 0;
                     float acc[MT][4];
-                    mx_warp_dot_ring<MT, S>(ws, lh, as, nbI, m, lane, acc, trow, primed && v == v_lo + di && c0 == 0);
+                    if (Ld.dn_ge2) mx_warp_dot_ring<MT, S, true>(ws, lh, as, nbI, m, lane, acc, trow, primed && v == v_lo + di && c0 == 0);
+                    else mx_warp_dot_ring<MT, S, false>(ws, lh, as, nbI, m, lane, acc, trow, primed && v == v_lo + di && c0 == 0);
                     mx_chain_combine<MT>(acc);
                     if (lh == 1 && lane < 16)
 #pragma unroll

@@ -33,6 +33,7 @@ struct Matrix {
     int rows = 0;               // N per expert
     int cols = 0;               // K
     int quant = 0;
+    int exp_ge2 = 0;            // MXFP4: every block exponent is >= 2 (normal block scales; set at create time)
     size_t code_bytes_per_expert() const { return (size_t)rows * (cols / 32) * (quant == UMSX_QUANT_MXFP4 ? 16 : 32); }
     size_t scale_bytes_per_expert() const {
         if (quant == UMSX_QUANT_MXFP4) return (size_t)(rows / 16) * (((cols / 64) + 3) / 4) * 128;
@@ -136,6 +137,7 @@ struct DecodeLayer {
     const uint8_t *dn_codes;  // down planes [E][H][I]
     const uint8_t *dn_scales;
     const float *dn_bias;     // [E][H] or null
+    int gu_ge2, dn_ge2;       // Matrix::exp_ge2 of the two matrices
 };
 
 struct DecodeParams {
@@ -194,7 +196,8 @@ struct MoeGemmParams {
 // Router for many tokens: tiled logits (same arithmetic as launch_router), per-token selection and
 // x -> Q8_0 (lane-pair order), then the dispatch build.
 int launch_router_tiled(const RouterParams &p, const Dispatch &d, cudaStream_t s);
-int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, cudaStream_t s);
+// Also ORs 1 into *low (if not null) when a block exponent of the matrix is below 2.
+int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, uint32_t *low, cudaStream_t s);
 // n_jobs: device count of the resident experts' jobs (offsets[e_local]) bounding `jobs`, or null.
 int launch_prefill_pack(const Dispatch &d, int jobs, const int32_t *n_jobs, int K, int hidden, void *a_hi, void *a_lo,
                         int32_t *inv, cudaStream_t s);

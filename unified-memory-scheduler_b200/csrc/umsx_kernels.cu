@@ -905,7 +905,8 @@ __global__ void __launch_bounds__(128) k_gate_up_mx(GateUpParams p, Dispatch d) 
             return;
         }
         float acc[MT][4];
-        mx_warp_dot_ring<MT, S>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
+        if (mat.exp_ge2) mx_warp_dot_ring<MT, S, true>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
+        else mx_warp_dot_ring<MT, S, false>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
         mx_chain_combine<MT>(acc);
         if (lh == 1 && lane < 16)
 #pragma unroll
@@ -1010,7 +1011,8 @@ __global__ void __launch_bounds__(W * 64) k_gemv_mx(GemvParams p, GemvSrc src, D
         __syncthreads();
         float acc[MT][4];
         if (active_rg) {
-            mx_warp_dot_ring<MT, S>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
+            if (p.m.exp_ge2) mx_warp_dot_ring<MT, S, true>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
+            else mx_warp_dot_ring<MT, S, false>(ws, lh, st, nb, m, lane, acc, trow, c0 == 0);
             mx_chain_combine<MT>(acc);
             if (lh == 1 && lane < 16)
 #pragma unroll

@@ -143,8 +143,19 @@ __device__ __forceinline__ size_t scale_offset(int quant, int e, int nrg, int rg
     return ((size_t)e * nrg + rg) * (size_t)chunks * 128;
 }
 
+// Block scale 2^(e-128) of exponent byte i of a lane's quad word.  GE2: every exponent of the
+// matrix is >= 2 (checked at create time), where the scale is the normal float (e - 1) << 23,
+// taken from ew - 0x01010101 (no byte borrows then) with one shift and one mask; otherwise the
+// general rule, subnormal for e < 2.  Both give the same bits where GE2 holds.
+template <bool GE2, int I>
+__device__ __forceinline__ float quad_scale(uint32_t ew, uint32_t ewm) {
+    if (!GE2) return e8m0_half((ew >> (8 * I)) & 0xffu);
+    constexpr int sh = 23 - 8 * I;
+    return __uint_as_float((sh >= 0 ? ewm << (sh >= 0 ? sh : 0) : ewm >> (sh >= 0 ? 0 : -sh)) & 0x7f800000u);
+}
+
 template <int MT>
-__device__ __forceinline__ void mx_half(uint2 wq, uint32_t e8, const uint4 *aq, const float *sc, int nb, int scs,
+__device__ __forceinline__ void mx_half(uint2 wq, float eh, const uint4 *aq, const float *sc, int nb, int scs,
                                         int m, float (&acc)[MT][4], const int (&trow)[MT]) {
     uint32_t pos[4], neg[4];
 #pragma unroll
@@ -155,7 +166,6 @@ __device__ __forceinline__ void mx_half(uint2 wq, uint32_t e8, const uint4 *aq, 
         pos[2 * q + 1] = prmt(kMagLo, kMagHi, w >> 16);
         neg[2 * q + 1] = prmt(kMagLo, kMagHi, n >> 16);
     }
-    const float eh = e8m0_half(e8);
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
         if (t < m) {
@@ -216,7 +226,8 @@ struct MxRing {
 
 // mx_warp_dot over a cp.async ring of S stages.
 // primed: the caller has already issued the ring's first S - 1 stages (mx_ring_prime).
-template <int MT, int S>
+// GE2: every block exponent of the matrix is >= 2 (quad_scale).
+template <int MT, int S, bool GE2 = false>
 __device__ __forceinline__ void mx_warp_dot_ring(const MxRing &ws, int lh, const Staged &a, int nb, int m, int lane,
                                                  float (&acc)[MT][4], const int (&trow)[MT], bool primed = false) {
 #pragma unroll
@@ -236,12 +247,18 @@ __device__ __forceinline__ void mx_warp_dot_ring(const MxRing &ws, int lh, const
         ws.issue<S>(j + S - 1, lane);
         const uint8_t *st = ws.ring + (j % S) * kRingStageBytes;
         const uint32_t ew = *reinterpret_cast<const uint32_t *>(st + 1024 + lane * 4);
+        const uint32_t ewm = ew - 0x01010101u;  // GE2 only (padding bytes past the last pair may borrow upward)
+        float eh[4];
+        eh[0] = quad_scale<GE2, 0>(ew, ewm);
+        eh[1] = quad_scale<GE2, 1>(ew, ewm);
+        eh[2] = quad_scale<GE2, 2>(ew, ewm);
+        eh[3] = quad_scale<GE2, 3>(ew, ewm);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int s = 4 * j + i;
             if (s < ws.steps) {
                 const uint2 wq = *reinterpret_cast<const uint2 *>(st + i * 256 + lane * 8);
-                mx_half<MT>(wq, (ew >> (8 * i)) & 0xffu, aq + (size_t)s * 8, sc + 2 * s, nb, a.scs, m, acc, trow);
+                mx_half<MT>(wq, eh[i], aq + (size_t)s * 8, sc + 2 * s, nb, a.scs, m, acc, trow);
             }
         }
     }

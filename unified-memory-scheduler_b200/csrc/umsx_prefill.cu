@@ -692,16 +692,21 @@ __global__ void k_prefill_scatter(const float *yj, const int32_t *inv, const int
 }
 
 // Largest block exponent of every row of an MXFP4 matrix (for the f16 rebase).
-__global__ void k_row_emax(Matrix m, int experts, uint8_t *emax) {
+__global__ void k_row_emax(Matrix m, int experts, uint8_t *emax, uint32_t *low) {
     const int nbK = m.cols / 32, nrg = m.rows / 16, quads = ((nbK / 2) + 3) / 4;
     const size_t total = (size_t)experts * m.rows;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int e = (int)(i / m.rows), row = (int)(i - (size_t)e * m.rows);
         const uint8_t *sc = m.scales + ((size_t)e * nrg + (row >> 4)) * (size_t)quads * 128;
-        uint32_t mx = 0;
+        uint32_t mx = 0, mn = 255;
         for (int pr = 0; pr < nbK / 2; ++pr)
-            for (int h = 0; h < 2; ++h) mx = max(mx, (uint32_t)sc[(size_t)(pr >> 2) * 128 + (16 * h + (row & 15)) * 4 + (pr & 3)]);
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t e = sc[(size_t)(pr >> 2) * 128 + (16 * h + (row & 15)) * 4 + (pr & 3)];
+                mx = max(mx, e);
+                mn = min(mn, e);
+            }
         emax[i] = (uint8_t)mx;
+        if (low && mn < 2) atomicOr(low, 1u);
     }
 }
 
@@ -735,8 +740,8 @@ int launch_router_tiled(const RouterParams &p, const Dispatch &d, cudaStream_t s
     return 2 + launch_dispatch(d, p.tokens * p.top_k, p.top_k, p.e_lo, p.e_local, s);
 }
 
-int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, cudaStream_t s) {
-    k_row_emax<<<592, 256, 0, s>>>(m, experts, emax);
+int launch_row_emax(const Matrix &m, int experts, uint8_t *emax, uint32_t *low, cudaStream_t s) {
+    k_row_emax<<<592, 256, 0, s>>>(m, experts, emax, low);
     return 1;
 }
 
