@@ -131,6 +131,42 @@ __device__ __forceinline__ void quantize_record(float v, uint8_t *rec, float *sc
     if (lane == 0) *scale = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
 }
 
+// Q8_0 records of n_blk 32-value blocks of src (block i = row i / nb, block i % nb, rows of width
+// H, each scaled by inv[row] first), eight threads per block with four values each, so a
+// block's scale takes three shuffles: thread j of a block holds elements 4j..4j+3, i.e. one code
+// word of the record.  Same codes and scales as quantize_record.  Called by whole warps
+// (first_warp .. first_warp + n_warps - 1, warp = this thread's warp).
+__device__ __forceinline__ void quantize_records4(const float *src, const float *inv, int n_blk, int nb, int H,
+                                                  uint8_t *rec, float *scale, int scale_stride, int warp, int lane,
+                                                  int first_warp, int n_warps) {
+    const int total = n_blk * 8;
+    for (int base = (warp - first_warp) * 32; base < total; base += n_warps * 32) {
+        const int it = base + lane;
+        const bool on = it < total;  // groups of 8 are all on or all off (total is a multiple of 8)
+        const int blk = on ? it >> 3 : 0, j = it & 7;
+        const int t = blk / nb, b = blk - t * nb;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (on) {
+            const float4 h = *reinterpret_cast<const float4 *>(src + (size_t)t * H + b * 32 + 4 * j);
+            const float sc = inv[t];
+            v = make_float4(__fmul_rn(h.x, sc), __fmul_rn(h.y, sc), __fmul_rn(h.z, sc), __fmul_rn(h.w, sc));
+        }
+        float am = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+        am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
+        if (on) {
+            const float qinv = am != 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+            const uint32_t w = ((uint32_t)q8_code(v.x, qinv) & 0xffu) | (((uint32_t)q8_code(v.y, qinv) & 0xffu) << 8) |
+                               (((uint32_t)q8_code(v.z, qinv) & 0xffu) << 16) | ((uint32_t)q8_code(v.w, qinv) << 24);
+            const int lh = j >> 2, pp = j & 3;
+            *reinterpret_cast<uint2 *>(rec + (size_t)blk * 64 + (lh * 2 + (pp >> 1)) * 16 + (pp & 1) * 8) =
+                make_uint2(w, neg8x4(w));
+            if (j == 0) scale[(size_t)t * scale_stride + b] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(am, 127.0f)));
+        }
+    }
+}
+
 // out4[i] = (residual ? h4[i] : 0) + sum_r w[t][r] * y[t*K + r] over float4 columns, rank order;
 // the loads of four ranks are in flight together.
 __device__ __forceinline__ float4 fold4(const float4 *y4, const float *w, int t, int K, int H4, int n4, float4 h,
@@ -267,11 +303,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             if (n_lw == 0 && tid == 0 && !(l == 0 && c == p.fault_cta)) grid_arrive(p.bar);  // no logits here
             // Q8_0 records of the normalised rows (the gate_up activations), every CTA its own copy,
             // made by the warps that have no logit to compute
-            for (int it = warp - n_lw; it < T * nb; it += kDecWarps - n_lw) {
-                const int t = it / nb, b = it - t * nb;
-                const float v = __fmul_rn(sm.hs[(size_t)t * H + b * 32 + lane], inv_s[t]);
-                quantize_record(v, sm.xrec + ((size_t)t * nb + b) * 64, sm.xsc + (size_t)t * pad4(nb) + b, lane);
-            }
+            quantize_records4(sm.hs, inv_s, T * nb, nb, H, sm.xrec, sm.xsc, pad4(nb), warp, lane, n_lw, kDecWarps - n_lw);
         }
         wphase ^= 1u;
         __syncthreads();
