@@ -645,9 +645,6 @@ DecodeParams decode_params(const umsx_moe *m, Workspace &ws, const void *x, int 
     p.y = ws.y;
     p.xr = ws.disp.xr;
     p.xr_sc = ws.disp.xr_sc;
-    p.act_rec = ws.act_rec;
-    p.act_sc = ws.act_sc;
-    p.act_done = ws.act_done;
     p.bar = ws.bar;
     p.err = ws.disp.err;
     p.fault_cta = -1;

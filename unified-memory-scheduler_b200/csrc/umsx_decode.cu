@@ -11,10 +11,10 @@
 //      (distinct experts, ascending) and the per-slot job lists.
 //   G  gate_up units = (slot, 16 rows of gate + the matching 16 rows of up), a
 //      contiguous share per CTA, five units at a time (4 warps each): exact
-//      MXFP4 x Q8_0 row dots, bias, SwiGLU-OAI / SiLU -> fp32 activations; the
-//      second of the two units of a 32-value block quantizes it to a Q8_0 record.
-//   D  down units = (slot, 16 rows of down), ten at a time (2 warps each), over
-//      the activation records -> per-job outputs y.
+//      MXFP4 x Q8_0 row dots, bias, SwiGLU-OAI / SiLU -> fp32 activations.
+//   D  every CTA quantizes the activation rows its down units read into Q8_0
+//      records in shared memory; down units = (slot, 16 rows of down), ten at a
+//      time (2 warps each), over those records -> per-job outputs y.
 // Every warp streams its weight rows through its own cp.async ring in shared
 // memory, several stages ahead, so that enough bytes are in flight per SM.
 // The arithmetic of every value is the per-stage path's (umsx_kernels.cu), so
@@ -123,14 +123,6 @@ __host__ __device__ inline size_t decode_smem_layout(int T, int H, int I, size_t
     return o;
 }
 
-// Q8_0 of 32 values held one per lane, written as an MXFP4 staging record.
-__device__ __forceinline__ void quantize_record(float v, uint8_t *rec, float *scale, int lane) {
-    const float amax = warp_max(fabsf(v));
-    const float qinv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-    write_mx_record(q8_code(v, qinv), rec, lane);
-    if (lane == 0) *scale = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f)));
-}
-
 // Q8_0 records of n_blk 32-value blocks of src (block i = row i / nb, block i % nb, rows of width
 // H, each scaled by inv[row] first), eight threads per block with four values each, so a
 // block's scale takes three shuffles: thread j of a block holds elements 4j..4j+3, i.e. one code
@@ -163,6 +155,47 @@ __device__ __forceinline__ void quantize_records4(const float *src, const float 
             *reinterpret_cast<uint2 *>(rec + (size_t)blk * 64 + (lh * 2 + (pp >> 1)) * 16 + (pp & 1) * 8) =
                 make_uint2(w, neg8x4(w));
             if (j == 0) scale[(size_t)t * scale_stride + b] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(am, 127.0f)));
+        }
+    }
+}
+
+// Q8_0 records (the codes and scales of quantize_records4) of nar activation rows of width I, row a
+// being row jobs[a] of act in global memory, by every thread of the CTA with four items each in
+// flight (an item: four values of a 32-value block).
+__device__ __forceinline__ void quantize_act_rows(const float *act, const int *jobs, int nar, int nbI, int I,
+                                                  uint8_t *rec, float *scale, int scale_stride, int warp, int lane) {
+    const int total = nar * nbI * 8;
+    for (int b0 = warp * 32; b0 < total; b0 += 4 * kDecThreads) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int it = b0 + k * kDecThreads + lane;
+            v[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (it < total) {
+                const int blk = it >> 3, a = blk / nbI, b = blk - a * nbI;
+                v[k] = __ldcg(reinterpret_cast<const float4 *>(act + (size_t)jobs[a] * I + b * 32 + 4 * (it & 7)));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int it = b0 + k * kDecThreads + lane;
+            const bool on = it < total;  // groups of 8 are all on or all off
+            float am = fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w)));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
+            if (on) {
+                const int blk = it >> 3, j = it & 7, a = blk / nbI, b = blk - a * nbI;
+                const float qinv = am != 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+                const uint32_t w = ((uint32_t)q8_code(v[k].x, qinv) & 0xffu) |
+                                   (((uint32_t)q8_code(v[k].y, qinv) & 0xffu) << 8) |
+                                   (((uint32_t)q8_code(v[k].z, qinv) & 0xffu) << 16) |
+                                   ((uint32_t)q8_code(v[k].w, qinv) << 24);
+                const int lh = j >> 2, pp = j & 3;
+                *reinterpret_cast<uint2 *>(rec + (size_t)blk * 64 + (lh * 2 + (pp >> 1)) * 16 + (pp & 1) * 8) =
+                    make_uint2(w, neg8x4(w));
+                if (j == 0) scale[(size_t)a * scale_stride + b] = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(am, 127.0f)));
+            }
         }
     }
 }
@@ -205,7 +238,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
     __shared__ float res_g[kGuGroups][MT][2][16];
     __shared__ float xch_d[kDnGroups][MT][16][4];
     __shared__ int ok_s, late_s;
-    __shared__ int last_g[kGuGroups][MT];
     __shared__ __align__(8) uint64_t wbar;
     __shared__ __align__(16) float wbias[kDecRouterRows][4];
 
@@ -419,23 +451,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                         const float a = p.activation == UMSX_ACT_SWIGLU_OAI ? swiglu_oai(gv, uv, p.alpha, p.limit) : silu_mul(gv, uv);
                         __stcg(p.act + (size_t)job_j[jf + c0 + t] * I + g * 16 + k, a);
                     }
-                    // The two units of a 32-value block: whichever finishes second quantizes
-                    // it into the down records.  Neither waits for the other.
-                    __threadfence();
-                    group_bar(1 + gi, 128);
-                    if (gt < m) {
-                        const unsigned prev = atomicAdd(p.act_done + (size_t)job_j[jf + c0 + gt] * nbI + (g >> 1), 1u);
-                        last_g[gi][gt] = prev == 1u;
-                    }
-                    group_bar(1 + gi, 128);
-                    for (int t = wg; t < m; t += 4) {
-                        if (!last_g[gi][t]) continue;
-                        __threadfence();
-                        const size_t job = (size_t)job_j[jf + c0 + t], blk = g >> 1;
-                        const float v = __ldcg(p.act + job * I + blk * 32 + lane);
-                        quantize_record(v, p.act_rec + (job * nbI + blk) * 64, p.act_sc + job * pad4(nbI) + blk, lane);
-                        if (lane == 0) p.act_done[job * nbI + blk] = 0;
-                    }
+                    // (the down phase quantizes the activations: each CTA the rows its units read)
                     group_bar(1 + gi, 128);
                 }
             }
@@ -466,16 +482,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             const int s_lo = v_lo / G2, s_hi = (v_hi - 1) / G2;
             jb = slot_first[s_lo];
             const int nar = slot_first[s_hi] + slot_cnt[s_hi] - jb;  // <= 2T: a CTA spans at most two slots
-            const int rq = nbI * 4, rs = pad4(nbI);
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.act_rec);
-            for (int i = tid; i < nar * rq; i += kDecThreads) {
-                const int a = i / rq;
-                reinterpret_cast<uint4 *>(sm.arec)[i] = __ldcg(src + (size_t)job_j[jb + a] * rq + (i - a * rq));
-            }
-            for (int i = tid; i < nar * rs; i += kDecThreads) {
-                const int a = i / rs;
-                sm.asc[i] = __ldcg(p.act_sc + (size_t)job_j[jb + a] * rs + (i - a * rs));
-            }
+            quantize_act_rows(p.act, job_j + jb, nar, nbI, I, sm.arec, sm.asc, pad4(nbI), warp, lane);
         }
         __syncthreads();
         {
@@ -552,7 +559,6 @@ int launch_decode_mt(const DecodeParams &p, cudaStream_t s) {
     // a CTA's down units then span at most two slots, whose jobs fit the 2T staged rows
     if (min(p.experts, p.tokens * p.top_k) > sms || p.experts > kDecRouterRows * sms) return -1;
     if (cudaMemsetAsync(p.bar, 0, sizeof(unsigned), s) != cudaSuccess) return -1;
-    if (cudaMemsetAsync(p.act_done, 0, (size_t)p.tokens * p.top_k * (p.inter / 32) * 4, s) != cudaSuccess) return -1;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(sms);
     cfg.blockDim = dim3(kDecThreads);

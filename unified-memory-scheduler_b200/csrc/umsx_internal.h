@@ -157,9 +157,6 @@ struct DecodeParams {
     float *y;          // [T*K][H] scratch
     uint8_t *xr;       // [T][H/32][64] Q8_0 records of the normalised rows
     float *xr_sc;      // [T][pad4(H/32)]
-    uint8_t *act_rec;  // [T*K][I/32][64] Q8_0 records of the activations
-    float *act_sc;     // [T*K][pad4(I/32)]
-    uint32_t *act_done;  // [T*K][I/32] arrival counters (zeroed by the launcher)
     unsigned *bar;     // grid barrier counter (zeroed by the launcher)
     uint32_t *err;     // status bits (kErr*): a grid barrier wait ran out, a non-finite output
     // fault injection for tests: CTA fault_cta withholds its first grid-barrier arrival (-1: none), so
