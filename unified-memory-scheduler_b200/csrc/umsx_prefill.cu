@@ -19,9 +19,13 @@
 // (expert, 128-row tile of the weights, 128-token tile of the expert's jobs)):
 //   warp 0    TMA producer of the activation tiles (128 tokens x 64 K, 128-byte swizzle)
 //   warp 1    MMA issuer (one thread) and owner of the tensor memory (two accumulators)
-//   warps 2-5 weight producers (MXFP4 -> f16 tiles), raw bytes prefetched by cp.async
+//   warps 2-5 weight producers (MXFP4 -> f16 tiles written straight into tensor memory
+//             with tcgen05.st, the MMA's A operand), raw bytes prefetched by cp.async
 //   warps 6-9 epilogue, draining one accumulator while the MMA fills the other
-// Rings of 4 weight tiles and 3 (hi + lo) activation tiles decouple them.
+// Rings of 4 weight tiles (tensor memory) and 4 (hi + lo) activation tiles (shared memory)
+// decouple them.  Each M128 x N128 x K16 MMA reading both operands from shared memory would
+// take the whole shared-memory bandwidth (8 KB per 64 cycles) with nothing left for the
+// activation and raw-weight traffic; with A in tensor memory it reads 4 KB.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -36,7 +40,7 @@
 namespace umsx {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64, kStagesA = 4, kStagesB = 3, kRaw = 6;
+constexpr int kBM = 128, kBN = 128, kBK = 64, kStagesA = 4, kStagesB = 4, kRaw = 6;
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB: one f16 operand tile
 constexpr int kGemmThreads = 320;
 constexpr long long kTcWaitCycles = 40000000;  // ~20 ms
@@ -57,9 +61,12 @@ struct RawRowQ8 {
 };
 constexpr int kRawQ8 = (int)(kRaw * sizeof(RawRow) / sizeof(RawRowQ8));
 static_assert(kRawQ8 >= 3, "Q8_0 raw ring depth");
-constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + kStagesA * kTileBytes /*weights*/ +
-                             kStagesB * 2 * kTileBytes /*activations hi, lo*/ + kRaw * kBM * sizeof(RawRow) +
-                             2 * 8 * 64 * sizeof(float) /*epilogue exchange*/;
+constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + kStagesB * 2 * kTileBytes /*activations hi, lo*/ +
+                             kRaw * kBM * sizeof(RawRow) + 2 * 8 * 64 * sizeof(float) /*epilogue exchange*/;
+// Tensor memory: two fp32 accumulators of kBN columns, then kStagesA weight tiles of kBK / 2
+// columns (128 rows = lanes, f16 pairs along K).
+constexpr uint32_t kTmemCols = 512, kTmemA = 2 * kBN, kColsA = kBK / 2;
+static_assert(kTmemA + kStagesA * kColsA <= kTmemCols, "tensor memory budget");
 
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, uint32_t *err) {
     if (mbar_wait_bounded(bar, parity, kTcWaitCycles)) return true;
@@ -87,8 +94,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                                                               const MoeGemmParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sA = smem;                                 // [kStagesA] weight tiles
-    uint8_t *sB = sA + kStagesA * kTileBytes;           // [kStagesB][hi, lo] activation tiles
+    uint8_t *sB = smem;                                 // [kStagesB][hi, lo] activation tiles
     RawRow *sRaw = reinterpret_cast<RawRow *>(sB + kStagesB * 2 * kTileBytes);  // [kRaw][row]
     float *xch = reinterpret_cast<float *>(sRaw + kRaw * kBM);                  // [2][8 cols][64 rows]
     __shared__ __align__(8) uint64_t full_a[kStagesA], empty_a[kStagesA], full_b[kStagesB], empty_b[kStagesB];
@@ -113,7 +119,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
         }
     }
     if (warp == 1) {
-        tc::tmem_alloc(&tmem_base_s, 2 * kBN);  // two accumulators: the epilogue drains one while the MMA fills the other
+        // two accumulators (the epilogue drains one while the MMA fills the other) and the weight tiles
+        tc::tmem_alloc(&tmem_base_s, kTmemCols);
         tc::tmem_relinquish();
     }
     if (warp == 0) {
@@ -174,14 +181,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                     wait_bar(&full_a[sa], (g / kStagesA) & 1u, p.err);
                     wait_bar(&full_b[sb], (g / kStagesB) & 1u, p.err);
                     tc::fence_after_sync();
-                    const uint64_t da = tc::smem_desc_sw128(sA + sa * kTileBytes);
+                    const uint32_t a_tm = tmem + kTmemA + sa * kColsA;
                     const uint64_t dh = tc::smem_desc_sw128(sB + sb * 2 * kTileBytes);
                     const uint64_t dl = tc::smem_desc_sw128(sB + sb * 2 * kTileBytes + kTileBytes);
 #pragma unroll
                     for (int k16 = 0; k16 < kBK / 16; ++k16) {  // 32 bytes of K per step, inside the swizzle atom
                         // activation = hi + lo exactly, so the sum of both products is the product with it
-                        tc::mma_f16(d_tm, da + 2 * k16, dh + 2 * k16, idesc, (kk | k16) != 0);
-                        tc::mma_f16(d_tm, da + 2 * k16, dl + 2 * k16, idesc, 1u);
+                        tc::mma_f16_ta(d_tm, a_tm + 8 * k16, dh + 2 * k16, idesc, (kk | k16) != 0);
+                        tc::mma_f16_ta(d_tm, a_tm + 8 * k16, dl + 2 * k16, idesc, 1u);
                     }
                     tc::mma_commit(&empty_a[sa]);
                     tc::mma_commit(&empty_b[sb]);
@@ -219,7 +226,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             const int rg = valid ? prow >> 5 : 0, r32 = prow & 31;
             const uint8_t *codes = cb + ((size_t)e * nrg + rg) * (size_t)nbK * 1024 + r32 * 32;
             const uint8_t *scl = sb + ((size_t)e * nrg + rg) * (size_t)(nbK / 2) * 128 + r32 * 4;
-            uint8_t *rowA = sA + r * 128;
+            const uint32_t lane_a = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kTmemA;
             auto fetch = [&](int kk) {
                 if (kk < nk && valid) {
                     RawRowQ8 *d = sRq + (kk % kRawQ8) * kBM + r;
@@ -247,7 +254,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                     sv = sr->s;
                 }
                 wait_bar(&empty_a[s], ((g / kStagesA) & 1u) ^ 1u, p.err);
-                uint8_t *dst = rowA + s * kTileBytes;
+                tc::fence_after_sync();  // the MMAs that read this stage's columns are complete
+                uint32_t col[32];
                 const __half2 k1152 = __float2half2_rn(1152.0f);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
@@ -268,12 +276,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                             const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&bits), k1152), d2);
                             o[q] = *reinterpret_cast<const uint32_t *>(&v);
                         }
-                        const int ch = 4 * h + cc;
-                        *reinterpret_cast<uint4 *>(dst + ((ch ^ (r & 7)) << 4)) =
-                            valid ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0u, 0u, 0u, 0u);
+                        // elements 32h + 8cc .. + 7 of the stage: columns 16h + 4cc .. + 3
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) col[16 * h + 4 * cc + q] = valid ? o[q] : 0u;
                     }
                 }
-                tc::fence_proxy_async();
+                tc::tmem_st32(lane_a + s * kColsA, col);
+                tc::tmem_wait_st();
+                tc::fence_before_sync();
                 tc::mbar_arrive(&full_a[s]);
             }
         }
@@ -301,7 +311,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             const bool valid = mrow < p.rows;
             const int grp = valid ? prow >> 4 : 0, rr = prow & 15;
             const int emax = valid ? __ldg(eb + (size_t)e * p.plane_rows + prow) : 0;
-            uint8_t *rowA = sA + r * 128;
+            const uint32_t lane_a = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kTmemA;
             // The warp's 32 rows are two 16-row groups of the plane; per K stage (block pair) a row group's
             // codes are one 512-byte chunk and its exponent quad one 128-byte chunk.  The warp copies them
             // 16 bytes a lane (cp.async, L2 only) kRaw - 1 stages ahead into its own raw area; each thread
@@ -352,7 +362,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                     ew = ((e0 >> (8 * (kk & 3))) & 0xffu) | (((e1 >> (8 * (kk & 3))) & 0xffu) << 8);
                 }
                 wait_bar(&empty_a[s], ((g / kStagesA) & 1u) ^ 1u, p.err);
-                uint8_t *dst = rowA + s * kTileBytes;
+                tc::fence_after_sync();  // the MMAs that read this stage's columns are complete
+                uint32_t col[32];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     // block 2*kk + h: elements 32h..32h+31 of the stage; f16 scale 2^(e - emax + 13)
@@ -372,13 +383,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                                 const __half2 v = __hmul2(*reinterpret_cast<const __half2 *>(&f), sc2);
                                 o[q * 4 + b] = *reinterpret_cast<const uint32_t *>(&v);
                             }
-                        // 16 elements = chunks c and c+1 of the 128-byte row, c = 4h + 2lh
-                        const int c = 4 * h + 2 * lh;
-                        *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-                        *reinterpret_cast<uint4 *>(dst + (((c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+                        // elements 32h + 16lh .. + 15 of the stage: columns 16h + 8lh .. + 7
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) col[16 * h + 8 * lh + i] = o[i];
                     }
                 }
-                tc::fence_proxy_async();
+                tc::tmem_st32(lane_a + s * kColsA, col);
+                tc::tmem_wait_st();
+                tc::fence_before_sync();
                 tc::mbar_arrive(&full_a[s]);
             }
         }
@@ -464,7 +476,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
     __syncthreads();
     if (warp == 1) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, 2 * kBN);
+        tc::tmem_dealloc(tmem, kTmemCols);
     }
 }
 
