@@ -441,7 +441,19 @@ def ep_decode_arm(a):
     expert_b = cfg.expert_bytes()
     step_bytes = a.layers * (distinct * expert_b + world * cfg.router_bytes())  # all ranks together
     per_gpu = step_bytes / world / (ms_step / 1e3) / 1e9
-    xbytes = a.layers * (world * (world - 1) * H * 4 + world * k * H * 4 * (world - 1) / world)
+    one_launch = launches == a.steps  # the one-launch expert-parallel decode kernel served every step
+    if one_launch:  # token rows once per step, every job's output row to every other rank per layer
+        xbytes = world * (world - 1) * H * 4 + a.layers * world * k * H * 4 * (world - 1)
+        exch = ("P2P NVLink stores inside the one-launch decode kernel k_decode (CUDA IPC mappings): token rows once "
+                "per step, each job's output row into every rank, a release/acquire flag exchange per layer; no "
+                "collective in the data path")
+        kern = ("k_decode, expert-parallel form (one launch per step per GPU: replicated router over all ranks' "
+                "tokens, this rank's experts, cross-rank flag exchange per layer)")
+    else:
+        xbytes = a.layers * (world * (world - 1) * H * 4 + world * k * H * 4 * (world - 1) / world)
+        exch = ("P2P NVLink stores inside k_ep_share / k_ep_combine (CUDA IPC mappings), release/acquire flags; "
+                "no collective in the data path")
+        kern = "whole decode step per GPU (per-stage exact kernels + exchange kernels)"
     res = {"metric": metric_name(a), "value": world * a.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "int8 dot (MXFP4 x Q8_0), fp32 accumulate", "data": "synthetic",
@@ -450,11 +462,10 @@ def ep_decode_arm(a):
                       "experts": cfg.experts, "experts_per_gpu": cfg.experts // world, "top_k": k, "hidden": H,
                       "ffn": cfg.intermediate, "quant": "mxfp4", "tokens_per_step_per_gpu": 1, "global_batch": world,
                       "parallelism": f"ep{world}",
-                      "exchange": "P2P NVLink stores inside k_ep_share / k_ep_combine (CUDA IPC mappings), "
-                                  "release/acquire flags; no collective in the data path",
+                      "exchange": exch,
                       "l2": "inputs larger than L2", "expected_distinct_experts_per_layer": distinct,
                       "parity": "every rank's token through a 2-layer slice, bit-exact with one GPU running whole layers"},
-           "roofline": {"kernel": "whole decode step per GPU (per-stage exact kernels + exchange kernels)",
+           "roofline": {"kernel": kern,
                         "bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                         "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_step_all_gpus": step_bytes,
                         "traffic": None},

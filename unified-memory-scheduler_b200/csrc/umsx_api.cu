@@ -1543,8 +1543,9 @@ umsx_status umsx_moe_create_gguf(const umsx_moe_desc *desc, const char *first_sh
 
 struct umsx_ep {
     int rank = 0, world = 1, device = 0, hidden = 0, top_k = 0;
-    uint8_t *buf = nullptr;  // h_all [world][H] f32 | y_recv [K][H] f32 | flags [world] u32 | epoch u32
-    size_t bytes = 0, off_y = 0, off_flags = 0, off_epoch = 0;
+    // h_all [world][H] f32 | y_recv [K][H] f32 | flags [world] u32 | epoch u32 | y_all [world*K][H] f32
+    uint8_t *buf = nullptr;
+    size_t bytes = 0, off_y = 0, off_flags = 0, off_epoch = 0, off_yall = 0;
     cudaIpcMemHandle_t handle{};
     std::vector<uint8_t *> peers;  // each rank's buffer as mapped here (own entry = buf)
     bool connected = false;
@@ -1562,10 +1563,60 @@ struct umsx_ep_stack {
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
     struct Graph { int dtype; cudaGraphExec_t exec; uint64_t kernels; };
     std::vector<Graph> graphs;
+    bool persistent = false;  // the one-launch expert-parallel decode kernel serves every step
     std::mutex mu;
 };
 
 namespace {
+
+// The persistent decode kernel in its expert-parallel form serves a stack when every layer is a
+// resident MXFP4 fused-gate_up layer and the step's G tokens (one per rank) fit the kernel.
+bool ep_persistent_eligible(const umsx_ep_stack *st) {
+    const int G = st->ep->world, L = (int)st->layers.size();
+    if (G < 2 || G > kDecodeMaxTokens) return false;
+    for (const umsx_moe *m : st->layers) {
+        const auto &d = m->d;
+        if (m->banked || d.quant != UMSX_QUANT_MXFP4 || !d.fused_gate_up || m->e_local * G != d.experts ||
+            m->e_lo != st->ep->rank * m->e_local || !decode_supported(G, d.hidden, d.intermediate, d.experts, d.top_k, L))
+            return false;
+    }
+    return true;
+}
+
+// One step as a single launch: this rank's token goes to every rank, every rank routes all G tokens
+// and runs its own experts' units, each job row goes to every rank, and every layer ends with a
+// cross-rank flag exchange inside the kernel (k_decode, DecodeParams::ep_world).  Row `rank` of the
+// kernel's [G][H] output is this rank's token.  Returns 1 launched, 0 not resident on this device.
+int record_ep_persistent(umsx_ep_stack *st, int dtype, cudaStream_t s) {
+    const umsx_ep *ep = st->ep;
+    const int G = ep->world, H = ep->hidden, L = (int)st->layers.size();
+    const umsx_moe *m0 = st->layers[0];
+    DecodeParams p = decode_params(m0, st->ws, st->x_dev, dtype, G, st->ws.out_dev);
+    p.n_layers = L;
+    for (int l = 0; l < L; ++l) set_decode_layer(p, l, st->layers[l]);
+    p.rmsnorm = 1;
+    p.residual = 1;
+    p.eps = st->eps;
+    p.ep_world = G;
+    p.ep_rank = ep->rank;
+    p.e_lo = m0->e_lo;
+    p.e_local = m0->e_local;
+    p.y = reinterpret_cast<float *>(ep->buf + ep->off_yall);
+    for (int q = 0; q < G; ++q) {
+        p.peer_y[q] = reinterpret_cast<float *>(ep->peers[q] + ep->off_yall);
+        p.peer_x[q] = reinterpret_cast<float *>(ep->peers[q]);
+        p.peer_flags[q] = reinterpret_cast<unsigned *>(ep->peers[q] + ep->off_flags);
+    }
+    p.x_all = reinterpret_cast<const float *>(ep->buf);
+    p.flags = reinterpret_cast<unsigned *>(ep->buf + ep->off_flags);
+    p.epoch = reinterpret_cast<unsigned *>(ep->buf + ep->off_epoch);
+    p.ep_wait_cycles = ep->wait_cycles;
+    if (try_decode(p, s) <= 0) return 0;
+    if (cudaMemcpyAsync(st->out_dev, st->ws.out_dev + (size_t)ep->rank * H, (size_t)H * 4, cudaMemcpyDeviceToDevice, s) !=
+        cudaSuccess)
+        return -1;
+    return 1;
+}
 
 EpParams ep_params(umsx_ep_stack *st, const umsx_moe *m) {
     const umsx_ep *ep = st->ep;
@@ -1595,6 +1646,11 @@ EpParams ep_params(umsx_ep_stack *st, const umsx_moe *m) {
 
 umsx_status record_ep_step(umsx_ep_stack *st, int dtype, cudaStream_t s) {
     const int H = st->ep->hidden, G = st->ep->world;
+    if (st->persistent) {
+        const int r = record_ep_persistent(st, dtype, s);
+        if (r < 0) return fail(UMSX_EDEVICE, "expert-parallel decode: copying the output row failed");
+        if (r > 0) return UMSX_OK;
+    }
     if (dtype == UMSX_DTYPE_BF16)
         UMSX_LAUNCHED(launch_bf16_to_f32(static_cast<const uint16_t *>(st->x_dev), st->h_own, (size_t)H, s));
     else
@@ -1633,7 +1689,8 @@ umsx_status umsx_ep_create(int rank, int world, int device, int hidden, int top_
     ep->off_y = align_up((size_t)world * hidden * 4);
     ep->off_flags = align_up(ep->off_y + (size_t)top_k * hidden * 4);
     ep->off_epoch = ep->off_flags + (size_t)world * 4;
-    ep->bytes = align_up(ep->off_epoch + 4);
+    ep->off_yall = align_up(ep->off_epoch + 4);
+    ep->bytes = align_up(ep->off_yall + (size_t)world * top_k * hidden * 4);
     auto run = [&]() -> umsx_status {
         UMSX_CUDA(cudaMalloc(&ep->buf, ep->bytes));
         UMSX_CUDA(cudaMemset(ep->buf, 0, ep->bytes));
@@ -1722,6 +1779,7 @@ umsx_status umsx_ep_stack_create(umsx_ep *ep, umsx_moe *const *layers, int n_lay
         return UMSX_OK;
     };
     if (umsx_status r = run()) { umsx_ep_stack_destroy(st); return r; }
+    st->persistent = ep_persistent_eligible(st);
     *out = st;
     return UMSX_OK;
 }

@@ -93,6 +93,47 @@ __device__ bool grid_sync(const DecodeParams &p, unsigned target, int *ok_s) {
     return grid_wait(p, target, ok_s);
 }
 
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Cross-rank end of a phase (expert parallelism): every thread's earlier stores, this GPU's and the
+// peers', are fenced system-wide; the CTAs of this rank meet at the grid barrier; CTA 0 then publishes
+// exchange number e into this rank's slot of every rank's flag array (release), and every CTA waits,
+// bounded, until every rank has published e here (acquire).  A rank that never arrives costs one wait
+// bound and sets bit 2 of err.  Returns the CTA-uniform outcome.
+__device__ bool ep_sync(const DecodeParams &p, unsigned &target, unsigned e, int *ok_s) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) grid_arrive(p.bar);
+    target += gridDim.x;
+    if (!grid_wait(p, target, ok_s)) return false;
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0)
+            for (int q = 0; q < p.ep_world; ++q) st_release_sys(p.peer_flags[q] + p.ep_rank, e);
+        int ok = 1;
+        const long long t0 = clock64();
+        for (int src = 0; src < p.ep_world && ok; ++src) {
+            for (unsigned it = 0; ld_acquire_sys(p.flags + src) < e; ++it) {
+                if ((it & 63u) != 63u) continue;
+                if ((*reinterpret_cast<volatile uint32_t *>(p.err) & ~kErrNonFinite) || clock64() - t0 > p.ep_wait_cycles) {
+                    atomicOr(p.err, 2u);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        *ok_s = ok;
+    }
+    __syncthreads();
+    return *ok_s != 0;
+}
+
 struct DecSmem {
     float *wrow;    // [kDecRouterRows][H] router rows of this CTA's experts (bulk-copied a layer ahead)
     float *hs;      // [T][H] residual stream (this CTA's copy)
@@ -110,7 +151,8 @@ constexpr int kDecRouterRows = 2;  // experts <= 2 * #CTAs
 // shared memory did); more tokens need the staging room.
 __host__ __device__ constexpr int ring_stages(int T) { return T == 1 ? 3 : 2; }
 
-__host__ __device__ inline size_t decode_smem_layout(int T, int H, int I, size_t off[7]) {
+// stages: the ring depth of the kernel instantiation (ring_stages(MT)).
+__host__ __device__ inline size_t decode_smem_layout(int T, int H, int I, int stages, size_t off[7]) {
     const size_t nb = H / 32, nbI = I / 32;
     size_t o = 0;
     off[0] = o; o += (size_t)kDecRouterRows * H * 4;
@@ -119,7 +161,7 @@ __host__ __device__ inline size_t decode_smem_layout(int T, int H, int I, size_t
     off[3] = o; o += (size_t)T * pad4((int)nb) * 4;
     off[4] = o; o += (size_t)2 * T * nbI * 64;
     off[5] = o; o += (size_t)2 * T * pad4((int)nbI) * 4;
-    off[6] = o; o += (size_t)kDecWarps * ring_stages(T) * kRingStageBytes;
+    off[6] = o; o += (size_t)kDecWarps * stages * kRingStageBytes;
     return o;
 }
 
@@ -225,7 +267,9 @@ __device__ __forceinline__ float4 fold4(const float4 *y4, const float *w, int t,
     return make_float4(__fadd_rn(h.x, acc.x), __fadd_rn(h.y, acc.y), __fadd_rn(h.z, acc.z), __fadd_rn(h.w, acc.w));
 }
 
-template <int MT>
+// EP: the expert-parallel form (DecodeParams::ep_world > 1), a separate instantiation so that the
+// single-GPU kernels carry none of its code.
+template <int MT, bool EP>
 __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float inv_s[kDecodeMaxTokens];
@@ -250,7 +294,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
     const int n_lw = my_e * T;                          // warps computing logits; the others quantize h
     constexpr int S = ring_stages(MT);
     size_t off[7];
-    decode_smem_layout(T, H, I, off);
+    decode_smem_layout(T, H, I, S, off);
     DecSmem sm{reinterpret_cast<float *>(smem + off[0]), reinterpret_cast<float *>(smem + off[1]), smem + off[2],
                reinterpret_cast<float *>(smem + off[3]), smem + off[4], reinterpret_cast<float *>(smem + off[5]),
                smem + off[6]};
@@ -263,8 +307,28 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
         late_s = 0;
         if (my_e > 0) load_router_rows(p.layer[0].router_w, p.layer[0].router_b, c, nC, my_e, H, sm.wrow, wbias, &wbar);
     }
-    // h <- x
-    if (p.x_dtype == UMSX_DTYPE_BF16) {
+    constexpr bool ep = EP;
+    __shared__ unsigned ep_base_s;
+    if (ep) {
+        // this rank's token into row ep_rank of every rank's x_all (a slice per CTA), the first exchange,
+        // then h <- x_all: every rank holds all ranks' tokens
+        if (tid == 0) ep_base_s = *reinterpret_cast<volatile unsigned *>(p.epoch);
+        const int lo4 = (int)((long long)c * H4 / nC), hi4 = (int)((long long)(c + 1) * H4 / nC);
+        for (int i = lo4 + tid; i < hi4; i += kDecThreads) {
+            float4 v;
+            if (p.x_dtype == UMSX_DTYPE_BF16) {
+                const uint2 b = reinterpret_cast<const uint2 *>(p.x)[i];
+                v = make_float4(bf16_bits_to_f32(b.x & 0xffffu), bf16_bits_to_f32(b.x >> 16), bf16_bits_to_f32(b.y & 0xffffu),
+                                bf16_bits_to_f32(b.y >> 16));
+            } else {
+                v = reinterpret_cast<const float4 *>(p.x)[i];
+            }
+            for (int q = 0; q < p.ep_world; ++q) reinterpret_cast<float4 *>(p.peer_x[q])[(size_t)p.ep_rank * H4 + i] = v;
+        }
+        if (!ep_sync(p, target, ep_base_s + 1u, &ok_s)) return;
+        for (int i = tid; i < T * H4; i += kDecThreads)
+            reinterpret_cast<float4 *>(sm.hs)[i] = __ldcg(reinterpret_cast<const float4 *>(p.x_all) + i);
+    } else if (p.x_dtype == UMSX_DTYPE_BF16) {
         const uint16_t *xb = static_cast<const uint16_t *>(p.x);
         for (int i = tid; i < T * H; i += kDecThreads) sm.hs[i] = bf16_bits_to_f32(xb[i]);
     } else {
@@ -359,7 +423,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             if (lane < K) { sel_e[warp * K + lane] = sel; sel_w[warp * K + lane] = w; }
         }
         __syncthreads();
-        if (MT == 1 && warp == 0) {
+        if (MT == 1 && T == 1 && warp == 0) {
             // one token: its k picks are distinct experts, so slot r is rank r with the one job r
             const bool has = lane < K;
             int ej = has ? sel_e[lane] : 0;
@@ -374,11 +438,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                 p.w_out[lane] = sel_w[lane];
             }
         } else if (warp == 0) {
-            const bool has = lane < N;
+            bool has = lane < N;
             int ej = has ? sel_e[lane] : 0x7fffffff;
             if (has && (ej < 0 || ej >= E)) {  // cannot happen (selection always picks a valid expert); never index with it
                 atomicOr(p.err, 8u);
                 ej = 0;
+            }
+            if (c == 0 && l == p.n_layers - 1 && p.ids_out && has) {
+                p.ids_out[lane] = ej;
+                p.w_out[lane] = sel_w[lane];
+            }
+            if (ep && has) {  // this rank runs the jobs of its own experts only, indexed locally
+                if (ej >= p.e_lo && ej < p.e_lo + p.e_local) {
+                    ej -= p.e_lo;
+                } else {
+                    has = false;
+                    ej = 0x7fffffff;
+                }
             }
             int same_before = 0, cnt = 0, less = 0;
             for (int j = 0; j < N; ++j) {
@@ -397,10 +473,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             if (first) { slot_e[slot] = ej; slot_cnt[slot] = cnt; slot_first[slot] = less; }
             if (has) job_j[less + same_before] = lane;
             if (lane == 0) n_slots_s = __popc(firsts);
-            if (c == 0 && l == p.n_layers - 1 && p.ids_out && has) {
-                p.ids_out[lane] = ej;
-                p.w_out[lane] = sel_w[lane];
-            }
         }
         __syncthreads();
         const int n_slots = n_slots_s;
@@ -521,15 +593,25 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                             if (t < m) {
                                 float y = mx_row_total(acc[t], xch_d[di][t][r]);
                                 if (Ld.dn_bias) y = __fadd_rn(y, bias);
-                                __stcg(p.y + (size_t)job_j[jf + c0 + t] * H + g * 16 + r, y);
+                                const size_t o = (size_t)job_j[jf + c0 + t] * H + g * 16 + r;
+                                if (ep) {  // every rank folds every token: the row goes to all of them
+                                    for (int q = 0; q < p.ep_world; ++q) __stcg(p.peer_y[q] + o, y);
+                                } else {
+                                    __stcg(p.y + o, y);
+                                }
                             }
                     group_bar(1 + di, 64);
                 }
             }
         }
-        target += nC;
-        if (!grid_sync(p, target, &ok_s)) return;
+        if (ep) {
+            if (!ep_sync(p, target, ep_base_s + 2u + (unsigned)l, &ok_s)) return;
+        } else {
+            target += nC;
+            if (!grid_sync(p, target, &ok_s)) return;
+        }
     }
+    if (ep && c == 0 && tid == 0) *p.epoch = ep_base_s + 1u + (unsigned)p.n_layers;  // every CTA read the base
     // final fold: each CTA writes its share of the output rows, and records a non-finite value (checking
     // the last layer suffices: an inf or NaN in h turns the next layer's RMSNorm, and so its output, NaN)
     const int total4 = T * H4;
@@ -543,11 +625,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
     }
 }
 
-template <int MT>
+template <int MT, bool EP>
 int launch_decode_mt(const DecodeParams &p, cudaStream_t s) {
     size_t off[7];
-    const size_t dyn = decode_smem_layout(p.tokens, p.hidden, p.inter, off);
-    auto kern = k_decode<MT>;
+    const size_t dyn = decode_smem_layout(p.tokens, p.hidden, p.inter, ring_stages(MT), off);
+    auto kern = k_decode<MT, EP>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) return -1;
     // shared memory as small as the kernel needs: the rest of the 256 KB stays L1
     if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxL1) != cudaSuccess) return -1;
@@ -581,7 +663,10 @@ bool decode_supported(int tokens, int hidden, int inter, int experts, int top_k,
 }
 
 int launch_decode(const DecodeParams &p, cudaStream_t s) {
-    return p.tokens == 1 ? launch_decode_mt<1>(p, s) : launch_decode_mt<kDecodeMaxTokens>(p, s);
+    // Expert parallelism: each rank's share of the G tokens' jobs mostly has one job per expert slot, so
+    // the one-job-per-pass kernel (deeper rings; a slot with more jobs streams its rows once per job) serves it.
+    if (p.ep_world > 1) return launch_decode_mt<1, true>(p, s);
+    return p.tokens == 1 ? launch_decode_mt<1, false>(p, s) : launch_decode_mt<kDecodeMaxTokens, false>(p, s);
 }
 
 }  // namespace umsx

@@ -124,6 +124,7 @@ struct GemvParams {
 // Persistent decode kernel (umsx_decode.cu): every layer of a stack, or one layer,
 // for at most kDecodeMaxTokens tokens in one cooperative launch.  MXFP4 weights with
 // fused gate_up only; all experts local.
+constexpr int kEpMaxRanks = 8;
 constexpr int kDecodeMaxLayers = 48;
 constexpr int kDecodeMaxTokens = 4;
 constexpr int kDecodeMaxTopK = 8;
@@ -163,6 +164,18 @@ struct DecodeParams {
     // every wait of that barrier runs out after wait_cycles (0: the default bound) and reports it
     int fault_cta;
     long long wait_cycles;
+    // Expert parallelism over NVLink (ep_world > 1; 1 = all experts local): tokens = ep_world, token g
+    // being rank g's (p.x holds this rank's one row); this rank holds experts [e_lo, e_lo + e_local) of
+    // every layer and routes all tokens; each local job's output row is stored into every rank's y;
+    // the token rows are exchanged first and every layer ends with a cross-rank flag exchange.
+    int ep_world, ep_rank, e_lo, e_local;
+    float *peer_y[kEpMaxRanks];         // each rank's y [T*K][H] (this rank's entry = y)
+    float *peer_x[kEpMaxRanks];         // each rank's x_all [world][H]
+    const float *x_all;                 // this rank's x_all
+    unsigned *peer_flags[kEpMaxRanks];  // each rank's flag array [world] (slot = source rank)
+    unsigned *flags;                    // this rank's flag array
+    unsigned *epoch;                    // this rank's exchange counter (monotonic, never zeroed)
+    long long ep_wait_cycles;           // bound of every cross-rank wait
 };
 
 bool decode_supported(int tokens, int hidden, int inter, int experts, int top_k, int n_layers);
@@ -208,7 +221,6 @@ int launch_moe_gemm(const MoeGemmParams &p, const void *act_hi, const void *act_
 
 // Expert-parallel exchange of a decode step (umsx_ep.cu): one token per rank, peers reached through
 // CUDA IPC mappings of their exchange buffers.
-constexpr int kEpMaxRanks = 8;
 
 struct EpParams {
     int rank, world, hidden, top_k, e_lo, e_local;
