@@ -436,17 +436,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                     for (int i = 0; i < 8; ++i) xo[i * 64 + ar] = v[up ? i : 8 + i];
                     asm volatile("bar.sync 1, 128;" ::: "memory");
                     const float *xi = xch + (up ? 8 * 64 : 0);
+                    float a[8], am[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float gv = up ? xi[i * 64 + ar] : v[i];
+                        const float uv = up ? v[8 + i] : xi[i * 64 + ar];
+                        a[i] = p.activation == UMSX_ACT_SWIGLU_OAI ? swiglu_oai(gv, uv, p.alpha, p.limit) : silu_mul(gv, uv);
+                        am[i] = warp_max(fabsf(a[i]));
+                    }
+                    // the block's two divisions for column i are the same on every lane: lane i computes
+                    // them once for the warp and hands them out
+                    float ami = am[0];
+#pragma unroll
+                    for (int i = 1; i < 8; ++i)
+                        if (lane == i) ami = am[i];
+                    const float my_qinv = ami != 0.0f ? __fdiv_rn(127.0f, ami) : 0.0f;
+                    const float my_d = f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(ami, 127.0f)));
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const int col = c0 + (up ? 8 : 0) + i;
-                        const float gv = up ? xi[i * 64 + ar] : v[i];
-                        const float uv = up ? v[8 + i] : xi[i * 64 + ar];
-                        const float a = p.activation == UMSX_ACT_SWIGLU_OAI ? swiglu_oai(gv, uv, p.alpha, p.limit)
-                                                                            : silu_mul(gv, uv);
-                        const float amax = warp_max(fabsf(a));
-                        const float qinv = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-                        const float qd = __fmul_rn((float)q8_code(a, qinv),
-                                                   f16_bits_to_f32(f32_to_f16_bits(__fdiv_rn(amax, 127.0f))));
+                        const float qinv = __shfl_sync(kFull, my_qinv, i), dq = __shfl_sync(kFull, my_d, i);
+                        const float qd = __fmul_rn((float)q8_code(a[i], qinv), dq);
                         const int n = nt * kBN + col;
                         if (n < cnt) {  // q * d exactly, as f16 hi + lo
                             const __half hi = __float2half_rn(qd);
