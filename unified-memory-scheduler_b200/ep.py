@@ -136,7 +136,10 @@ class EpGroup:
 
 class EpStack:
     """A decode stack split over the group by expert: h <- h + MoE_l(RMSNorm(h)) for one token per
-    rank (token g on rank g), each layer a handle created with ep_rank / ep_world of the group."""
+    rank (token g on rank g), each layer a handle created with ep_rank / ep_world of the group.
+    With up to four ranks and MXFP4 layers with fused gate_up a step is one kernel launch per rank
+    (the exchanges happen inside it); otherwise the per-stage kernels run between two exchange
+    kernels per layer.  Every rank must step in turn."""
 
     def __init__(self, group: EpGroup, layers: list, rms_eps: float = 1e-5):
         import ctypes as C
