@@ -283,8 +283,11 @@ umsx_status umsx_route_static(const void *x, int x_dtype, int tokens, const floa
  * per layer, each rank stores its hidden row into every peer's buffer, all ranks route all the
  * group's tokens (the router is replicated), each runs the jobs of its own experts, stores each
  * job's output row into the buffer of the rank that owns the token, and that rank combines its
- * token in rank order with the residual.  Stores are plain P2P stores from inside the exchange
- * kernels, flags st.release.sys, waits ld.acquire.sys bounded by umsx_ep_set_wait (default about
+ * token in rank order with the residual.  With up to four ranks and MXFP4 layers with fused gate_up
+ * the whole step is one kernel launch per rank: each rank's token goes to every rank once, every
+ * rank folds every token, and each job's output row goes to every rank, with one flag exchange per
+ * layer inside the kernel.  Stores are plain P2P stores from inside the kernels, flags
+ * st.release.sys, waits ld.acquire.sys bounded by umsx_ep_set_wait (default about
  * one second): a rank that never arrives gives the others UMSX_ETIMEOUT from _host calls or
  * umsx_ep_stack_status, not a hang.  Each token's result has the single-GPU stack's bits.  All ranks
  * must call forward the same number of times, in step. */
