@@ -353,6 +353,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
             if (p.rmsnorm) {
                 const float *ht = sm.hs + (size_t)warp * H;
                 float a = 0.0f;
+#pragma unroll 2  // the next chunk's shared-memory loads in flight during this chunk's chain
                 for (int k0 = lane; k0 < H; k0 += 32 * 8) {
                     float v[8];
 #pragma unroll
@@ -376,6 +377,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode(const __grid_constant
                 const float *ht = sm.hs + (size_t)t * H;
                 const float inv = inv_s[t];
                 float acc = 0.0f;
+#pragma unroll 2  // the next chunk's shared-memory loads in flight during this chunk's chain
                 for (int k0 = lane; k0 < H; k0 += 32 * 8) {
                     float w[8], x[8];
 #pragma unroll
